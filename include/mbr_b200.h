@@ -1,0 +1,152 @@
+/*
+ * mbr_b200.h — C ABI of the B200-native MelBandRoformer separator.
+ *
+ * The reference (baicai-1145/MBR-CUDA-Tile) exposes its hot path only as C++
+ * (cudasep::app::load_model / run_inference, MelBandRoformer::load / forward,
+ * the mbr_tile / stft_tile / chunk_tile op namespaces).  This header is the
+ * drop-in boundary a maintainer binds from any FFI: plain pointers, sizes and
+ * status codes, no C++ or CUDA types.  Each entry point names the reference
+ * interface (file:line) it replaces.
+ *
+ * Conventions
+ *  - Every function returns MBR_OK (0) or an MBR_ERR_* code; the message of
+ *    the last failure on the calling thread is mbr_last_error().
+ *  - "d_" pointers are device memory on the handle's device, "h_" pointers are
+ *    host memory.  All buffers are caller owned; the library owns only its
+ *    weights and workspaces (one set per handle).
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *    device entry points enqueue work and return without synchronising.
+ *  - One handle per host thread at a time; handles on different devices run
+ *    concurrently.
+ */
+#ifndef MBR_B200_H
+#define MBR_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MBR_API __attribute__((visibility("default")))
+
+/* status codes */
+#define MBR_OK 0
+#define MBR_ERR_INVALID 1     /* bad argument / shape */
+#define MBR_ERR_CUDA 2        /* CUDA runtime failure */
+#define MBR_ERR_IO 3          /* file missing or malformed (.csm) */
+#define MBR_ERR_UNSUPPORTED 4 /* configuration the kernels do not cover */
+#define MBR_ERR_OOM 5         /* device allocation failed */
+#define MBR_ERR_TIMEOUT 6     /* a bounded wait gave up */
+
+/* compute dtypes (the .csm dtype codes) */
+#define MBR_FP32 0
+#define MBR_FP16 1
+#define MBR_BF16 3
+
+/* mbr_get_info keys */
+#define MBR_INFO_DIM 0
+#define MBR_INFO_DEPTH 1
+#define MBR_INFO_NUM_STEMS 2
+#define MBR_INFO_CHANNELS 3
+#define MBR_INFO_NUM_BANDS 4
+#define MBR_INFO_SAMPLE_RATE 5
+#define MBR_INFO_CHUNK_SIZE 6
+#define MBR_INFO_NUM_OVERLAP 7
+#define MBR_INFO_HEADS 8
+#define MBR_INFO_DIM_HEAD 9
+#define MBR_INFO_BAND_FREQS 10
+#define MBR_INFO_DTYPE 11
+#define MBR_INFO_DEVICE 12
+#define MBR_INFO_HOP 13
+
+/* kernel backends for mbr_set_backend */
+#define MBR_BACKEND_SIMT 0 /* CUDA-core kernels (fp32 path, cross-check) */
+#define MBR_BACKEND_TC 1   /* tcgen05 tensor-core kernels (fp16 / bf16) */
+
+typedef struct mbr_handle mbr_handle;
+
+/* Message of the last failed call on this thread ("" if none). */
+MBR_API const char* mbr_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+MBR_API int mbr_version(void);
+
+/* Load a .csm checkpoint onto `device` with compute dtype MBR_FP32 / MBR_FP16 /
+ * MBR_BF16 (2-D fp32 weights are rounded to the dtype, as --fp16/--bf16 do).
+ * Replaces cudasep::app::load_model (src/inference_app.cpp:258-311) and
+ * MelBandRoformer::load (src/model_mel_band_roformer.cu:75-264). */
+MBR_API int mbr_create(const char* csm_path, int device, int dtype, mbr_handle** out);
+
+/* Release the handle, its weights and workspaces. */
+MBR_API void mbr_destroy(mbr_handle* h);
+
+/* Config / handle queries (MBR_INFO_*).  Replaces MelBandRoformer::config()
+ * (src/model_mel_band_roformer.h:46) and LoadedModel fields
+ * (src/inference_app.h:16-30). */
+MBR_API int mbr_get_info(mbr_handle* h, int what, int64_t* value);
+
+/* Output samples per channel of a forward over `L` input samples. */
+MBR_API int mbr_output_length(mbr_handle* h, int64_t L, int64_t* lout);
+
+/* One forward over a chunk batch: d_audio [B][C][L] -> d_out [B][S][C][lout]
+ * (S = num_stems; lout from mbr_output_length).  Replaces
+ * MelBandRoformer::forward (src/model_mel_band_roformer.cu:682-845). */
+MBR_API int mbr_forward_chunk(mbr_handle* h, const float* d_audio, int B, int64_t L, float* d_out, void* stream);
+
+/* Per-stage tap of one forward, for parity checks (fp32 copy into d_tap):
+ * 0 band-split output [B][T][NB][D], 1 residual stream after depth block 0,
+ * 2 final residual stream, 3 stem-0 mask [B*T][2J], 4 masked spectrum
+ * [B][S][C][T][F][2].  With d_tap == NULL only *n is set. */
+MBR_API int mbr_forward_tap(mbr_handle* h, const float* d_audio, int B, int64_t L, int tap, float* d_tap,
+                            int64_t* n, void* stream);
+
+/* Whole-track separation with inputs and outputs in device memory:
+ * d_track [C][N] -> d_out [S][C][N].  overlap <= 0 uses the checkpoint's
+ * num_overlap, (0,1) is an overlap ratio, >= 1 a num_overlap; chunk_batch >= 1.
+ * Replaces process_chunked (src/inference_app.cpp:72-232) and the timed part
+ * of run_inference (:313-357). */
+MBR_API int mbr_separate_device(mbr_handle* h, const float* d_track, int64_t N, float overlap, int chunk_batch,
+                                float* d_out, void* stream);
+
+/* Whole-track separation from host memory (copies in, separates, copies out,
+ * synchronises): h_track [C][N] -> h_out [S][C][N].  With n_gpus > 1 the
+ * chunk list is split into contiguous ranges run on devices
+ * device .. device+n_gpus-1 in parallel; only the overlap-add boundary is
+ * exchanged (peer copies).  Replaces run_inference (src/inference_app.cpp:313-357)
+ * without the WAV file I/O. */
+MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float overlap, int chunk_batch, int n_gpus,
+                         float* h_out);
+
+/* Sharded separation for one-process-per-GPU callers (e.g. torch.distributed).
+ * mbr_shard_info: for track length N and (rank, world) gives the chunk range
+ * [c0, c1), the padded-sample window [lo, hi) the shard accumulates, the
+ * part [send_lo, hi) it must send to rank+1, and the track range
+ * [out_lo, out_hi) it finalises.  Values are written to info[0..7] as
+ * c0, c1, lo, hi, send_lo, out_lo, out_hi, n_chunks. */
+MBR_API int mbr_shard_info(mbr_handle* h, int64_t N, float overlap, int rank, int world, int64_t* info);
+/* Runs the shard's chunks: d_acc [S*C][hi-lo], d_wsum [hi-lo] (overwritten). */
+MBR_API int mbr_shard_run(mbr_handle* h, const float* d_track, int64_t N, float overlap, int chunk_batch, int rank,
+                          int world, float* d_acc, float* d_wsum, void* stream);
+/* Adds the previous rank's boundary (d_recv_acc [S*C][recv_len],
+ * d_recv_wsum [recv_len], recv_len = previous hi - this lo) into the
+ * shard's accumulators (call before sending this shard's own boundary). */
+MBR_API int mbr_shard_add_boundary(mbr_handle* h, int64_t N, float overlap, int rank, int world, float* d_acc,
+                                   float* d_wsum, const float* d_recv_acc, const float* d_recv_wsum,
+                                   int64_t recv_len, void* stream);
+/* Normalises the shard's own range into d_out [S*C][out_stride] at columns
+ * [out_lo, out_hi) (track coordinates). */
+MBR_API int mbr_shard_finalize(mbr_handle* h, int64_t N, float overlap, int rank, int world, float* d_acc,
+                               float* d_wsum, float* d_out, int64_t out_stride, void* stream);
+
+/* Kernel backend selection (MBR_BACKEND_*) for the GEMMs and the attention. */
+MBR_API int mbr_set_backend(mbr_handle* h, int gemm, int attention);
+
+/* Kernel launches issued by the last forward / separation on this handle. */
+MBR_API int mbr_last_launches(mbr_handle* h, int64_t* n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MBR_B200_H */

@@ -1,0 +1,325 @@
+// capi.cpp — extern "C" boundary (include/mbr_b200.h).  No C++ exception crosses it.
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/mbr_b200.h"
+#include "common.h"
+#include "model.h"
+#include "separator.h"
+#include "weights.h"
+
+struct mbr_handle {
+    std::string path;
+    int device = 0;
+    int dtype = 1;
+    std::unique_ptr<mbr::MelBandRoformer> model;
+    std::unique_ptr<mbr::Separator> sep;
+    cudaStream_t stream = nullptr;
+    // host-path buffers
+    float* d_track = nullptr;
+    float* d_out = nullptr;
+    size_t track_cap = 0, out_cap = 0;
+    // per-extra-GPU handles for multi-GPU mbr_separate
+    std::vector<std::unique_ptr<mbr_handle>> peers;
+    int64_t launches = 0;
+    ~mbr_handle() {
+        peers.clear();
+        if (model) cudaSetDevice(device);
+        if (d_track) cudaFree(d_track);
+        if (d_out) cudaFree(d_out);
+        if (stream) cudaStreamDestroy(stream);
+        sep.reset();
+        model.reset();
+    }
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+template <class F>
+int guard(F&& f) {
+    try {
+        g_err.clear();
+        f();
+        return MBR_OK;
+    } catch (const mbr::Error& e) {
+        g_err = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        g_err = "host out of memory";
+        return MBR_ERR_OOM;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return MBR_ERR_INVALID;
+    }
+}
+
+void need(bool c, const char* m) {
+    if (!c) throw mbr::Error(MBR_ERR_INVALID, m);
+}
+
+std::unique_ptr<mbr_handle> make_handle(const char* path, int device, int dtype) {
+    auto h = std::make_unique<mbr_handle>();
+    h->path = path;
+    h->device = device;
+    h->dtype = dtype;
+    int ndev = 0;
+    MBR_CUDA(cudaGetDeviceCount(&ndev));
+    need(device >= 0 && device < ndev, "device index out of range");
+    MBR_CUDA(cudaSetDevice(device));
+    mbr::ModelWeights w = mbr::ModelWeights::load(path);
+    h->model = std::make_unique<mbr::MelBandRoformer>(w, device, dtype);
+    h->sep = std::make_unique<mbr::Separator>(*h->model);
+    MBR_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    return h;
+}
+
+float* ensure(float*& p, size_t& cap, size_t bytes) {
+    if (cap < bytes) {
+        if (p) MBR_CUDA(cudaFree(p));
+        p = nullptr;
+        MBR_CUDA(cudaMalloc(&p, bytes));
+        cap = bytes;
+    }
+    return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+MBR_API const char* mbr_last_error(void) { return g_err.c_str(); }
+MBR_API int mbr_version(void) { return 100; }
+
+MBR_API int mbr_create(const char* csm_path, int device, int dtype, mbr_handle** out) {
+    return guard([&] {
+        need(csm_path && out, "null argument");
+        *out = nullptr;
+        *out = make_handle(csm_path, device, dtype).release();
+    });
+}
+
+MBR_API void mbr_destroy(mbr_handle* h) { delete h; }
+
+MBR_API int mbr_get_info(mbr_handle* h, int what, int64_t* value) {
+    return guard([&] {
+        need(h && value, "null argument");
+        const mbr::MBRConfig& c = h->model->config();
+        switch (what) {
+            case MBR_INFO_DIM: *value = c.dim; break;
+            case MBR_INFO_DEPTH: *value = c.depth; break;
+            case MBR_INFO_NUM_STEMS: *value = c.num_stems; break;
+            case MBR_INFO_CHANNELS: *value = h->model->channels(); break;
+            case MBR_INFO_NUM_BANDS: *value = c.num_bands; break;
+            case MBR_INFO_SAMPLE_RATE: *value = c.sample_rate; break;
+            case MBR_INFO_CHUNK_SIZE: *value = c.chunk_size; break;
+            case MBR_INFO_NUM_OVERLAP: *value = c.num_overlap; break;
+            case MBR_INFO_HEADS: *value = c.heads; break;
+            case MBR_INFO_DIM_HEAD: *value = c.dim_head; break;
+            case MBR_INFO_BAND_FREQS: *value = h->model->band_freqs(); break;
+            case MBR_INFO_DTYPE: *value = h->dtype; break;
+            case MBR_INFO_DEVICE: *value = h->device; break;
+            case MBR_INFO_HOP: *value = c.stft_hop_length; break;
+            default: throw mbr::Error(MBR_ERR_INVALID, "unknown info key");
+        }
+    });
+}
+
+MBR_API int mbr_output_length(mbr_handle* h, int64_t L, int64_t* lout) {
+    return guard([&] {
+        need(h && lout, "null argument");
+        *lout = h->model->out_length(L);
+    });
+}
+
+MBR_API int mbr_forward_chunk(mbr_handle* h, const float* d_audio, int B, int64_t L, float* d_out, void* stream) {
+    return guard([&] {
+        need(h && d_audio && d_out, "null argument");
+        h->model->forward(d_audio, B, L, d_out, (cudaStream_t)stream);
+        h->launches = h->model->last_launches();
+    });
+}
+
+MBR_API int mbr_forward_tap(mbr_handle* h, const float* d_audio, int B, int64_t L, int tap, float* d_tap, int64_t* n,
+                            void* stream) {
+    return guard([&] {
+        need(h && n, "null argument");
+        *n = h->model->forward_tap(d_audio, B, L, tap, d_tap, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_separate_device(mbr_handle* h, const float* d_track, int64_t N, float overlap, int chunk_batch,
+                                float* d_out, void* stream) {
+    return guard([&] {
+        need(h && d_track && d_out, "null argument");
+        need(N > 0, "empty track");
+        MBR_CUDA(cudaSetDevice(h->device));
+        h->sep->separate(d_track, N, overlap, chunk_batch, d_out, (cudaStream_t)stream);
+        h->launches = h->sep->last_launches();
+    });
+}
+
+MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float overlap, int chunk_batch, int n_gpus,
+                         float* h_out) {
+    return guard([&] {
+        need(h && h_track && h_out, "null argument");
+        need(N > 0, "empty track");
+        need(n_gpus >= 1, "n_gpus must be >= 1");
+        const int C = h->model->channels(), S = h->model->config().num_stems, SC = S * C;
+        const mbr::MBRConfig& cfg = h->model->config();
+        mbr::ChunkPlan plan = mbr::make_chunk_plan(N, cfg.chunk_size, overlap, cfg.num_overlap);
+        int world = (plan.single || (int)plan.starts.size() < n_gpus) ? 1 : n_gpus;
+        if (world == 1) {
+            MBR_CUDA(cudaSetDevice(h->device));
+            float* dt = ensure(h->d_track, h->track_cap, sizeof(float) * C * N);
+            float* dout = ensure(h->d_out, h->out_cap, sizeof(float) * SC * N);
+            MBR_CUDA(cudaMemcpyAsync(dt, h_track, sizeof(float) * C * N, cudaMemcpyHostToDevice, h->stream));
+            h->sep->separate(dt, N, overlap, chunk_batch, dout, h->stream);
+            MBR_CUDA(cudaMemcpyAsync(h_out, dout, sizeof(float) * SC * N, cudaMemcpyDeviceToHost, h->stream));
+            MBR_CUDA(cudaStreamSynchronize(h->stream));
+            h->launches = h->sep->last_launches();
+            return;
+        }
+        // one handle per GPU (device, device+1, ...)
+        while ((int)h->peers.size() < world - 1)
+            h->peers.push_back(make_handle(h->path.c_str(), h->device + 1 + (int)h->peers.size(), h->dtype));
+        std::vector<mbr_handle*> hs{h};
+        for (auto& p : h->peers) hs.push_back(p.get());
+        std::vector<mbr::Shard> sh(world);
+        std::vector<float*> acc(world), ws(world);
+        std::vector<std::string> errs(world);
+        for (int r = 0; r < world; ++r) sh[r] = mbr::make_shard(plan, r, world);
+        auto run = [&](int r) {
+            try {
+                mbr_handle* x = hs[r];
+                MBR_CUDA(cudaSetDevice(x->device));
+                int64_t span = sh[r].hi - sh[r].lo;
+                float* dt = ensure(x->d_track, x->track_cap, sizeof(float) * C * N);
+                // accumulators followed by the receive buffer for the previous boundary
+                float* buf = ensure(x->d_out, x->out_cap, sizeof(float) * ((size_t)(SC + 1) * span * 2 + SC * N));
+                acc[r] = buf;
+                ws[r] = buf + (size_t)SC * span;
+                MBR_CUDA(cudaMemcpyAsync(dt, h_track, sizeof(float) * C * N, cudaMemcpyHostToDevice, x->stream));
+                x->sep->run_shard(plan, sh[r], dt, chunk_batch, acc[r], ws[r], x->stream);
+                MBR_CUDA(cudaStreamSynchronize(x->stream));
+            } catch (const std::exception& e) {
+                errs[r] = e.what();
+            }
+        };
+        std::vector<std::thread> th;
+        for (int r = 0; r < world; ++r) th.emplace_back(run, r);
+        for (auto& t : th) t.join();
+        for (auto& e : errs)
+            if (!e.empty()) throw mbr::Error(MBR_ERR_CUDA, e);
+        // boundary chain: rank r-1's tail [send_lo, hi) is added into rank r
+        for (int r = 1; r < world; ++r) {
+            mbr_handle* x = hs[r];
+            int64_t rlen = sh[r - 1].hi - sh[r - 1].send_lo;
+            int64_t off = sh[r - 1].send_lo - sh[r - 1].lo, span_prev = sh[r - 1].hi - sh[r - 1].lo;
+            int64_t span = sh[r].hi - sh[r].lo;
+            float* racc = ws[r] + span;  // receive area after the accumulators
+            float* rws = racc + (size_t)SC * rlen;
+            MBR_CUDA(cudaSetDevice(x->device));
+            for (int o = 0; o < SC; ++o)
+                MBR_CUDA(cudaMemcpyPeerAsync(racc + (size_t)o * rlen, x->device,
+                                             acc[r - 1] + (size_t)o * span_prev + off, hs[r - 1]->device,
+                                             sizeof(float) * rlen, x->stream));
+            MBR_CUDA(cudaMemcpyPeerAsync(rws, x->device, ws[r - 1] + off, hs[r - 1]->device, sizeof(float) * rlen,
+                                         x->stream));
+            x->sep->add_boundary(sh[r], acc[r], ws[r], racc, rws, rlen, x->stream);
+            MBR_CUDA(cudaStreamSynchronize(x->stream));
+        }
+        // normalise each own range and copy it out
+        for (int r = 0; r < world; ++r) {
+            mbr_handle* x = hs[r];
+            MBR_CUDA(cudaSetDevice(x->device));
+            int64_t span = sh[r].hi - sh[r].lo;
+            int64_t rlen = r > 0 ? sh[r - 1].hi - sh[r - 1].send_lo : 0;
+            float* dout = ws[r] + span + (size_t)(SC + 1) * rlen;
+            x->sep->finalize_shard(plan, sh[r], acc[r], ws[r], dout, N, x->stream);
+            int64_t w = sh[r].out_hi - sh[r].out_lo;
+            if (w > 0)
+                MBR_CUDA(cudaMemcpy2DAsync(h_out + sh[r].out_lo, sizeof(float) * N, dout + sh[r].out_lo,
+                                           sizeof(float) * N, sizeof(float) * w, SC, cudaMemcpyDeviceToHost,
+                                           x->stream));
+        }
+        for (int r = 0; r < world; ++r) {
+            MBR_CUDA(cudaSetDevice(hs[r]->device));
+            MBR_CUDA(cudaStreamSynchronize(hs[r]->stream));
+        }
+        MBR_CUDA(cudaSetDevice(h->device));
+    });
+}
+
+MBR_API int mbr_shard_info(mbr_handle* h, int64_t N, float overlap, int rank, int world, int64_t* info) {
+    return guard([&] {
+        need(h && info, "null argument");
+        const mbr::MBRConfig& c = h->model->config();
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, c.chunk_size, overlap, c.num_overlap);
+        need(!p.single, "track fits one chunk: nothing to shard");
+        mbr::Shard s = mbr::make_shard(p, rank, world);
+        int64_t v[8] = {s.c0, s.c1, s.lo, s.hi, s.send_lo, s.out_lo, s.out_hi, (int64_t)p.starts.size()};
+        for (int i = 0; i < 8; ++i) info[i] = v[i];
+    });
+}
+
+MBR_API int mbr_shard_run(mbr_handle* h, const float* d_track, int64_t N, float overlap, int chunk_batch, int rank,
+                          int world, float* d_acc, float* d_wsum, void* stream) {
+    return guard([&] {
+        need(h && d_track && d_acc && d_wsum, "null argument");
+        const mbr::MBRConfig& c = h->model->config();
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, c.chunk_size, overlap, c.num_overlap);
+        need(!p.single, "track fits one chunk: nothing to shard");
+        MBR_CUDA(cudaSetDevice(h->device));
+        h->sep->run_shard(p, mbr::make_shard(p, rank, world), d_track, chunk_batch, d_acc, d_wsum,
+                          (cudaStream_t)stream);
+        h->launches = h->sep->last_launches();
+    });
+}
+
+MBR_API int mbr_shard_add_boundary(mbr_handle* h, int64_t N, float overlap, int rank, int world, float* d_acc,
+                                   float* d_wsum, const float* d_recv_acc, const float* d_recv_wsum,
+                                   int64_t recv_len, void* stream) {
+    return guard([&] {
+        need(h && d_acc && d_wsum, "null argument");
+        const mbr::MBRConfig& c = h->model->config();
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, c.chunk_size, overlap, c.num_overlap);
+        mbr::Shard s = mbr::make_shard(p, rank, world);
+        MBR_CUDA(cudaSetDevice(h->device));
+        h->sep->add_boundary(s, d_acc, d_wsum, d_recv_acc, d_recv_wsum, recv_len, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_shard_finalize(mbr_handle* h, int64_t N, float overlap, int rank, int world, float* d_acc,
+                               float* d_wsum, float* d_out, int64_t out_stride, void* stream) {
+    return guard([&] {
+        need(h && d_acc && d_wsum && d_out, "null argument");
+        const mbr::MBRConfig& c = h->model->config();
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, c.chunk_size, overlap, c.num_overlap);
+        mbr::Shard s = mbr::make_shard(p, rank, world);
+        MBR_CUDA(cudaSetDevice(h->device));
+        h->sep->finalize_shard(p, s, d_acc, d_wsum, d_out, out_stride, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_set_backend(mbr_handle* h, int gemm, int attention) {
+    return guard([&] {
+        need(h, "null argument");
+        need((gemm == 0 || gemm == 1) && (attention == 0 || attention == 1), "backend must be 0 or 1");
+        h->model->set_backend(gemm, attention);
+    });
+}
+
+MBR_API int mbr_last_launches(mbr_handle* h, int64_t* n) {
+    return guard([&] {
+        need(h && n, "null argument");
+        *n = h->launches;
+    });
+}
+
+}  // extern "C"

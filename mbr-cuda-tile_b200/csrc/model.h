@@ -1,0 +1,177 @@
+// model.h — MelBandRoformer forward on one B200 (host orchestration).
+//
+// Mirrors the reference class of src/model_mel_band_roformer.h:11-141
+// (MBRConfig::from_json, MelBandRoformer::load/forward/config).  The forward is
+// a fixed sequence of kernel launches on one stream over a workspace that is
+// allocated once per input shape; weights are uploaded once, converted to the
+// compute dtype and packed for the kernels (band-split weights as one
+// block-diagonal matrix, per-band mask-estimator weights stacked per layer).
+#pragma once
+
+#include <stdint.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "ops.h"
+#include "weights.h"
+
+namespace mbr {
+
+struct MBRConfig {
+    int dim = 384;
+    int depth = 6;
+    bool stereo = true;
+    int num_stems = 1;
+    int time_transformer_depth = 1;
+    int freq_transformer_depth = 1;
+    int num_bands = 60;
+    int dim_head = 64;
+    int heads = 8;
+    int mask_estimator_depth = 2;
+    int mlp_expansion_factor = 4;
+    bool zero_dc = true;
+    int sample_rate = 44100;
+    int stft_n_fft = 2048;
+    int stft_hop_length = 441;
+    int stft_win_length = 2048;
+    bool stft_normalized = false;
+    bool match_input_audio_length = false;
+    int dim_freqs_in = 1025;
+    bool skip_connection = false;
+    // app-level keys (src/inference_app.cpp:42-44, :298)
+    int chunk_size = 0;
+    int num_overlap = 1;
+    std::vector<std::string> instruments;
+    static MBRConfig from_json(const JsonValue& j);
+};
+
+// Kernel backends selectable per model (the tensor-core path is the default for
+// fp16/bf16; the CUDA-core path is the fp32 path and a cross-check).
+enum Backend { BACKEND_SIMT = 0, BACKEND_TC = 1 };
+
+class MelBandRoformer {
+public:
+    // Loads and uploads the weights to `device`; dtype DT_F32 / DT_F16 / DT_BF16.
+    MelBandRoformer(const ModelWeights& w, int device, int dtype);
+    ~MelBandRoformer();
+    MelBandRoformer(const MelBandRoformer&) = delete;
+    MelBandRoformer& operator=(const MelBandRoformer&) = delete;
+
+    const MBRConfig& config() const { return cfg_; }
+    int device() const { return device_; }
+    int dtype() const { return dtype_; }
+    int channels() const { return C_; }
+    int64_t band_freqs() const { return J_; }
+    int64_t frames(int64_t L) const;      // STFT frames T of an L-sample input
+    int64_t out_length(int64_t L) const;  // output samples of an L-sample input
+
+    // audio [B][C][L] (device, fp32) -> out [B][S][C][out_length(L)] (device, fp32).
+    void forward(const float* d_audio, int B, int64_t L, float* d_out, cudaStream_t st);
+
+    // Per-stage taps for parity tests (same numbering as the oracle):
+    //  0 band-split output, 1 after depth block 0, 2 final residual stream,
+    //  3 stem-0 mask, 4 masked spectrum.  Copies into d_tap (fp32) and
+    //  returns the element count (d_tap == nullptr only sizes).
+    int64_t forward_tap(const float* d_audio, int B, int64_t L, int tap, float* d_tap, cudaStream_t st);
+
+    void set_backend(int gemm, int attention) {
+        gemm_backend_ = gemm;
+        attn_backend_ = attention;
+    }
+    int gemm_backend() const { return gemm_backend_; }
+    int attn_backend() const { return attn_backend_; }
+    // Kernel launches issued by the last forward().
+    int64_t last_launches() const { return launches_; }
+
+private:
+    struct Plan {
+        size_t first = 0;  // index into the workspace's group array
+        int n = 0, maxM = 0, maxN = 0, maxK = 0, epi = 0;
+        // operand tensor shapes for the tensor-core path (rows x cols, elements)
+        const void* a_base = nullptr;
+        int64_t a_rows = 0, a_cols = 0;
+        const void* b_base = nullptr;
+        int64_t b_rows = 0, b_cols = 0;
+    };
+    struct LayerW {
+        float* attn_gamma;
+        void* wqkv;
+        float* wg;
+        float* bg;
+        void* wo;
+        float* ff_gamma;
+        void* w1;
+        float* b1;
+        void* w2;
+        float* b2;
+    };
+    struct TransW {
+        std::vector<LayerW> layers;
+        float* final_gamma;
+    };
+    struct Workspace {
+        int B = 0;
+        int64_t L = 0, T = 0, MT = 0, M = 0, lout = 0;
+        void* base = nullptr;
+        size_t bytes = 0;
+        float2* spec;
+        void* xb;
+        float* R;
+        void* xn;
+        float* gates;
+        void* qkv;
+        void* q;
+        void* k;
+        void* v;
+        void* merged;
+        void* hf;
+        void* rm;
+        void* mh[2];
+        float* masks;
+        float2* y;
+        float* frames;
+        std::vector<float*> skip;
+        float *rope_t_cos, *rope_t_sin, *rope_f_cos, *rope_f_sin;
+        ops::GemmGroup* d_groups;
+        std::vector<ops::GemmGroup> h_groups;
+        Plan band_split;
+        std::vector<Plan> layer_plans;  // [depth][2][layers][4]: qkv, out, ffn1, ffn2
+        std::vector<std::vector<Plan>> mask_plans;  // [stem][linear]
+    };
+
+    Workspace& workspace(int B, int64_t L);
+    void build_plans(Workspace& ws);
+    void run_gemm(const Workspace& ws, const Plan& p, cudaStream_t st);
+    void run_transformer(Workspace& ws, const TransW& tw, int mode, const Plan* plans, bool last_of_model,
+                         cudaStream_t st);
+    void run_forward(Workspace& ws, const float* d_audio, float* d_out, int tap, float* d_tap, int64_t* tap_n,
+                     cudaStream_t st);
+
+    MBRConfig cfg_;
+    int device_ = 0, dtype_ = DT_F16, C_ = 2, F_ = 1025, NB_ = 60, D_ = 384, H_ = 8, dh_ = 64, DI_ = 512,
+        hid_ = 1536;
+    int64_t J_ = 0, KP_ = 0;
+    int gemm_backend_ = BACKEND_SIMT, attn_backend_ = BACKEND_SIMT;
+    int64_t launches_ = 0;
+
+    std::vector<int> band_bd_, band_boff_, band_kofs_;  // host copies
+    void* wbase_ = nullptr;  // single device allocation holding every weight
+    int *d_fi_, *d_band_jofs_, *d_band_kofs_, *d_rev_off_, *d_rev_idx_;
+    float *d_nbpf_, *d_window_, *d_bs_gamma_, *d_bs_bias_;
+    float2* d_twiddle_;
+    void* d_wbs_;
+    std::vector<TransW> tt_, ft_;
+    struct MaskW {
+        std::vector<void*> w;
+        std::vector<float*> b;
+        std::vector<int> in, out;  // per-band dims (out of the last layer varies per band)
+    };
+    std::vector<MaskW> mask_;
+    std::map<std::pair<int, int64_t>, std::unique_ptr<Workspace>> ws_;
+};
+
+}  // namespace mbr

@@ -1,0 +1,196 @@
+"""cudasep — Python binding of libmbr_b200.so (include/mbr_b200.h) over ctypes.
+
+Mirrors the reference's C++ entry points (cudasep::app::load_model /
+run_inference, MelBandRoformer::forward) for Python callers, tests and the
+benchmark.  torch is used only to hold device memory and streams; every
+computation runs in the library's CUDA kernels.  There is no fallback: if the
+shared library is missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmbr_b200.so")
+
+FP32, FP16, BF16 = 0, 1, 3
+DTYPES = {"fp32": FP32, "float32": FP32, "fp16": FP16, "float16": FP16, "bf16": BF16, "bfloat16": BF16}
+BACKEND_SIMT, BACKEND_TC = 0, 1
+
+INFO = dict(dim=0, depth=1, num_stems=2, channels=3, num_bands=4, sample_rate=5, chunk_size=6, num_overlap=7,
+            heads=8, dim_head=9, band_freqs=10, dtype=11, device=12, hop=13)
+
+# Every symbol include/mbr_b200.h declares (checked by the ABI test).
+EXPORTS = [
+    "mbr_last_error", "mbr_version", "mbr_create", "mbr_destroy", "mbr_get_info", "mbr_output_length",
+    "mbr_forward_chunk", "mbr_forward_tap", "mbr_separate_device", "mbr_separate", "mbr_shard_info",
+    "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_backend", "mbr_last_launches",
+]
+
+_lib = None
+
+
+class MBRError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+def lib():
+    """Load libmbr_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` (or __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i64, i64p, fp = ctypes.c_void_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64), ctypes.c_void_p
+        c_int, c_float = ctypes.c_int, ctypes.c_float
+        L.mbr_last_error.restype = ctypes.c_char_p
+        L.mbr_version.restype = c_int
+        L.mbr_create.argtypes = [ctypes.c_char_p, c_int, c_int, ctypes.POINTER(vp)]
+        L.mbr_destroy.argtypes = [vp]
+        L.mbr_destroy.restype = None
+        L.mbr_get_info.argtypes = [vp, c_int, i64p]
+        L.mbr_output_length.argtypes = [vp, i64, i64p]
+        L.mbr_forward_chunk.argtypes = [vp, fp, c_int, i64, fp, vp]
+        L.mbr_forward_tap.argtypes = [vp, fp, c_int, i64, c_int, fp, i64p, vp]
+        L.mbr_separate_device.argtypes = [vp, fp, i64, c_float, c_int, fp, vp]
+        L.mbr_separate.argtypes = [vp, fp, i64, c_float, c_int, c_int, fp]
+        L.mbr_shard_info.argtypes = [vp, i64, c_float, c_int, c_int, i64p]
+        L.mbr_shard_run.argtypes = [vp, fp, i64, c_float, c_int, c_int, c_int, fp, fp, vp]
+        L.mbr_shard_add_boundary.argtypes = [vp, i64, c_float, c_int, c_int, fp, fp, fp, fp, i64, vp]
+        L.mbr_shard_finalize.argtypes = [vp, i64, c_float, c_int, c_int, fp, fp, fp, i64, vp]
+        L.mbr_set_backend.argtypes = [vp, c_int, c_int]
+        L.mbr_last_launches.argtypes = [vp, i64p]
+        _lib = L
+    return _lib
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise MBRError(rc, lib().mbr_last_error().decode())
+
+
+def _ptr(t) -> int:
+    """Device/host address of a torch tensor or numpy array."""
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+
+
+class Model:
+    """A loaded MelBandRoformer (`.csm`) on one GPU.
+
+    dtype: "fp32" | "fp16" | "bf16" (the reference's --bf16/--fp16 switch; fp32
+    keeps every weight in fp32).
+    """
+
+    def __init__(self, csm_path: str, device: int = 0, dtype="fp16"):
+        self.h = ctypes.c_void_p()
+        d = DTYPES[dtype] if isinstance(dtype, str) else int(dtype)
+        _check(lib().mbr_create(csm_path.encode(), int(device), d, ctypes.byref(self.h)))
+        self.device = int(device)
+        self.path = csm_path
+
+    def close(self):
+        if self.h:
+            lib().mbr_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self, key: str) -> int:
+        v = ctypes.c_int64()
+        _check(lib().mbr_get_info(self.h, INFO[key], ctypes.byref(v)))
+        return v.value
+
+    def output_length(self, L: int) -> int:
+        v = ctypes.c_int64()
+        _check(lib().mbr_output_length(self.h, int(L), ctypes.byref(v)))
+        return v.value
+
+    def set_backend(self, gemm: int = BACKEND_TC, attention: int = BACKEND_TC):
+        _check(lib().mbr_set_backend(self.h, int(gemm), int(attention)))
+
+    def last_launches(self) -> int:
+        v = ctypes.c_int64()
+        _check(lib().mbr_last_launches(self.h, ctypes.byref(v)))
+        return v.value
+
+    # ---- device entry points (torch CUDA tensors) ----
+    def forward(self, audio, out=None, stream=None):
+        """audio: float32 CUDA tensor [B, C, L] -> [B, S, C, Lout]."""
+        import torch
+        assert audio.is_cuda and audio.dtype == torch.float32 and audio.is_contiguous()
+        B, C, L = audio.shape
+        S = self.info("num_stems")
+        lo = self.output_length(L)
+        if out is None:
+            out = torch.empty((B, S, C, lo), dtype=torch.float32, device=audio.device)
+        _check(lib().mbr_forward_chunk(self.h, _ptr(audio), B, L, _ptr(out), _stream(stream)))
+        return out
+
+    def tap(self, audio, tap: int, stream=None):
+        import torch
+        B, C, L = audio.shape
+        n = ctypes.c_int64()
+        _check(lib().mbr_forward_tap(self.h, _ptr(audio), B, L, tap, None, ctypes.byref(n), _stream(stream)))
+        buf = torch.empty(n.value, dtype=torch.float32, device=audio.device)
+        _check(lib().mbr_forward_tap(self.h, _ptr(audio), B, L, tap, _ptr(buf), ctypes.byref(n), _stream(stream)))
+        return buf
+
+    def separate_device(self, track, overlap: float = -1.0, chunk_batch: int = 1, out=None, stream=None):
+        """track: float32 CUDA tensor [C, N] -> [S, C, N]."""
+        import torch
+        C, N = track.shape
+        S = self.info("num_stems")
+        if out is None:
+            out = torch.empty((S, C, N), dtype=torch.float32, device=track.device)
+        _check(lib().mbr_separate_device(self.h, _ptr(track), N, float(overlap), int(chunk_batch), _ptr(out),
+                                         _stream(stream)))
+        return out
+
+    # ---- host entry point ----
+    def separate(self, track: np.ndarray, overlap: float = -1.0, chunk_batch: int = 1, n_gpus: int = 1,
+                 out: np.ndarray | None = None) -> np.ndarray:
+        """track: float32 host array [C, N] -> [S, C, N] (host); synchronous."""
+        track = np.ascontiguousarray(track, dtype=np.float32)
+        C, N = track.shape
+        S = self.info("num_stems")
+        if out is None:
+            out = np.empty((S, C, N), dtype=np.float32)
+        _check(lib().mbr_separate(self.h, _ptr(track), N, float(overlap), int(chunk_batch), int(n_gpus), _ptr(out)))
+        return out
+
+    # ---- sharded (one process per GPU) ----
+    def shard_info(self, N: int, overlap: float, rank: int, world: int) -> dict:
+        info = (ctypes.c_int64 * 8)()
+        _check(lib().mbr_shard_info(self.h, int(N), float(overlap), rank, world, info))
+        keys = ["c0", "c1", "lo", "hi", "send_lo", "out_lo", "out_hi", "n_chunks"]
+        return dict(zip(keys, list(info)))
+
+    def shard_run(self, track, N, overlap, chunk_batch, rank, world, acc, wsum, stream=None):
+        _check(lib().mbr_shard_run(self.h, _ptr(track), int(N), float(overlap), int(chunk_batch), rank, world,
+                                   _ptr(acc), _ptr(wsum), _stream(stream)))
+
+    def shard_add_boundary(self, N, overlap, rank, world, acc, wsum, racc, rwsum, rlen, stream=None):
+        _check(lib().mbr_shard_add_boundary(self.h, int(N), float(overlap), rank, world, _ptr(acc), _ptr(wsum),
+                                            _ptr(racc), _ptr(rwsum), int(rlen), _stream(stream)))
+
+    def shard_finalize(self, N, overlap, rank, world, acc, wsum, out, out_stride, stream=None):
+        _check(lib().mbr_shard_finalize(self.h, int(N), float(overlap), rank, world, _ptr(acc), _ptr(wsum),
+                                        _ptr(out), int(out_stride), _stream(stream)))

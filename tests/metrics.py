@@ -1,0 +1,21 @@
+"""Error metrics used by the parity tests."""
+import numpy as np
+
+
+def rel_max_err(ref: np.ndarray, got: np.ndarray) -> float:
+    """max |got - ref| / max |ref| (the fp32 parity measure; bar 1e-4)."""
+    ref = np.asarray(ref, np.float64)
+    got = np.asarray(got, np.float64)
+    den = np.abs(ref).max()
+    return float(np.abs(got - ref).max() / (den if den > 0 else 1.0))
+
+
+def snr_db(ref: np.ndarray, got: np.ndarray) -> float:
+    """Signal-to-error ratio of got against ref in dB (the fp16/bf16 measure; bar 60 dB)."""
+    ref = np.asarray(ref, np.float64)
+    got = np.asarray(got, np.float64)
+    err = np.sum((got - ref) ** 2)
+    sig = np.sum(ref ** 2)
+    if err == 0:
+        return float("inf")
+    return float(10.0 * np.log10(sig / err))

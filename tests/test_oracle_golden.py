@@ -1,0 +1,126 @@
+"""Pins the CPU oracle against known answers (no GPU).
+
+ - band map: the 38 distinct widths 8*nf of the 60-band split equal the
+   reference's hard-coded mask-estimator output whitelist for dim 256
+   (src/mbr_cuda_tile.cu:2289-2311, out_features of the last band linear,
+   = 2 * band_dim = 8 * nf); the oracle's C++ generator and csm_tool's numpy
+   generator agree bit-exactly with the committed fixture.
+ - STFT / iSTFT: the oracle equals torch.stft / torch.istft (fp64) fixtures.
+ - chunk plans: chunk starts / border / padded length equal an independent
+   restatement of resolve_step + process_chunked.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+G = os.path.join(HERE, "golden")
+
+# src/mbr_cuda_tile.cu:2300-2311 (out_features accepted with in_features == 1024)
+# plus the two separate cases of :2296-2299 (128 and 48).
+REFERENCE_WIDTH_WHITELIST = sorted([
+    128, 48, 56, 72, 80, 88, 104, 120, 136, 152, 160, 176, 192, 208, 224, 232, 248, 264, 288, 312, 328, 352,
+    376, 400, 432, 456, 488, 528, 568, 608, 640, 688, 744, 792, 840, 904, 976, 1040,
+])
+
+
+def test_band_map_matches_reference_whitelist():
+    import oracle
+
+    fi, nfpb, nbpf = oracle.band_map(44100, 2048, 60, True)
+    assert len(fi) == 3958 and nfpb.sum() == 1979
+    assert nbpf.max() == 2 and nbpf.min() >= 1
+    assert sorted(set((8 * nfpb).tolist())) == REFERENCE_WIDTH_WHITELIST
+
+
+def test_band_map_generators_agree_with_fixture():
+    import csm_tool
+    import oracle
+
+    g = np.load(os.path.join(G, "band_map.npz"))
+    for fi, nfpb, nbpf in (oracle.band_map(44100, 2048, 60, True), csm_tool.mel_band_map(44100, 2048, 60, True)):
+        assert np.array_equal(fi, g["freq_indices"])
+        assert np.array_equal(nfpb, g["num_freqs_per_band"])
+        assert np.array_equal(nbpf, g["num_bands_per_freq"])
+
+
+def test_band_map_mono_and_invariants():
+    import oracle
+
+    fi, nfpb, nbpf = oracle.band_map(44100, 2048, 60, False)
+    assert len(fi) == 1979
+    assert fi[0] == 0 and fi[-1] == 1024  # DC forced into band 0, Nyquist into the last band
+    assert np.all(np.bincount(fi, minlength=1025) == nbpf)
+
+
+def test_stft_istft_match_torch_fixture():
+    import oracle
+
+    g = np.load(os.path.join(G, "stft.npz"))
+    S = oracle.stft(g["x"])
+    assert S.shape == g["spec"].shape
+    assert np.abs(S - g["spec"]).max() <= 1e-5 * np.abs(g["spec"]).max()
+    y = oracle.istft(g["spec"])
+    assert y.shape == g["y"].shape
+    assert np.abs(y - g["y"]).max() <= 1e-5
+
+
+def test_chunk_plans_match_fixture():
+    import oracle
+
+    with open(os.path.join(G, "chunk_plans.json")) as f:
+        cases = json.load(f)
+    for c in cases:
+        starts, step, border, total = oracle.chunk_plan(c["N"], c["chunk"], c["overlap"], c["default"])
+        assert step == c["step"] and border == c["border"] and total == c["total"], c
+        assert starts.tolist() == c["starts"]
+
+
+def test_oracle_forward_runs_and_is_deterministic(make_csm):
+    import oracle
+
+    path = make_csm("tiny", seed=0)
+    m = oracle.Model(path)
+    x = np.random.default_rng(0).uniform(-0.5, 0.5, (1, 2, 44100)).astype(np.float32)
+    a = m.forward(x)
+    b = m.forward(x)
+    assert a.shape == (1, 1, 2, 44100)
+    assert np.array_equal(a, b) and np.isfinite(a).all()
+
+
+def test_oracle_identity_mask_reconstructs_input(make_csm):
+    """With the mask estimator forced to mask = 1 and zero_dc off, the forward is
+    STFT -> scatter-average -> iSTFT, which must return its input."""
+    import csm_tool
+    import oracle
+
+    path = identity_csm(make_csm, "tiny")
+    m = oracle.Model(path)
+    x = np.random.default_rng(1).uniform(-0.5, 0.5, (1, 2, 44100)).astype(np.float32)
+    y = m.forward(x)[:, 0]
+    assert np.abs(y - x).max() < 1e-5
+
+
+def identity_csm(make_csm, preset, **ov):
+    """Random-init checkpoint whose mask estimators output exactly 1 + 0i."""
+    import csm_tool
+
+    base = make_csm(preset, seed=21, zero_dc=False, **ov)
+    out = base.replace(".csm", "_identity.csm")
+    if not os.path.exists(out):
+        cfg, t = csm_tool.read_csm(base)
+        md = cfg["mask_estimator_depth"]
+        for s in range(cfg["num_stems"]):
+            for b in range(cfg["num_bands"]):
+                p = f"mask_estimators.{s}.to_freqs.{b}.0.{2 * md}"
+                w = t[p + ".weight"]
+                bd = w.shape[0] // 2
+                t[p + ".weight"] = np.zeros_like(w)
+                bias = np.zeros(2 * bd, np.float32)
+                bias[:bd:2] = 1.0    # real part of the value half
+                bias[bd:] = 30.0     # gate half: sigmoid(30) == 1 in fp32
+                t[p + ".bias"] = bias
+        csm_tool.write_csm(out, cfg, t)
+    return out
