@@ -1,12 +1,365 @@
-// gemm_tc.cu — tcgen05 grouped GEMM (placeholder until the tensor-core kernel lands).
+// gemm_tc.cu — persistent, warp-specialised tcgen05 grouped GEMM (sm_100a).
+//
+// Warp roles (192 threads): warp 0 lane 0 issues the TMA loads, warp 1 lane 0
+// issues tcgen05.mma (and owns the TMEM allocation), warps 2-5 run the
+// epilogue.  Operand tiles are 128 x 64 (A) and BN x 64 (B) 16-bit elements
+// with the 128-byte swizzle, so every MMA descriptor addresses a canonical
+// K-major layout.  The accumulator is double buffered in TMEM so the epilogue
+// of tile i overlaps the MMAs of tile i+1.  Every wait is bounded: on timeout
+// the kernel records an error word and unwinds instead of hanging.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 #include "gemm_tc.h"
+#include "sm100.cuh"
 
 namespace mbr {
 namespace tc {
 
-bool gemm_supported(int) { return false; }
-void gemm(const GemmPlanTC&, int, cudaStream_t) { throw Error(ERR_UNSUPPORTED, "tcgen05 GEMM not built"); }
+using namespace sm100;
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+
+template <int BN>
+struct TileCfg {
+    static constexpr int STAGES = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <typename T>
+struct IsBf16 {
+    static constexpr bool value = false;
+};
+template <>
+struct IsBf16<__nv_bfloat16> {
+    static constexpr bool value = true;
+};
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Applies the epilogue to 32 accumulator columns [n0, n0+32) of one row.
+template <typename T, int EPI>
+__device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row, int n0, const uint32_t (&r)[32]) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    const int nvalid = min(32, g.N - n0);
+    if (g.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < nvalid) v[j] += __ldg(g.bias + n0 + j);
+    }
+    if constexpr (EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32) {
+        float* c = (float*)g.C + (int64_t)row * g.ldc + n0;
+        if (nvalid == 32 && ((uintptr_t)c & 15) == 0) {
+            float4* c4 = reinterpret_cast<float4*>(c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                if constexpr (EPI == ops::EPI_ADD_F32) {
+                    float4 p = c4[j];
+                    o.x += p.x, o.y += p.y, o.z += p.z, o.w += p.w;
+                }
+                c4[j] = o;
+            }
+        } else {
+            for (int j = 0; j < nvalid; ++j) c[j] = EPI == ops::EPI_ADD_F32 ? c[j] + v[j] : v[j];
+        }
+    } else if constexpr (EPI == ops::EPI_GLU_F32) {
+        float o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = v[2 * i] / (1.0f + __expf(-v[2 * i + 1]));
+        float* c = (float*)g.C + (int64_t)row * g.ldc + n0 / 2;
+        const int ovalid = nvalid / 2;
+        if (ovalid == 16 && ((uintptr_t)c & 15) == 0) {
+            float4* c4 = reinterpret_cast<float4*>(c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) c4[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        } else {
+            for (int i = 0; i < ovalid; ++i) c[i] = o[i];
+        }
+    } else {
+        if constexpr (EPI == ops::EPI_GELU_T) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        } else if constexpr (EPI == ops::EPI_TANH_T) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+        }
+        T* c = (T*)g.C + (int64_t)row * g.ldc + n0;
+        if (nvalid == 32 && ((uintptr_t)c & 15) == 0) {
+            uint4* c4 = reinterpret_cast<uint4*>(c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                c4[j] = make_uint4(pack2(v[8 * j], v[8 * j + 1], (T*)nullptr), pack2(v[8 * j + 2], v[8 * j + 3], (T*)nullptr),
+                                   pack2(v[8 * j + 4], v[8 * j + 5], (T*)nullptr),
+                                   pack2(v[8 * j + 6], v[8 * j + 7], (T*)nullptr));
+        } else {
+            for (int j = 0; j < nvalid; ++j) c[j] = from_f32<T>(v[j]);
+        }
+    }
+}
+
+template <typename T, int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const ops::GemmGroup* __restrict__ groups, const int4* __restrict__ tiles, int ntiles, int* err) {
+    using Cfg = TileCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + Cfg::STAGES * Cfg::A_BYTES;
+    uint64_t* full = (uint64_t*)(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + Cfg::STAGES;
+    uint64_t* acc_full = empty + Cfg::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tensormap(&tmA);
+            prefetch_tensormap(&tmB);
+            uint32_t it = 0;
+            bool alive = true;
+            for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
+                const int4 tl = tiles[t];
+                const ops::GemmGroup& g = groups[tl.x];
+                for (int kb = 0; kb < tl.w; ++kb, ++it) {
+                    const int s = it % Cfg::STAGES;
+                    const uint32_t r = it / Cfg::STAGES;
+                    if (!mbar_wait(&empty[s], (r & 1) ^ 1, err)) {
+                        alive = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    const int kx = g.k_col0 + kb * BK;
+                    tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kx, g.a_row0 + tl.y, &full[s]);
+                    tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kx, g.b_row0 + tl.z, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(BM, BN, IsBf16<T>::value);
+            uint32_t it = 0;
+            int tcount = 0;
+            bool alive = true;
+            for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, ++tcount) {
+                const int4 tl = tiles[t];
+                const int K = groups[tl.x].K;
+                const int buf = tcount & 1;
+                const uint32_t use = tcount >> 1;
+                if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * BN;
+                for (int kb = 0; kb < tl.w; ++kb, ++it) {
+                    const int s = it % Cfg::STAGES;
+                    const uint32_t r = it / Cfg::STAGES;
+                    if (!mbar_wait(&full[s], r & 1, err)) {
+                        alive = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
+                    const int ksteps = min(BK / 16, (K - kb * BK) / 16);
+                    for (int k = 0; k < ksteps; ++k)
+                        mma_f16(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, (kb | k) != 0);
+                    mma_commit(&empty[s]);
+                }
+                if (!alive) break;
+                mma_commit(&acc_full[buf]);
+            }
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int tcount = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tcount) {
+            const int4 tl = tiles[t];
+            const ops::GemmGroup g = groups[tl.x];
+            const int buf = tcount & 1;
+            const uint32_t use = tcount >> 1;
+            if (!mbar_wait(&acc_full[buf], use & 1, err)) break;
+            tc_fence_after();
+            const int row = tl.y + q * 32 + lane;
+            const bool rv = row < g.M;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                const int n0 = tl.z + c * 32;
+                if (n0 >= g.N) break;
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, r);
+                tmem_ld_wait();
+                if (rv) epilogue_chunk<T, EPI>(g, row, n0, r);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+// ---- host: tensor maps ----
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    if (!fn) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+void make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_rows, int dtype) {
+    MBR_CHECK(((uintptr_t)base & 15) == 0, "TMA base must be 16-byte aligned");
+    MBR_CHECK((cols * 2) % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(m, dtype == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+int num_sms() {
+    int dev = 0, n = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    MBR_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    return n;
+}
+
+template <typename T, int BN, int EPI>
+void launch_one(const GemmLaunch& L, int* d_err, cudaStream_t st) {
+    auto kern = gemm_tc_kernel<T, BN, EPI>;
+    static bool attr[64] = {};  // per instantiation and device
+    static int sms[64] = {};
+    int dev = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    MBR_CHECK(dev >= 0 && dev < 64, "device index out of range");
+    if (!attr[dev]) {
+        MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg<BN>::SMEM));
+        sms[dev] = num_sms();
+        attr[dev] = true;
+    }
+    int grid = std::min(L.ntiles, sms[dev]);
+    kern<<<grid, 192, TileCfg<BN>::SMEM, st>>>(L.tmA, L.tmB, L.groups, L.tiles, L.ntiles, d_err);
+    MBR_CUDA(cudaGetLastError());
+}
+
+template <typename T, int BN>
+void launch_bn(const GemmLaunch& L, int* d_err, cudaStream_t st) {
+    switch (L.epi) {
+        case ops::EPI_F32: launch_one<T, BN, ops::EPI_F32>(L, d_err, st); break;
+        case ops::EPI_T: launch_one<T, BN, ops::EPI_T>(L, d_err, st); break;
+        case ops::EPI_ADD_F32: launch_one<T, BN, ops::EPI_ADD_F32>(L, d_err, st); break;
+        case ops::EPI_GELU_T: launch_one<T, BN, ops::EPI_GELU_T>(L, d_err, st); break;
+        case ops::EPI_TANH_T: launch_one<T, BN, ops::EPI_TANH_T>(L, d_err, st); break;
+        case ops::EPI_GLU_F32: launch_one<T, BN, ops::EPI_GLU_F32>(L, d_err, st); break;
+        default: throw Error(ERR_INVALID, "tc gemm: bad epilogue");
+    }
+}
+
+template <typename T>
+void launch_t(const GemmLaunch& L, int* d_err, cudaStream_t st) {
+    if (L.bn == 256) launch_bn<T, 256>(L, d_err, st);
+    else if (L.bn == 192) launch_bn<T, 192>(L, d_err, st);
+    else launch_bn<T, 128>(L, d_err, st);
+}
+
+}  // namespace
+
+bool gemm_supported(int epi) { return epi >= ops::EPI_F32 && epi <= ops::EPI_GLU_F32; }
+
+void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, GemmLaunch& L, size_t& L_first) {
+    MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "tc gemm needs fp16 or bf16 operands");
+    int bn;
+    if (p.epi == ops::EPI_GLU_F32) bn = 128;
+    else if (p.maxN % 256 == 0) bn = 256;
+    else if (p.maxN % 192 == 0) bn = 192;
+    else if (p.maxN % 128 == 0 || p.maxN < 256) bn = 128;
+    else bn = 256;
+    L.bn = bn;
+    L.epi = p.epi;
+    make_map(&L.tmA, p.a_base, p.a_rows, p.a_cols, BM, dtype);
+    make_map(&L.tmB, p.b_base, p.b_rows, p.b_cols, bn, dtype);
+    L_first = tiles.size();
+    for (int gi = 0; gi < p.ngroups; ++gi) {
+        const ops::GemmGroup& g = p.h_groups[gi];
+        MBR_CHECK(g.K % 16 == 0 && g.K > 0, "tc gemm: K must be a positive multiple of 16");
+        MBR_CHECK((int64_t)g.a_row0 + g.M <= p.a_rows && (int64_t)g.b_row0 + g.N <= p.b_rows &&
+                      (int64_t)g.k_col0 + g.K <= p.a_cols && (int64_t)g.k_col0 + g.K <= p.b_cols,
+                  "tc gemm: group outside its operand tensors");
+        MBR_CHECK(g.k_col0 % 8 == 0, "tc gemm: K offset must be 16-byte aligned");
+        int kb = (int)ceil_div(g.K, BK);
+        for (int m0 = 0; m0 < g.M; m0 += BM)
+            for (int n0 = 0; n0 < g.N; n0 += bn) tiles.push_back(make_int4(gi, m0, n0, kb));
+    }
+    L.ntiles = (int)(tiles.size() - L_first);
+    L.groups = p.groups;
+    L.ok = true;
+}
+
+void gemm_launch(const GemmLaunch& L, int dtype, int* d_err, cudaStream_t st) {
+    MBR_CHECK(L.ok, "tc gemm launch not prepared");
+    if (L.ntiles == 0) return;
+    if (dtype == DT_BF16) launch_t<__nv_bfloat16>(L, d_err, st);
+    else launch_t<__half>(L, d_err, st);
+}
 
 }  // namespace tc
 }  // namespace mbr

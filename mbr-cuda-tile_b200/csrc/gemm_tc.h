@@ -1,8 +1,19 @@
 // gemm_tc.h — tcgen05 (5th-gen tensor core) grouped GEMM for sm_100a.
+//
+// C_g = epi(A_g * B_g^T + bias_g) for a list of groups whose A (and B) operands
+// are row blocks of one K-major 2-D tensor each.  A persistent kernel walks a
+// host-built tile list; TMA streams 128 x 64 A tiles and BN x 64 B tiles
+// (128-byte swizzle) through a shared-memory ring, one thread issues
+// tcgen05.mma into a double-buffered TMEM accumulator, and four epilogue warps
+// drain TMEM (tcgen05.ld) through the fused epilogue while the next tile's
+// MMAs run.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <vector>
 
 #include "ops.h"
 
@@ -22,8 +33,22 @@ struct GemmPlanTC {
     int64_t b_rows = 0, b_cols = 0;
 };
 
+// Prepared launch: tensor maps and the tile list (built once per workspace).
+struct GemmLaunch {
+    CUtensorMap tmA, tmB;
+    const int4* tiles = nullptr;  // device: (group, m0, n0, k-blocks)
+    int ntiles = 0;
+    int bn = 128;
+    int epi = 0;
+    const ops::GemmGroup* groups = nullptr;
+    bool ok = false;
+};
+
 bool gemm_supported(int epi);
-void gemm(const GemmPlanTC& p, int dtype, cudaStream_t st);
+// Appends the plan's tiles to `tiles` (host) and fills `L` except L.tiles,
+// which the caller points at the uploaded copy (offset `L_first`).
+void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, GemmLaunch& L, size_t& L_first);
+void gemm_launch(const GemmLaunch& L, int dtype, int* d_err, cudaStream_t st);
 
 }  // namespace tc
 }  // namespace mbr

@@ -288,6 +288,8 @@ MelBandRoformer::MelBandRoformer(const ModelWeights& w, int device, int dtype) :
 
     MBR_CUDA(cudaMalloc(&wbase_, pk.buf.size()));
     MBR_CUDA(cudaMemcpy(wbase_, pk.buf.data(), pk.buf.size(), cudaMemcpyHostToDevice));
+    MBR_CUDA(cudaMalloc(&d_err_, 256));
+    MBR_CUDA(cudaMemset(d_err_, 0, 256));
     uint8_t* base = (uint8_t*)wbase_;
     d_fi_ = (int*)(base + o_fi);
     d_band_jofs_ = (int*)(base + o_jofs);
@@ -333,8 +335,23 @@ MelBandRoformer::MelBandRoformer(const ModelWeights& w, int device, int dtype) :
 
 MelBandRoformer::~MelBandRoformer() {
     cudaSetDevice(device_);
-    for (auto& kv : ws_) cudaFree(kv.second->base);
+    for (auto& kv : ws_) {
+        cudaFree(kv.second->base);
+        if (kv.second->d_tiles) cudaFree(kv.second->d_tiles);
+    }
+    cudaFree(d_err_);
     cudaFree(wbase_);
+}
+
+void MelBandRoformer::check_device_error() {
+    int e = 0;
+    MBR_CUDA(cudaSetDevice(device_));
+    MBR_CUDA(cudaMemcpy(&e, d_err_, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e != 0) {
+        MBR_CUDA(cudaMemset(d_err_, 0, sizeof(int)));
+        throw Error(ERR_TIMEOUT, "a tensor-core kernel timed out waiting on a pipeline barrier (error " +
+                                     std::to_string(e) + ")");
+    }
 }
 
 int64_t MelBandRoformer::frames(int64_t L) const {
@@ -411,6 +428,39 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
     build_plans(*ws);
     MBR_CUDA(cudaMemcpy(ws->d_groups, ws->h_groups.data(), ws->h_groups.size() * sizeof(ops::GemmGroup),
                         cudaMemcpyHostToDevice));
+    if (dtype_ != DT_F32) {
+        // tensor-core launches: tensor maps + tile lists of every GEMM plan
+        std::vector<int4> tiles;
+        std::vector<size_t> firsts;
+        std::vector<Plan*> plans{&ws->band_split};
+        for (auto& p : ws->layer_plans) plans.push_back(&p);
+        for (auto& v : ws->mask_plans)
+            for (auto& p : v) plans.push_back(&p);
+        for (Plan* p : plans) {
+            tc::GemmPlanTC tp;
+            tp.groups = ws->d_groups + p->first;
+            tp.h_groups = ws->h_groups.data() + p->first;
+            tp.ngroups = p->n;
+            tp.maxM = p->maxM;
+            tp.maxN = p->maxN;
+            tp.epi = p->epi;
+            tp.a_base = p->a_base;
+            tp.a_rows = p->a_rows;
+            tp.a_cols = p->a_cols;
+            tp.b_base = p->b_base;
+            tp.b_rows = p->b_rows;
+            tp.b_cols = p->b_cols;
+            tc::GemmLaunch L;
+            size_t first = 0;
+            tc::gemm_prepare(tp, dtype_, tiles, L, first);
+            p->launch = (int)ws->launches.size();
+            ws->launches.push_back(L);
+            firsts.push_back(first);
+        }
+        MBR_CUDA(cudaMalloc(&ws->d_tiles, sizeof(int4) * std::max<size_t>(1, tiles.size())));
+        MBR_CUDA(cudaMemcpy(ws->d_tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice));
+        for (size_t i = 0; i < ws->launches.size(); ++i) ws->launches[i].tiles = ws->d_tiles + firsts[i];
+    }
     Workspace& ref = *ws;
     ws_[key] = std::move(ws);
     return ref;
@@ -525,21 +575,8 @@ void MelBandRoformer::build_plans(Workspace& ws) {
 }
 
 void MelBandRoformer::run_gemm(const Workspace& ws, const Plan& p, cudaStream_t st) {
-    if (gemm_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::gemm_supported(p.epi)) {
-        tc::GemmPlanTC tp;
-        tp.groups = ws.d_groups + p.first;
-        tp.h_groups = ws.h_groups.data() + p.first;
-        tp.ngroups = p.n;
-        tp.maxM = p.maxM;
-        tp.maxN = p.maxN;
-        tp.epi = p.epi;
-        tp.a_base = p.a_base;
-        tp.a_rows = p.a_rows;
-        tp.a_cols = p.a_cols;
-        tp.b_base = p.b_base;
-        tp.b_rows = p.b_rows;
-        tp.b_cols = p.b_cols;
-        tc::gemm(tp, dtype_, st);
+    if (gemm_backend_ == BACKEND_TC && dtype_ != DT_F32 && p.launch >= 0) {
+        tc::gemm_launch(ws.launches[p.launch], dtype_, d_err_, st);
     } else {
         ops::gemm_simt(ws.d_groups + p.first, p.n, p.maxM, p.maxN, dtype_, p.epi, st);
     }

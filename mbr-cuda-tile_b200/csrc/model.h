@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "common.h"
+#include "gemm_tc.h"
 #include "ops.h"
 #include "weights.h"
 
@@ -86,11 +87,15 @@ public:
     int attn_backend() const { return attn_backend_; }
     // Kernel launches issued by the last forward().
     int64_t last_launches() const { return launches_; }
+    // Reads (synchronously) and clears the device error word the tensor-core
+    // kernels set when a bounded wait gives up; throws ERR_TIMEOUT if set.
+    void check_device_error();
 
 private:
     struct Plan {
         size_t first = 0;  // index into the workspace's group array
         int n = 0, maxM = 0, maxN = 0, maxK = 0, epi = 0;
+        int launch = -1;  // index into Workspace::launches (tensor-core path)
         // operand tensor shapes for the tensor-core path (rows x cols, elements)
         const void* a_base = nullptr;
         int64_t a_rows = 0, a_cols = 0;
@@ -138,6 +143,8 @@ private:
         float *rope_t_cos, *rope_t_sin, *rope_f_cos, *rope_f_sin;
         ops::GemmGroup* d_groups;
         std::vector<ops::GemmGroup> h_groups;
+        std::vector<tc::GemmLaunch> launches;
+        int4* d_tiles = nullptr;
         Plan band_split;
         std::vector<Plan> layer_plans;  // [depth][2][layers][4]: qkv, out, ffn1, ffn2
         std::vector<std::vector<Plan>> mask_plans;  // [stem][linear]
@@ -160,6 +167,7 @@ private:
 
     std::vector<int> band_bd_, band_boff_, band_kofs_;  // host copies
     void* wbase_ = nullptr;  // single device allocation holding every weight
+    int* d_err_ = nullptr;   // error word of the tensor-core kernels
     int *d_fi_, *d_band_jofs_, *d_band_kofs_, *d_rev_off_, *d_rev_idx_;
     float *d_nbpf_, *d_window_, *d_bs_gamma_, *d_bs_bias_;
     float2* d_twiddle_;
