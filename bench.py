@@ -1,0 +1,449 @@
+#!/usr/bin/env python
+"""bench.py — audio-seconds/sec of MelBandRoformer separation on B200.
+
+Workload (N=1): the "Standard" configuration — random-init MelBandRoformer
+dim 384, depth 6, 8 heads x 64, FFN x4, 60 mel bands, mask-estimator depth 2,
+1 stem, fp16 — separating a 30 s stereo 44.1 kHz seeded pink-noise track
+(1/f, -18 dBFS RMS, 16-bit quantised) in 8 s chunks with overlap 4,
+chunk-batch 1.  One step = one separation of the whole track.  With
+--gpus N (one process per GPU under torchrun) every rank adds 30 s of track
+(weak scaling): the N*30 s track's chunk list is split into contiguous ranges,
+one per rank, and only the overlap-add boundary moves between neighbours
+(NCCL send/recv).
+
+Prints one JSON line (rank 0).  `value` times device-resident input; `e2e`
+times the host entry point (mbr_separate: pinned host track in, stems out).
+`--impl reference` times the reference path's CPU restatement (the reference
+has no CPU implementation of its own) on a bounded excerpt per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mbr-cuda-tile_b200")
+sys.path.insert(0, PKG)
+
+SR = 44100
+WORKLOADS = {
+    "std": dict(preset="std", dtype="fp16", seconds=30.0, overlap=4.0, chunk_batch=1,
+                desc="std: dim 384, depth 6, 8x64 heads, 1 stem; 30 s stereo track, 8 s chunks, overlap 4, "
+                     "chunk-batch 1"),
+    "two_stem": dict(preset="two_stem", dtype="bf16", seconds=180.0, overlap=4.0, chunk_batch=4,
+                     desc="two_stem: dim 384, depth 12, 8x64 heads, 2 stems; 3 min track, 8 s chunks, overlap 4, "
+                          "chunk-batch 4"),
+    "large": dict(preset="large", dtype="fp16", seconds=600.0, overlap=2.0, chunk_batch=8,
+                  desc="large: dim 512, depth 12, 16x64 heads, 2 stems; 10 min track, 11 s chunks, overlap 2, "
+                       "chunk-batch 8"),
+}
+
+
+def pink_noise(seconds: float, seed: int, channels: int = 2) -> np.ndarray:
+    """Seeded 1/f noise, RMS -18 dBFS, quantised to 16-bit levels (k / 32768)."""
+    n = int(round(seconds * SR))
+    rng = np.random.default_rng(seed)
+    out = np.empty((channels, n), np.float32)
+    for c in range(channels):
+        w = rng.standard_normal(n)
+        X = np.fft.rfft(w)
+        f = np.arange(X.shape[0], dtype=np.float64)
+        f[0] = 1.0
+        X /= np.sqrt(f)
+        x = np.fft.irfft(X, n)
+        x *= (10 ** (-18 / 20)) / np.sqrt(np.mean(x ** 2))
+        out[c] = np.clip(np.round(x * 32768.0), -32768, 32767) / 32768.0
+    return out
+
+
+def model_flops(cfg: dict, T: int, B: int, bd: list) -> dict:
+    """Algorithmic FLOPs of one forward over B chunks of T frames, per kernel class."""
+    D, H, dh = cfg["dim"], cfg["heads"], cfg["dim_head"]
+    DI, hid, NB = H * dh, cfg["dim"] * cfg["mlp_expansion_factor"], cfg["num_bands"]
+    MT = B * T
+    M = MT * NB
+    L = cfg["depth"] * (cfg["time_transformer_depth"] + cfg["freq_transformer_depth"])
+    Lt = cfg["depth"] * cfg["time_transformer_depth"]
+    Lf = cfg["depth"] * cfg["freq_transformer_depth"]
+    S, md = cfg["num_stems"], cfg["mask_estimator_depth"]
+    f = {
+        "gemm_bandsplit": 2.0 * MT * D * sum(bd),
+        "gemm_qkv": L * 2.0 * M * D * 3 * DI,
+        "gemm_out": L * 2.0 * M * DI * D,
+        "gemm_ffn1": L * 2.0 * M * D * hid,
+        "gemm_ffn2": L * 2.0 * M * hid * D,
+        "attn_time": Lt * 4.0 * T * T * dh * H * B * NB,
+        "attn_freq": Lf * 4.0 * NB * NB * dh * H * MT,
+        "gemm_mask_hidden": S * 2.0 * MT * NB * (D * hid + (md - 1) * hid * hid),
+        "gemm_mask_out": S * 2.0 * MT * hid * 2 * sum(bd),
+    }
+    return f
+
+
+def band_dims(cfg: dict) -> list:
+    import csm_tool
+
+    _, nfpb, _ = csm_tool.mel_band_map(cfg["sample_rate"], cfg["stft_n_fft"], cfg["num_bands"], cfg["stereo"])
+    C = 2 if cfg["stereo"] else 1
+    return [int(2 * n * C) for n in nfpb]
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm_gbs=d["hbm_gbs"], tflops=d["bf16_tflops"], tflops_sustained=d["bf16_tflops_sustained"],
+                    source="measured")
+    return dict(hbm_gbs=6650.0, tflops=1590.0, tflops_sustained=1400.0, source="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            p = [x.strip() for x in l.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(csm: str, cfg: dict, step_flops: float, seconds_audio: float, excerpt_s: float, reps: int = 1):
+    """Times the CPU oracle (all host threads) on a `excerpt_s` forward of the same
+    model and scales by algorithmic FLOPs to the benchmark step."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    m = oracle.Model(csm, 1 if cfg.get("_dtype") == "fp16" else 3 if cfg.get("_dtype") == "bf16" else 0)
+    L = int(excerpt_s * SR)
+    x = pink_noise(excerpt_s, 7)[None]
+    T = L // cfg["stft_hop_length"] + 1
+    fl = sum(model_flops(cfg, T, 1, band_dims(cfg)).values())
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        m.forward(x)
+        ts.append(time.perf_counter() - t0)
+    t = float(np.median(ts))
+    step_s = t * step_flops / fl
+    return dict(value=seconds_audio / step_s, unit="audio-s/s", cores=oracle.threads(), kind="port",
+                sample=f"CPU oracle forward of a {excerpt_s:g} s stereo excerpt ({T} frames, {fl / 1e12:.3f} TFLOP) "
+                       f"in {t:.2f} s, scaled by algorithmic FLOPs to the {step_flops / 1e12:.2f} TFLOP step",
+                sample_seconds=t)
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_reference(args, wl):
+    """The reference arm: the CPU restatement of the reference path, all host threads."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import csm_tool
+
+    cfg = csm_tool.base_config(**csm_tool.PRESETS[wl["preset"]])
+    cfg["_dtype"] = wl["dtype"]
+    with tempfile.TemporaryDirectory() as d:
+        csm = os.path.join(d, "model.csm")
+        csm_tool.write_csm(csm, {k: v for k, v in cfg.items() if not k.startswith("_")},
+                           csm_tool.random_weights({k: v for k, v in cfg.items() if not k.startswith("_")}, 0))
+        seconds = wl["seconds"] * args.gpus
+        T = cfg["chunk_size"] // cfg["stft_hop_length"] + 1
+        step_flops = step_model_flops(cfg, seconds, wl)
+        vals = []
+        for i in range(args.warmup + args.steps):
+            r = cpu_sample(csm, cfg, step_flops, seconds, args.cpu_excerpt)
+            if i >= args.warmup:
+                vals.append(r)
+        v = float(np.mean([r["value"] for r in vals]))
+        ms = float(np.mean([r["sample_seconds"] for r in vals])) * 1e3
+        base = vals[-1]
+        line = {
+            "impl": "reference", "metric": "audio-seconds/sec", "value": v, "unit": "audio-s/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp64 reductions)",
+            "data": "synthetic: seeded pink noise, random-init weights", "config": {"workload": wl["desc"]},
+            "cpu_baseline": {"value": v, "unit": "audio-s/s", "cores": base["cores"], "kind": "port",
+                             "sample": base["sample"]},
+            "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference has no CPU implementation of this path; this arm times the CPU restatement "
+                    "(oracle/) of the reference's forward with all host threads",
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def step_model_flops(cfg, seconds, wl):
+    """Algorithmic FLOPs of one whole-track separation (all chunks)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    N = int(round(seconds * SR))
+    starts, step, border, total = oracle.chunk_plan(N, cfg["chunk_size"], -1.0 if wl["overlap"] <= 0 else wl["overlap"],
+                                                    cfg["num_overlap"])
+    T = cfg["chunk_size"] // cfg["stft_hop_length"] + 1
+    per_chunk = sum(model_flops(cfg, T, 1, band_dims(cfg)).values())
+    return per_chunk * len(starts)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mbr_b200", choices=["mbr_b200", "reference"])
+    ap.add_argument("--workload", default="std", choices=sorted(WORKLOADS))
+    ap.add_argument("--cpu-excerpt", type=float, default=1.0, help="seconds of audio in the CPU sample")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, wl)
+
+    import torch
+
+    import csm_tool
+    import cudasep
+
+    world, rank, local = dist_env()
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    cfg = csm_tool.base_config(**csm_tool.PRESETS[wl["preset"]])
+    tmpdir = tempfile.mkdtemp(prefix="mbr_bench_")
+    csm = os.path.join(tmpdir, "model.csm")
+    csm_tool.write_csm(csm, cfg, csm_tool.random_weights(cfg, 0))
+    m = cudasep.Model(csm, local, wl["dtype"])
+    S, C = m.info("num_stems"), m.info("channels")
+    seconds = wl["seconds"] * world
+    track = pink_noise(seconds, 1234)
+    N = track.shape[1]
+    stream = torch.cuda.current_stream(dev)
+    d_track = torch.from_numpy(track).to(dev)
+    d_out = torch.empty((S, C, N), dtype=torch.float32, device=dev)
+
+    if world == 1:
+        def step():
+            m.separate_device(d_track, wl["overlap"], wl["chunk_batch"], out=d_out, stream=stream)
+    else:
+        info = m.shard_info(N, wl["overlap"], rank, world)
+        span = info["hi"] - info["lo"]
+        acc = torch.empty((S * C, span), dtype=torch.float32, device=dev)
+        wsum = torch.empty((span,), dtype=torch.float32, device=dev)
+        prev = m.shard_info(N, wl["overlap"], rank - 1, world) if rank > 0 else None
+        rlen = prev["hi"] - prev["send_lo"] if prev else 0
+        racc = torch.empty((S * C, max(rlen, 1)), dtype=torch.float32, device=dev)
+        rws = torch.empty((max(rlen, 1),), dtype=torch.float32, device=dev)
+        soff = info["send_lo"] - info["lo"]
+
+        def step():
+            m.shard_run(d_track, N, wl["overlap"], wl["chunk_batch"], rank, world, acc, wsum, stream=stream)
+            if rank > 0:
+                dist.recv(racc, rank - 1)
+                dist.recv(rws, rank - 1)
+                m.shard_add_boundary(N, wl["overlap"], rank, world, acc, wsum, racc, rws, rlen, stream=stream)
+            if rank < world - 1:
+                dist.send(acc[:, soff:].contiguous(), rank + 1)
+                dist.send(wsum[soff:].contiguous(), rank + 1)
+            m.shard_finalize(N, wl["overlap"], rank, world, acc, wsum, d_out.view(S * C, N), N, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    m.sync_check()
+    launches = m.last_launches()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    m.sync_check()
+    value = seconds / (ms / 1e3)
+
+    # ---- end to end through the host entry point (pinned host buffers) ----
+    h_in = torch.from_numpy(track).pin_memory()
+    h_out = torch.empty((S, C, N), dtype=torch.float32).pin_memory()
+    h_in_np, h_out_np = h_in.numpy(), h_out.numpy()
+    if world == 1:
+        m.separate(h_in_np, wl["overlap"], wl["chunk_batch"], out=h_out_np)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            m.separate(h_in_np, wl["overlap"], wl["chunk_batch"], out=h_out_np)
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        h2d, d2h = C * N * 4, S * C * N * 4
+    else:
+        def e2e_step():
+            d_track.copy_(h_in, non_blocking=True)
+            step()
+            lo, hi = info["out_lo"], info["out_hi"]
+            h_out.view(S * C, N)[:, lo:hi].copy_(d_out.view(S * C, N)[:, lo:hi], non_blocking=False)
+        e2e_step()
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        h2d, d2h = C * N * 4, S * C * (info["out_hi"] - info["out_lo"]) * 4
+    e2e = {"value": seconds / (e2e_ms / 1e3), "unit": "audio-s/s", "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
+           "path": "mbr_separate (host track in, stems out)" if world == 1 else
+                   "H2D track + mbr_shard_* + NCCL boundary + D2H of the own range, per rank"}
+
+    # ---- roofline of the dominant kernel class (one profiled step) ----
+    peaks = load_peaks()
+    m.profile(True)
+    step()
+    torch.cuda.synchronize(dev)
+    prof = m.profile_read()
+    m.profile(False)
+    T = cfg["chunk_size"] // cfg["stft_hop_length"] + 1
+    flops_fwd = model_flops(cfg, T, wl["chunk_batch"], band_dims(cfg))
+    nchunks_rank = info["c1"] - info["c0"] if world > 1 else None
+    kind = max(prof, key=lambda k: prof[k][0])
+    kms, kn = prof[kind]
+    roof = None
+    traffic = read_traffic(kind)
+    if kind in flops_fwd and kn > 0:
+        # launches of this class per forward
+        per_fwd = {"gemm_bandsplit": 1, "gemm_mask_out": cfg["num_stems"],
+                   "gemm_mask_hidden": cfg["num_stems"] * cfg["mask_estimator_depth"],
+                   "attn_time": cfg["depth"] * cfg["time_transformer_depth"],
+                   "attn_freq": cfg["depth"] * cfg["freq_transformer_depth"]}.get(
+            kind, cfg["depth"] * (cfg["time_transformer_depth"] + cfg["freq_transformer_depth"]))
+        per_launch = flops_fwd[kind] / per_fwd
+        achieved = per_launch / (kms / kn / 1e3) / 1e12
+        roof = {"kernel": kind, "bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
+                "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"], "traffic": traffic,
+                "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside a long step)",
+                "avg_launch_ms": kms / kn, "launches_profiled": kn,
+                "algorithmic_flop_per_launch": per_launch}
+    breakdown = {k: {"ms": round(v[0], 3), "launches": v[1]} for k, v in prof.items() if v[1] > 0}
+
+    line = {
+        "metric": "audio-seconds/sec", "value": value, "unit": "audio-s/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16" if wl["dtype"] == "fp16" else wl["dtype"].replace("fp", "f"),
+        "data": "synthetic: seeded pink noise (1/f, -18 dBFS RMS, 16-bit levels), random-init weights "
+                "N(0,0.02), gamma=1",
+        "config": {"workload": wl["desc"] + (f"; {world} ranks x {wl['seconds']:g} s (weak scaling)" if world > 1 else ""),
+                   "track_seconds": seconds, "parallelism": f"chunk-range shards x{world}",
+                   "l2": "no flush: the per-step working set (activations ~1 GB, mask-estimator weights "
+                         "~400 MB) exceeds the 126 MB L2"},
+        "roofline": roof, "profile_ms_per_step": breakdown, "e2e": e2e, "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu:
+        cfg["_dtype"] = wl["dtype"]
+        line["cpu_baseline"] = cpu_sample(csm, cfg, step_model_flops(cfg, seconds, wl), seconds, args.cpu_excerpt)
+        line["cpu_baseline"].pop("sample_seconds", None)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    try:
+        os.remove(csm)
+        os.rmdir(tmpdir)
+    except OSError:
+        pass
+    return 0
+
+
+def read_traffic(kind: str):
+    """DRAM bytes per launch of `kind` from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == kind and not line.startswith("#"):
+                try:
+                    return float(parts[1])
+                except ValueError:
+                    return None
+    return None
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -145,6 +145,21 @@ MBR_API int mbr_set_backend(mbr_handle* h, int gemm, int attention);
 /* Kernel launches issued by the last forward / separation on this handle. */
 MBR_API int mbr_last_launches(mbr_handle* h, int64_t* n);
 
+/* Waits for the handle's device and reports a kernel-side failure: the
+ * tensor-core kernels bound every pipeline wait and, instead of hanging, set an
+ * error word that this call turns into MBR_ERR_TIMEOUT.  No reference
+ * counterpart (the reference's kernels have no device-side waits). */
+MBR_API int mbr_sync_check(mbr_handle* h);
+
+/* Per-kernel-class profiler (CUDA events on the launching stream).
+ * Classes: 0 stft, 1 band gather+norm, 2 band-split GEMM, 3 rms norms,
+ * 4 QKV GEMM, 5 rope scatter, 6 time attention, 7 band attention,
+ * 8 out-proj GEMM, 9 FFN1 GEMM, 10 FFN2 GEMM, 11 mask hidden GEMMs,
+ * 12 mask output GEMM, 13 mask scatter, 14 iSTFT.  Replaces the out-of-band
+ * nsys summaries of the reference (bench/nsys_kernel_summary.sh). */
+MBR_API int mbr_profile_enable(mbr_handle* h, int on);
+MBR_API int mbr_profile_read(mbr_handle* h, int kind, double* ms, int64_t* count);
+
 #ifdef __cplusplus
 }
 #endif

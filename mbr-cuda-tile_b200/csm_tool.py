@@ -41,6 +41,8 @@ PRESETS = {
     "tiny": dict(dim=64, depth=1, heads=2, dim_head=64, num_stems=1, chunk_size=44100, num_overlap=2),
     "tiny2": dict(dim=128, depth=2, heads=2, dim_head=64, num_stems=2, chunk_size=88200, num_overlap=4,
                   time_transformer_depth=2),
+    # the std layer shapes (dim 384, 8x64) at depth 1 with 1 s chunks
+    "mid": dict(dim=384, depth=1, heads=8, dim_head=64, num_stems=1, chunk_size=44100, num_overlap=2),
 }
 
 

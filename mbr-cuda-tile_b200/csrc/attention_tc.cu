@@ -7,7 +7,7 @@ namespace tc {
 
 bool attention_supported(int) { return false; }
 void attention(const void*, const void*, const void*, int64_t, int, int, int, float, const float*, int, int, int,
-               void*, int, cudaStream_t) {
+               void*, int, int*, cudaStream_t) {
     throw Error(ERR_UNSUPPORTED, "tcgen05 attention not built");
 }
 

@@ -10,7 +10,7 @@ namespace tc {
 bool attention_supported(int dim_head);
 // q, k, v [nseq][H][L][dh] (fp16/bf16) -> merged[token][h*dh + d] = softmax(q k^T * scale) v * gate[token][h]
 void attention(const void* q, const void* k, const void* v, int64_t nseq, int H, int L, int dh, float scale,
-               const float* gates, int mode, int NB, int T, void* merged, int dtype, cudaStream_t st);
+               const float* gates, int mode, int NB, int T, void* merged, int dtype, int* d_err, cudaStream_t st);
 
 }  // namespace tc
 }  // namespace mbr

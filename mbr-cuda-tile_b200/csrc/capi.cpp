@@ -183,6 +183,7 @@ MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float o
             MBR_CUDA(cudaMemcpyAsync(h_out, dout, sizeof(float) * SC * N, cudaMemcpyDeviceToHost, h->stream));
             MBR_CUDA(cudaStreamSynchronize(h->stream));
             h->launches = h->sep->last_launches();
+            h->model->check_device_error();
             return;
         }
         // one handle per GPU (device, device+1, ...)
@@ -319,6 +320,29 @@ MBR_API int mbr_last_launches(mbr_handle* h, int64_t* n) {
     return guard([&] {
         need(h && n, "null argument");
         *n = h->launches;
+    });
+}
+
+MBR_API int mbr_sync_check(mbr_handle* h) {
+    return guard([&] {
+        need(h, "null argument");
+        MBR_CUDA(cudaSetDevice(h->device));
+        MBR_CUDA(cudaDeviceSynchronize());
+        h->model->check_device_error();
+    });
+}
+
+MBR_API int mbr_profile_enable(mbr_handle* h, int on) {
+    return guard([&] {
+        need(h, "null argument");
+        h->model->profile_enable(on != 0);
+    });
+}
+
+MBR_API int mbr_profile_read(mbr_handle* h, int kind, double* ms, int64_t* count) {
+    return guard([&] {
+        need(h && ms && count, "null argument");
+        h->model->profile_read(kind, ms, count);
     });
 }
 

@@ -574,13 +574,68 @@ void MelBandRoformer::build_plans(Workspace& ws) {
         }
 }
 
-void MelBandRoformer::run_gemm(const Workspace& ws, const Plan& p, cudaStream_t st) {
-    if (gemm_backend_ == BACKEND_TC && dtype_ != DT_F32 && p.launch >= 0) {
-        tc::gemm_launch(ws.launches[p.launch], dtype_, d_err_, st);
-    } else {
-        ops::gemm_simt(ws.d_groups + p.first, p.n, p.maxM, p.maxN, dtype_, p.epi, st);
+// ---- profiler ----
+void MelBandRoformer::profile_enable(bool on) {
+    prof_on_ = on;
+    profile_reset();
+}
+
+void MelBandRoformer::profile_reset() {
+    prof_recs_.clear();
+    prof_used_ = 0;
+    for (int i = 0; i < PK_COUNT; ++i) prof_ms_[i] = 0.0, prof_n_[i] = 0;
+}
+
+int MelBandRoformer::prof_begin(int kind, cudaStream_t st) {
+    while (prof_pool_.size() < prof_used_ + 2) {
+        cudaEvent_t e;
+        MBR_CUDA(cudaEventCreate(&e));
+        prof_pool_.push_back(e);
     }
-    ++launches_;
+    ProfRec r{kind, prof_pool_[prof_used_], prof_pool_[prof_used_ + 1]};
+    prof_used_ += 2;
+    MBR_CUDA(cudaEventRecord(r.a, st));
+    prof_recs_.push_back(r);
+    return (int)prof_recs_.size() - 1;
+}
+
+void MelBandRoformer::prof_end(int rec, cudaStream_t st) { MBR_CUDA(cudaEventRecord(prof_recs_[rec].b, st)); }
+
+void MelBandRoformer::prof_collect() {
+    for (auto& r : prof_recs_) {
+        MBR_CUDA(cudaEventSynchronize(r.b));
+        float ms = 0.f;
+        MBR_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+        prof_ms_[r.kind] += ms;
+        prof_n_[r.kind] += 1;
+    }
+    prof_recs_.clear();
+    prof_used_ = 0;
+}
+
+void MelBandRoformer::profile_read(int kind, double* ms, int64_t* count) {
+    MBR_CHECK(kind >= 0 && kind < PK_COUNT, "profile kind out of range");
+    MBR_CUDA(cudaSetDevice(device_));
+    prof_collect();
+    *ms = prof_ms_[kind];
+    *count = prof_n_[kind];
+}
+
+// Runs `fn` (one kernel launch) bracketed by profiler events when enabled.
+#define MBR_LAUNCH(kind, ...)                                    \
+    do {                                                         \
+        int rec_ = prof_on_ ? prof_begin((kind), st) : -1;       \
+        __VA_ARGS__;                                             \
+        if (rec_ >= 0) prof_end(rec_, st);                       \
+        ++launches_;                                             \
+    } while (0)
+
+void MelBandRoformer::run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st) {
+    if (gemm_backend_ == BACKEND_TC && dtype_ != DT_F32 && p.launch >= 0) {
+        MBR_LAUNCH(kind, tc::gemm_launch(ws.launches[p.launch], dtype_, d_err_, st));
+    } else {
+        MBR_LAUNCH(kind, ops::gemm_simt(ws.d_groups + p.first, p.n, p.maxM, p.maxN, dtype_, p.epi, st));
+    }
 }
 
 void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode, const Plan* plans,
@@ -592,31 +647,31 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
     const int64_t nseq = M / L;
     const float* rc = mode == ops::SEQ_TIME ? ws.rope_t_cos : ws.rope_f_cos;
     const float* rs = mode == ops::SEQ_TIME ? ws.rope_t_sin : ws.rope_f_sin;
+    const int attn_kind = mode == ops::SEQ_TIME ? PK_ATTN_TIME : PK_ATTN_FREQ;
     for (size_t l = 0; l < tw.layers.size(); ++l) {
         const LayerW& lw = tw.layers[l];
         const Plan* p = plans + 4 * l;
-        ops::rms_norm(ws.R, M, D_, lw.attn_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, lw.wg, lw.bg, H_, ws.gates,
-                      st);
-        run_gemm(ws, p[0], st);
-        ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k, ws.v, dtype_, st);
+        MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.attn_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, lw.wg,
+                                          lw.bg, H_, ws.gates, st));
+        run_gemm(ws, p[0], PK_GEMM_QKV, st);
+        MBR_LAUNCH(PK_ROPE, ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k, ws.v,
+                                              dtype_, st));
         if (attn_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::attention_supported(dh_))
-            tc::attention(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode, NB_, (int)ws.T, ws.merged,
-                          dtype_, st);
+            MBR_LAUNCH(attn_kind, tc::attention(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode, NB_,
+                                                (int)ws.T, ws.merged, dtype_, d_err_, st));
         else
-            ops::attention_simt(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode, NB_, (int)ws.T,
-                                ws.merged, dtype_, st);
-        run_gemm(ws, p[1], st);
-        ops::rms_norm(ws.R, M, D_, lw.ff_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, nullptr, nullptr, 0, nullptr,
-                      st);
-        run_gemm(ws, p[2], st);
-        run_gemm(ws, p[3], st);
-        launches_ += 4;
+            MBR_LAUNCH(attn_kind, ops::attention_simt(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode,
+                                                      NB_, (int)ws.T, ws.merged, dtype_, st));
+        run_gemm(ws, p[1], PK_GEMM_OUT, st);
+        MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.ff_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, nullptr,
+                                          nullptr, 0, nullptr, st));
+        run_gemm(ws, p[2], PK_GEMM_FFN1, st);
+        run_gemm(ws, p[3], PK_GEMM_FFN2, st);
     }
     // final RMSNorm of the transformer; the model's last one also writes the
     // band-major 16-bit copy the mask estimators read
-    ops::rms_norm(ws.R, M, D_, tw.final_gamma, scale, last_of_model ? ws.rm : nullptr, dtype_,
-                  last_of_model ? ws.MT : 0, NB_, ws.R, nullptr, nullptr, 0, nullptr, st);
-    ++launches_;
+    MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, tw.final_gamma, scale, last_of_model ? ws.rm : nullptr, dtype_,
+                                      last_of_model ? ws.MT : 0, NB_, ws.R, nullptr, nullptr, 0, nullptr, st));
 }
 
 void MelBandRoformer::run_forward(Workspace& ws, const float* d_audio, float* d_out, int tap, float* d_tap,
@@ -631,23 +686,20 @@ void MelBandRoformer::run_forward(Workspace& ws, const float* d_audio, float* d_
         if (d_tap) MBR_CUDA(cudaMemcpyAsync(d_tap, src, 4 * n, cudaMemcpyDeviceToDevice, st));
     };
     // 1-6: STFT, stereo merge, band gather (src/model_mel_band_roformer.cu:700-728)
-    ops::stft(d_audio, B, C_, ws.L, c.stft_hop_length, d_window_, d_twiddle_,
-              c.stft_normalized ? 1.0f / std::sqrt((float)c.stft_n_fft) : 1.0f, ws.spec, (int)T, st);
-    ops::band_gather_norm(ws.spec, MT, F_ * C_, d_fi_, d_band_jofs_, d_band_kofs_, d_bs_gamma_, NB_, ws.xb, KP_,
-                          dtype_, st);
-    launches_ += 2;
+    MBR_LAUNCH(PK_STFT, ops::stft(d_audio, B, C_, ws.L, c.stft_hop_length, d_window_, d_twiddle_,
+                                  c.stft_normalized ? 1.0f / std::sqrt((float)c.stft_n_fft) : 1.0f, ws.spec, (int)T,
+                                  st));
+    MBR_LAUNCH(PK_BAND_GATHER, ops::band_gather_norm(ws.spec, MT, F_ * C_, d_fi_, d_band_jofs_, d_band_kofs_,
+                                                     d_bs_gamma_, NB_, ws.xb, KP_, dtype_, st));
     // 7: band split
-    run_gemm(ws, ws.band_split, st);
+    run_gemm(ws, ws.band_split, PK_GEMM_BANDSPLIT, st);
     emit_tap(0, ws.R, M * D_);
     if (tap == 0) return;
     // 8: depth loop (:740-801)
     size_t pi = 0;
     for (int d = 0; d < c.depth; ++d) {
         if (c.skip_connection)
-            for (int j = 0; j < d; ++j) {
-                ops::add_inplace_f32(ws.R, ws.skip[j], M * D_, st);
-                ++launches_;
-            }
+            for (int j = 0; j < d; ++j) MBR_LAUNCH(PK_NORM, ops::add_inplace_f32(ws.R, ws.skip[j], M * D_, st));
         bool last = d == c.depth - 1;
         run_transformer(ws, tt_[d], ops::SEQ_TIME, ws.layer_plans.data() + pi, false, st);
         pi += 4 * tt_[d].layers.size();
@@ -663,20 +715,21 @@ void MelBandRoformer::run_forward(Workspace& ws, const float* d_audio, float* d_
     if (tap == 2) return;
     // 9: mask estimators
     for (int s = 0; s < S; ++s)
-        for (auto& p : ws.mask_plans[s]) run_gemm(ws, p, st);
+        for (size_t i = 0; i < ws.mask_plans[s].size(); ++i)
+            run_gemm(ws, ws.mask_plans[s][i], i + 1 < ws.mask_plans[s].size() ? PK_GEMM_MASK_HIDDEN : PK_GEMM_MASK_OUT,
+                     st);
     emit_tap(3, ws.masks, MT * 2 * J_);
     if (tap == 3) return;
     // 10-11: mask apply + scatter-average + zero_dc
-    ops::mask_scatter(ws.spec, ws.masks, B, S, (int)T, C_, F_, d_rev_off_, d_rev_idx_, d_nbpf_, J_, c.zero_dc, ws.y,
-                      st);
+    MBR_LAUNCH(PK_MASK_SCATTER, ops::mask_scatter(ws.spec, ws.masks, B, S, (int)T, C_, F_, d_rev_off_, d_rev_idx_,
+                                                  d_nbpf_, J_, c.zero_dc, ws.y, st));
     emit_tap(4, ws.y, (int64_t)B * S * C_ * T * F_ * 2);
     if (tap == 4) return;
     // 12: iSTFT
     int64_t nsig = (int64_t)B * S * C_;
-    ops::istft_frames(ws.y, nsig, (int)T, d_window_, d_twiddle_,
-                      c.stft_normalized ? std::sqrt((float)c.stft_n_fft) : 1.0f, ws.frames, st);
-    ops::istft_ola(ws.frames, nsig, (int)T, c.stft_hop_length, d_window_, ws.lout, d_out, st);
-    launches_ += 3;
+    MBR_LAUNCH(PK_ISTFT, ops::istft_frames(ws.y, nsig, (int)T, d_window_, d_twiddle_,
+                                           c.stft_normalized ? std::sqrt((float)c.stft_n_fft) : 1.0f, ws.frames, st));
+    MBR_LAUNCH(PK_ISTFT, ops::istft_ola(ws.frames, nsig, (int)T, c.stft_hop_length, d_window_, ws.lout, d_out, st));
 }
 
 void MelBandRoformer::forward(const float* d_audio, int B, int64_t L, float* d_out, cudaStream_t st) {

@@ -54,6 +54,27 @@ struct MBRConfig {
 // fp16/bf16; the CUDA-core path is the fp32 path and a cross-check).
 enum Backend { BACKEND_SIMT = 0, BACKEND_TC = 1 };
 
+// Kernel classes timed by the optional per-launch profiler (CUDA events on the
+// launching stream).
+enum ProfKind {
+    PK_STFT = 0,
+    PK_BAND_GATHER,
+    PK_GEMM_BANDSPLIT,
+    PK_NORM,
+    PK_GEMM_QKV,
+    PK_ROPE,
+    PK_ATTN_TIME,
+    PK_ATTN_FREQ,
+    PK_GEMM_OUT,
+    PK_GEMM_FFN1,
+    PK_GEMM_FFN2,
+    PK_GEMM_MASK_HIDDEN,
+    PK_GEMM_MASK_OUT,
+    PK_MASK_SCATTER,
+    PK_ISTFT,
+    PK_COUNT
+};
+
 class MelBandRoformer {
 public:
     // Loads and uploads the weights to `device`; dtype DT_F32 / DT_F16 / DT_BF16.
@@ -90,6 +111,13 @@ public:
     // Reads (synchronously) and clears the device error word the tensor-core
     // kernels set when a bounded wait gives up; throws ERR_TIMEOUT if set.
     void check_device_error();
+
+    // Per-kernel-class profiler: when enabled every launch is bracketed by CUDA
+    // events; profile_read() synchronises on the recorded events and returns the
+    // accumulated milliseconds and launch count of `kind` since the last reset.
+    void profile_enable(bool on);
+    void profile_reset();
+    void profile_read(int kind, double* ms, int64_t* count);
 
 private:
     struct Plan {
@@ -152,7 +180,7 @@ private:
 
     Workspace& workspace(int B, int64_t L);
     void build_plans(Workspace& ws);
-    void run_gemm(const Workspace& ws, const Plan& p, cudaStream_t st);
+    void run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st);
     void run_transformer(Workspace& ws, const TransW& tw, int mode, const Plan* plans, bool last_of_model,
                          cudaStream_t st);
     void run_forward(Workspace& ws, const float* d_audio, float* d_out, int tap, float* d_tap, int64_t* tap_n,
@@ -164,6 +192,21 @@ private:
     int64_t J_ = 0, KP_ = 0;
     int gemm_backend_ = BACKEND_SIMT, attn_backend_ = BACKEND_SIMT;
     int64_t launches_ = 0;
+
+    // profiler state
+    bool prof_on_ = false;
+    struct ProfRec {
+        int kind;
+        cudaEvent_t a, b;
+    };
+    std::vector<ProfRec> prof_recs_;
+    std::vector<cudaEvent_t> prof_pool_;
+    size_t prof_used_ = 0;
+    double prof_ms_[PK_COUNT] = {};
+    int64_t prof_n_[PK_COUNT] = {};
+    int prof_begin(int kind, cudaStream_t st);
+    void prof_end(int rec, cudaStream_t st);
+    void prof_collect();
 
     std::vector<int> band_bd_, band_boff_, band_kofs_;  // host copies
     void* wbase_ = nullptr;  // single device allocation holding every weight

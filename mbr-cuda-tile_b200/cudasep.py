@@ -28,7 +28,12 @@ EXPORTS = [
     "mbr_last_error", "mbr_version", "mbr_create", "mbr_destroy", "mbr_get_info", "mbr_output_length",
     "mbr_forward_chunk", "mbr_forward_tap", "mbr_separate_device", "mbr_separate", "mbr_shard_info",
     "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_backend", "mbr_last_launches",
+    "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
 ]
+
+# Kernel classes of mbr_profile_read.
+PROFILE_KINDS = ["stft", "band_gather", "gemm_bandsplit", "norm", "gemm_qkv", "rope", "attn_time", "attn_freq",
+                 "gemm_out", "gemm_ffn1", "gemm_ffn2", "gemm_mask_hidden", "gemm_mask_out", "mask_scatter", "istft"]
 
 _lib = None
 
@@ -65,6 +70,9 @@ def lib():
         L.mbr_shard_finalize.argtypes = [vp, i64, c_float, c_int, c_int, fp, fp, fp, i64, vp]
         L.mbr_set_backend.argtypes = [vp, c_int, c_int]
         L.mbr_last_launches.argtypes = [vp, i64p]
+        L.mbr_sync_check.argtypes = [vp]
+        L.mbr_profile_enable.argtypes = [vp, c_int]
+        L.mbr_profile_read.argtypes = [vp, c_int, ctypes.POINTER(ctypes.c_double), i64p]
         _lib = L
     return _lib
 
@@ -130,6 +138,22 @@ class Model:
         v = ctypes.c_int64()
         _check(lib().mbr_last_launches(self.h, ctypes.byref(v)))
         return v.value
+
+    def sync_check(self):
+        """Synchronise the device and raise if a kernel reported a timed-out wait."""
+        _check(lib().mbr_sync_check(self.h))
+
+    def profile(self, on: bool = True):
+        _check(lib().mbr_profile_enable(self.h, int(bool(on))))
+
+    def profile_read(self) -> dict:
+        """{kind: (milliseconds, launches)} accumulated since profile(True)."""
+        out = {}
+        for i, k in enumerate(PROFILE_KINDS):
+            ms, n = ctypes.c_double(), ctypes.c_int64()
+            _check(lib().mbr_profile_read(self.h, i, ctypes.byref(ms), ctypes.byref(n)))
+            out[k] = (ms.value, n.value)
+        return out
 
     # ---- device entry points (torch CUDA tensors) ----
     def forward(self, audio, out=None, stream=None):

@@ -136,3 +136,38 @@ def test_forward_deterministic(torch_cuda, make_csm):
     a = m.forward(x).cpu().numpy()
     b = m.forward(x).cpu().numpy()
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("preset,dtype", [("tiny2", "fp16"), ("mid", "fp16"), ("mid", "bf16")])
+def test_tensor_core_gemm_matches_cuda_core_gemm(torch_cuda, make_csm, preset, dtype):
+    """The tcgen05 GEMM and the CUDA-core GEMM compute the same forward (same
+    16-bit operands, fp32 accumulation; only the summation order differs)."""
+    torch = torch_cuda
+    import cudasep
+
+    path = make_csm(preset, seed=15)
+    m = _model(path, dtype)
+    x = torch.from_numpy(_audio(16, 1, 2, 44100)).cuda()
+    m.set_backend(cudasep.BACKEND_TC, cudasep.BACKEND_SIMT)
+    a = m.forward(x).cpu().numpy()
+    m.sync_check()
+    m.set_backend(cudasep.BACKEND_SIMT, cudasep.BACKEND_SIMT)
+    b = m.forward(x).cpu().numpy()
+    s = snr_db(b, a)
+    print(f"{preset}/{dtype}: tcgen05 vs CUDA-core GEMM forward SNR {s:.1f} dB")
+    assert s >= 70.0
+
+
+def test_mid_fp16_forward_snr(torch_cuda, make_csm):
+    """std layer shapes (dim 384, 8x64 heads): fp16 forward vs the oracle."""
+    torch = torch_cuda
+    path = make_csm("mid", seed=17)
+    orc = _oracle(path, 1)
+    m = _model(path, "fp16")
+    x = _audio(18, 1, 2, 44100)
+    ref = orc.forward(x)
+    got = m.forward(torch.from_numpy(x).cuda()).cpu().numpy()
+    m.sync_check()
+    s = snr_db(ref, got)
+    print(f"mid fp16 forward SNR vs oracle: {s:.2f} dB")
+    assert s >= FP16_SNR_DB
