@@ -1,14 +1,376 @@
-// attention_tc.cu — tcgen05 attention (placeholder until the tensor-core kernel lands).
+// attention_tc.cu — tcgen05 flash attention for the time axis (L = T frames,
+// 128-key blocks) and the band axis (L <= 64 bands, two sequences packed per
+// 128-row tile with a block-diagonal mask), head dim 64, fp16/bf16.
+//
+// One CTA = one 128-query tile of one (sequence, head) [or two packed band
+// sequences].  Warp 4 lane 0 issues TMA loads and tcgen05.mma; warps 0-3 (one
+// thread per query row, TMEM lane = row) run the online softmax:
+//   S = Q K^T          -> TMEM (128 x 128 fp32)
+//   P = exp2(S*c - m)  -> shared memory (16-bit, 128-byte swizzled K-major)
+//   O_blk = P V        -> TMEM (128 x 64 fp32), folded into registers with the
+//                         running-max correction.
+// V is stored transposed ([seq*H][64][Lp], Lp = L rounded up to 8) so both MMAs
+// read canonical K-major operands.  The epilogue multiplies by the sigmoid gate
+// and writes the merged-head row of each token (apply_gates_and_merge_heads).
+// All waits are bounded (error word instead of a hang).
+#include <cuda.h>
+
+#include <mutex>
+
 #include "attention_tc.h"
 #include "common.cuh"
+#include "ops.h"
+#include "sm100.cuh"
 
 namespace mbr {
 namespace tc {
 
-bool attention_supported(int) { return false; }
-void attention(const void*, const void*, const void*, int64_t, int, int, int, float, const float*, int, int, int,
-               void*, int, int*, cudaStream_t) {
-    throw Error(ERR_UNSUPPORTED, "tcgen05 attention not built");
+using namespace sm100;
+
+namespace {
+
+constexpr int DH = 64;
+constexpr int QT = 128;  // queries per tile
+constexpr int KB = 128;  // keys per block
+
+struct AttnSmem {
+    static constexpr int Q = 0;
+    static constexpr int K0 = 16384;
+    static constexpr int K1 = 32768;
+    static constexpr int V = 49152;
+    static constexpr int P = 65536;  // two 16 KB K-blocks
+    static constexpr int BAR = 98304;
+    static constexpr int TOTAL = BAR + 128 + 1024;  // + barriers + alignment slack
+};
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename T>
+struct IsBf16 {
+    static constexpr bool value = false;
+};
+template <>
+struct IsBf16<__nv_bfloat16> {
+    static constexpr bool value = true;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <typename T, bool PACK>
+__global__ void __launch_bounds__(160, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, float scale_log2,
+                   const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bar = (uint64_t*)(sm + AttnSmem::BAR);
+    uint64_t* bar_q = bar + 0;
+    uint64_t* bar_k = bar + 1;  // [2]
+    uint64_t* bar_v = bar + 3;
+    uint64_t* bar_s = bar + 4;
+    uint64_t* bar_p = bar + 5;
+    uint64_t* bar_o = bar + 6;
+    uint32_t* tmem_slot = (uint32_t*)(bar + 7);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // tile decode
+    int sh0, sh1 = 0, q0 = 0, nkv;
+    if (PACK) {
+        sh0 = blockIdx.x * 2;
+        sh1 = min(sh0 + 1, nsh - 1);
+        nkv = 1;
+    } else {
+        sh0 = blockIdx.y;
+        q0 = blockIdx.x * QT;
+        nkv = (L + KB - 1) / KB;
+    }
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar_q, 1);
+        mbar_init(&bar_k[0], 1);
+        mbar_init(&bar_k[1], 1);
+        mbar_init(bar_v, 1);
+        mbar_init(bar_s, 1);
+        mbar_init(bar_p, 4);
+        mbar_init(bar_o, 1);
+        fence_barrier_init();
+    }
+    if (warp == 4) {
+        tmem_alloc(tmem_slot, 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tS = tmem, tO = tmem + 128;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            prefetch_tensormap(&tmQ);
+            prefetch_tensormap(&tmK);
+            prefetch_tensormap(&tmV);
+            auto load_k = [&](int j) {
+                uint8_t* dst = sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0);
+                mbar_arrive_expect_tx(&bar_k[j & 1], 16384);
+                if (PACK) {
+                    tma_load_2d(dst, &tmK, 0, sh0 * L, &bar_k[j & 1]);
+                    tma_load_2d(dst + 8192, &tmK, 0, sh1 * L, &bar_k[j & 1]);
+                } else {
+                    tma_load_2d(dst, &tmK, 0, sh0 * L + j * KB, &bar_k[j & 1]);
+                }
+            };
+            auto load_v = [&](int j) {
+                uint8_t* dst = sm + AttnSmem::V;
+                mbar_arrive_expect_tx(bar_v, 16384);
+                if (PACK) {
+                    tma_load_2d(dst, &tmV, 0, sh0 * DH, bar_v);
+                    tma_load_2d(dst + 8192, &tmV, 0, sh1 * DH, bar_v);
+                } else {
+                    tma_load_2d(dst, &tmV, j * KB, sh0 * DH, bar_v);
+                    tma_load_2d(dst + 8192, &tmV, j * KB + 64, sh0 * DH, bar_v);
+                }
+            };
+            mbar_arrive_expect_tx(bar_q, 16384);
+            if (PACK) {
+                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L, bar_q);
+                tma_load_2d(sm + AttnSmem::Q + 8192, &tmQ, 0, sh1 * L, bar_q);
+            } else {
+                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L + q0, bar_q);
+            }
+            load_k(0);
+            load_v(0);
+            if (nkv > 1) load_k(1);
+            constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
+            constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value);
+            const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sV = smem_u32(sm + AttnSmem::V),
+                           sP = smem_u32(sm + AttnSmem::P);
+            for (int j = 0; j < nkv; ++j) {
+                if (j == 0 && !mbar_wait(bar_q, 0, err)) break;
+                if (!mbar_wait(&bar_k[j & 1], (j >> 1) & 1, err)) break;
+                tc_fence_after();
+                const uint32_t sK = smem_u32(sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0));
+#pragma unroll
+                for (int k = 0; k < DH / 16; ++k)
+                    mma_f16(tS, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idS, k > 0);
+                mma_commit(bar_s);
+                if (j >= 1 && j + 1 < nkv) load_k(j + 1);  // its buffer's S(j-1) is complete
+                if (!mbar_wait(bar_p, j & 1, err)) break;
+                if (!mbar_wait(bar_v, j & 1, err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < KB / 16; ++k) {
+                    const uint32_t blk = k >> 2, kk = k & 3;
+                    mma_f16(tO, sdesc_sw128(sP + blk * 16384 + 32 * kk), sdesc_sw128(sV + blk * 8192 + 32 * kk),
+                            idO, k > 0);
+                }
+                mma_commit(bar_o);
+                if (j + 1 < nkv) {
+                    if (!mbar_wait(bar_o, j & 1, err)) break;  // P.V(j) done reading V
+                    load_v(j + 1);
+                }
+            }
+        }
+    } else {
+        // softmax / epilogue warps: thread r owns query row r (TMEM lane r)
+        const int r = threadIdx.x;
+        int seg = 0, pos, sh = sh0;
+        bool valid;
+        if (PACK) {
+            seg = r >> 6;
+            pos = r & 63;
+            sh = seg ? sh1 : sh0;
+            valid = pos < L && (seg == 0 || sh0 + 1 < nsh);
+        } else {
+            pos = q0 + r;
+            valid = pos < L;
+        }
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        float o[DH];
+#pragma unroll
+        for (int d = 0; d < DH; ++d) o[d] = 0.f;
+        float m = -INFINITY, l = 0.f;
+        uint8_t* sP = sm + AttnSmem::P;
+        bool ok = true;
+        for (int j = 0; j < nkv && ok; ++j) {
+            if (!mbar_wait(bar_s, j & 1, err)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            // pass 1: row max of the valid keys
+            float mx = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < KB / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tS + lane_off + c * 32, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int kc = c * 32 + i;
+                    bool kv = PACK ? ((kc >> 6) == seg && (kc & 63) < L) : (j * KB + kc < L);
+                    if (kv) mx = fmaxf(mx, __uint_as_float(v[i]) * scale_log2);
+                }
+            }
+            float m_new = fmaxf(m, mx);
+            if (m_new == -INFINITY) m_new = 0.f;  // fully masked row (padding rows only)
+            const float alpha = exp2f(m - m_new);
+            // pass 2: probabilities -> shared memory (swizzled K-major rows)
+            float rs = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < KB / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tS + lane_off + c * 32, v);
+                tmem_ld_wait();
+                float p[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int kc = c * 32 + i;
+                    bool kv = PACK ? ((kc >> 6) == seg && (kc & 63) < L) : (j * KB + kc < L);
+                    p[i] = kv ? exp2f(__uint_as_float(v[i]) * scale_log2 - m_new) : 0.f;
+                    rs += p[i];
+                }
+                // keys [32c, 32c+32) = 4 chunks of 8 in K-block (32c)/64
+                uint8_t* blk = sP + ((c * 32) >> 6) * 16384 + r * 128;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int ch = (((c * 32) & 63) >> 3) + q;
+                    uint4 u = make_uint4(pack2(p[8 * q], p[8 * q + 1], (T*)nullptr),
+                                         pack2(p[8 * q + 2], p[8 * q + 3], (T*)nullptr),
+                                         pack2(p[8 * q + 4], p[8 * q + 5], (T*)nullptr),
+                                         pack2(p[8 * q + 6], p[8 * q + 7], (T*)nullptr));
+                    *reinterpret_cast<uint4*>(blk + ((ch ^ (r & 7)) << 4)) = u;
+                }
+            }
+            l = l * alpha + rs;
+            m = m_new;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_p);
+            if (!mbar_wait(bar_o, j & 1, err)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < DH / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tO + lane_off + c * 32, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha + __uint_as_float(v[i]);
+            }
+        }
+        if (ok && valid) {
+            const int h = sh % H;
+            const int64_t s = sh / H;
+            int64_t tok;
+            if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
+            else tok = s * NB + pos;
+            const float g = gates[tok * H + h] / l;
+            uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + h * DH);
+#pragma unroll
+            for (int q = 0; q < DH / 8; ++q)
+                dst[q] = make_uint4(pack2(o[8 * q] * g, o[8 * q + 1] * g, (T*)nullptr),
+                                    pack2(o[8 * q + 2] * g, o[8 * q + 3] * g, (T*)nullptr),
+                                    pack2(o[8 * q + 4] * g, o[8 * q + 5] * g, (T*)nullptr),
+                                    pack2(o[8 * q + 6] * g, o[8 * q + 7] * g, (T*)nullptr));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    if (!fn) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+void make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_cols, int box_rows, int dtype) {
+    MBR_CHECK(((uintptr_t)base & 15) == 0 && (cols * 2) % 16 == 0, "attention TMA operand misaligned");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(m, dtype == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+template <typename T, bool PACK>
+void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int nsh, int H, int L,
+            float scale_log2, const float* gates, int mode, int NB, int Tn, void* merged, int* err, cudaStream_t st) {
+    auto kern = attn_tc_kernel<T, PACK>;
+    static bool attr[64] = {};
+    int dev = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    MBR_CHECK(dev >= 0 && dev < 64, "device index out of range");
+    if (!attr[dev]) {
+        MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::TOTAL));
+        attr[dev] = true;
+    }
+    dim3 grid = PACK ? dim3((unsigned)((nsh + 1) / 2)) : dim3((unsigned)((L + QT - 1) / QT), (unsigned)nsh);
+    kern<<<grid, 160, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
+                                              err);
+    MBR_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+bool attention_supported(int dim_head) { return dim_head == DH; }
+
+int64_t vt_pitch(int L) { return round_up(L, 8); }
+
+void attention(const void* q, const void* k, const void* vt, int64_t nseq, int H, int L, int dh, float scale,
+               const float* gates, int mode, int NB, int T, void* merged, int dtype, int* d_err, cudaStream_t st) {
+    MBR_CHECK(dh == DH, "tc attention: dim_head must be 64");
+    MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "tc attention: fp16 or bf16 only");
+    const int64_t nsh = nseq * H;
+    MBR_CHECK(nsh < (1 << 30) && nsh * L < (1ll << 31), "tc attention: problem too large for 32-bit coordinates");
+    const bool pack = L <= 64;
+    CUtensorMap mq, mk, mv;
+    const int qrows = pack ? 64 : QT;
+    make_map(&mq, q, nsh * L, DH, DH, qrows, dtype);
+    make_map(&mk, k, nsh * L, DH, DH, pack ? 64 : KB, dtype);
+    make_map(&mv, vt, nsh * DH, vt_pitch(L), 64, DH, dtype);
+    const float scale_log2 = scale * 1.4426950408889634f;
+    if (dtype == DT_BF16) {
+        if (pack) launch<__nv_bfloat16, true>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        else launch<__nv_bfloat16, false>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
+    } else {
+        if (pack) launch<__half, true>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        else launch<__half, false>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
+    }
 }
 
 }  // namespace tc

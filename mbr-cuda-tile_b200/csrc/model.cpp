@@ -389,7 +389,11 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
     take(&ws->qkv, es * M * 3 * DI_);
     take(&ws->q, es * M * DI_);
     take(&ws->k, es * M * DI_);
-    take(&ws->v, es * M * DI_);
+    // v holds [seq][H][L][dh] (CUDA-core attention) or V^T [seq*H][dh][round_up(L, 8)]
+    // (tensor-core attention) for both the time (L = T) and band (L = NB) passes
+    int64_t v_elems = std::max<int64_t>({M * DI_, (int64_t)B * NB_ * H_ * dh_ * round_up(T, 8),
+                                         MT * H_ * dh_ * round_up(NB_, 8)});
+    take(&ws->v, es * v_elems);
     take(&ws->merged, es * M * DI_);
     take(&ws->hf, es * M * hid_);
     take(&ws->rm, es * M * D_);
@@ -654,14 +658,17 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
         MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.attn_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, lw.wg,
                                           lw.bg, H_, ws.gates, st));
         run_gemm(ws, p[0], PK_GEMM_QKV, st);
-        MBR_LAUNCH(PK_ROPE, ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k, ws.v,
-                                              dtype_, st));
-        if (attn_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::attention_supported(dh_))
+        const bool tc_attn = attn_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::attention_supported(dh_);
+        MBR_LAUNCH(PK_ROPE, ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k,
+                                              tc_attn ? nullptr : ws.v, dtype_, st));
+        if (tc_attn) {
+            MBR_LAUNCH(PK_ROPE, ops::scatter_vt(ws.qkv, M, H_, mode, NB_, (int)ws.T, ws.v, dtype_, st));
             MBR_LAUNCH(attn_kind, tc::attention(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode, NB_,
                                                 (int)ws.T, ws.merged, dtype_, d_err_, st));
-        else
+        } else {
             MBR_LAUNCH(attn_kind, ops::attention_simt(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode,
                                                       NB_, (int)ws.T, ws.merged, dtype_, st));
+        }
         run_gemm(ws, p[1], PK_GEMM_OUT, st);
         MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.ff_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, nullptr,
                                           nullptr, 0, nullptr, st));

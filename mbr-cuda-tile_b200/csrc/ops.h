@@ -38,8 +38,12 @@ void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale,
               int64_t band_major_mt, int NB, float* r_out, const float* wg, const float* bg, int H, float* gates,
               cudaStream_t st);
 
+// q, k (rotated) and, if v is non-null, v -> [nseq][H][L][dh].
 void rope_scatter(const void* qkv, int64_t M, int H, int dh, const float* cos_t, const float* sin_t, int mode,
                   int NB, int T, void* q, void* k, void* v, int dtype, cudaStream_t st);
+// v -> V^T [nseq*H][64][lp] (lp = L rounded up to 8, padding zeroed), the
+// K-major B operand of the tensor-core P.V product.  dh = 64, 16-bit.
+void scatter_vt(const void* qkv, int64_t M, int H, int mode, int NB, int T, void* vt, int dtype, cudaStream_t st);
 
 void attention_simt(const void* q, const void* k, const void* v, int64_t nseq, int H, int L, int dh, float scale,
                     const float* gates, int mode, int NB, int T, void* merged, int dtype, cudaStream_t st);
