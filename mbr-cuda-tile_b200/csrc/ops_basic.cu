@@ -3,6 +3,8 @@
 // chunk overlap-add.  Every kernel reads and writes HBM once per element with
 // coalesced (mostly 128-bit) accesses and keeps reductions in registers /
 // warp shuffles.
+#include <algorithm>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -111,59 +113,81 @@ __global__ void __launch_bounds__(256) band_gather_norm_kernel(const float2* __r
     }
 }
 
-// Warp per row.  D % 4 == 0, D <= 1024.
 template <typename T>
+__device__ __forceinline__ void store4(T* p, float4 y) {
+    if constexpr (sizeof(T) == 4) {
+        *reinterpret_cast<float4*>(p) = y;
+    } else {
+        T e[4] = {from_f32<T>(y.x), from_f32<T>(y.y), from_f32<T>(y.z), from_f32<T>(y.w)};
+        *reinterpret_cast<uint2*>(p) = *reinterpret_cast<uint2*>(e);
+    }
+}
+
+// One warp per row, rows strided over a persistent grid (the gate weights are
+// staged in shared memory once per CTA).  Each lane holds up to MAXC float4
+// chunks of the row in registers.  D % 4 == 0, D <= 128 * MAXC, H <= 32.
+template <typename T, int MAXC>
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ R, int64_t M, int D,
                                                        const float* __restrict__ gamma, float scale,
                                                        T* __restrict__ xn, int64_t band_major_mt, int NB,
                                                        float* r_out, const float* __restrict__ wg,
                                                        const float* __restrict__ bg, int H,
                                                        float* __restrict__ gates) {
-    extern __shared__ float swg[];  // [H][D]
+    extern __shared__ float4 swg4[];  // [H][D/4]
+    const int D4 = D / 4;
     if (wg) {
-        for (int i = threadIdx.x; i < H * D; i += blockDim.x) swg[i] = wg[i];
+        const float4* w4 = reinterpret_cast<const float4*>(wg);
+        for (int i = threadIdx.x; i < H * D4; i += blockDim.x) swg4[i] = w4[i];
         __syncthreads();
     }
-    int lane = threadIdx.x & 31;
-    int64_t m = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (m >= M) return;
-    const float4* x4 = reinterpret_cast<const float4*>(R + m * D);
-    float4 v[8];
-    int nv = 0;
-    float ss = 0.f;
-    for (int c = lane; c < D / 4; c += 32) {
-        float4 a = x4[c];
-        v[nv++] = a;
-        ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
-    }
-    ss = warp_sum(ss);
-    float inv = rsqrtf(ss + 1e-12f) * scale;
+    const int lane = threadIdx.x & 31;
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
-    int64_t orow = m;
-    if (band_major_mt > 0) orow = (m % NB) * band_major_mt + m / NB;
-    int i = 0;
-    for (int c = lane; c < D / 4; c += 32, ++i) {
-        float4 g = g4[c];
-        float4 y = make_float4(v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w);
-        v[i] = y;
-        if (r_out) reinterpret_cast<float4*>(r_out + m * D)[c] = y;
-        if (xn) {
-            T* o = xn + orow * D + 4 * c;
-            o[0] = from_f32<T>(y.x);
-            o[1] = from_f32<T>(y.y);
-            o[2] = from_f32<T>(y.z);
-            o[3] = from_f32<T>(y.w);
-        }
+    float4 g[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+        const int c = lane + 32 * i;
+        g[i] = c < D4 ? g4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (wg) {
-        for (int h = 0; h < H; ++h) {
-            const float* w = swg + h * D;
-            float acc = 0.f;
-            i = 0;
-            for (int c = lane; c < D / 4; c += 32, ++i)
-                acc += v[i].x * w[4 * c] + v[i].y * w[4 * c + 1] + v[i].z * w[4 * c + 2] + v[i].w * w[4 * c + 3];
-            acc = warp_sum(acc);
-            if (lane == 0) gates[m * H + h] = 1.0f / (1.0f + expf(-(acc + bg[h])));
+    const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t m = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += stride) {
+        const float4* x4 = reinterpret_cast<const float4*>(R + m * D);
+        float4 v[MAXC];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < MAXC; ++i) {
+            const int c = lane + 32 * i;
+            v[i] = c < D4 ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        }
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss + 1e-12f) * scale;
+        const int64_t orow = band_major_mt > 0 ? (m % NB) * band_major_mt + m / NB : m;
+#pragma unroll
+        for (int i = 0; i < MAXC; ++i) {
+            const int c = lane + 32 * i;
+            v[i] = make_float4(v[i].x * inv * g[i].x, v[i].y * inv * g[i].y, v[i].z * inv * g[i].z,
+                               v[i].w * inv * g[i].w);
+            if (c < D4) {
+                if (r_out) reinterpret_cast<float4*>(r_out + m * D)[c] = v[i];
+                if (xn) store4<T>(xn + orow * D + 4 * c, v[i]);
+            }
+        }
+        if (wg) {
+            float mine = 0.f;  // lane h ends up holding the dot product of gate h
+            for (int h = 0; h < H; ++h) {
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < MAXC; ++i) {
+                    const int c = lane + 32 * i;
+                    if (c < D4) {
+                        const float4 w = swg4[h * D4 + c];
+                        acc += v[i].x * w.x + v[i].y * w.y + v[i].z * w.z + v[i].w * w.w;
+                    }
+                }
+                acc = warp_sum(acc);
+                if (lane == h) mine = acc;
+            }
+            if (lane < H) gates[m * H + lane] = 1.0f / (1.0f + expf(-(mine + bg[lane])));
         }
     }
 }
@@ -518,12 +542,26 @@ void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale,
               int64_t band_major_mt, int NB, float* r_out, const float* wg, const float* bg, int H, float* gates,
               cudaStream_t st) {
     MBR_CHECK(D % 4 == 0 && D <= 1024, "rms_norm: dim must be a multiple of 4 and <= 1024");
+    MBR_CHECK(!wg || H <= 32, "rms_norm: at most 32 gates");
     size_t sm = wg ? sizeof(float) * H * D : 0;
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        MBR_CUDA(cudaGetDevice(&dev));
+        MBR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    }
+    unsigned grid = (unsigned)std::min<int64_t>(ceil_div(M, 8), (int64_t)sms * 8);
     MBR_DISPATCH_DTYPE(dtype, T, {
-        if (sm > 48 * 1024)
-            MBR_CUDA(cudaFuncSetAttribute(rms_norm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        rms_norm_kernel<T><<<nblk(M, 8), 256, sm, st>>>(R, M, D, gamma, scale, (T*)xn, band_major_mt, NB, r_out,
-                                                        wg, bg, H, gates);
+        auto run = [&](auto kern) {
+            if (sm > 48 * 1024)
+                MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+            kern<<<grid, 256, sm, st>>>(R, M, D, gamma, scale, (T*)xn, band_major_mt, NB, r_out, wg, bg, H, gates);
+        };
+        if (D <= 128) run(rms_norm_kernel<T, 1>);
+        else if (D <= 256) run(rms_norm_kernel<T, 2>);
+        else if (D <= 384) run(rms_norm_kernel<T, 3>);
+        else if (D <= 512) run(rms_norm_kernel<T, 4>);
+        else run(rms_norm_kernel<T, 8>);
     });
     MBR_CUDA(cudaGetLastError());
 }
