@@ -9,8 +9,8 @@
 //   P = exp2(S*c - m)  -> shared memory (16-bit, 128-byte swizzled K-major)
 //   O_blk = P V        -> TMEM (128 x 64 fp32), folded into registers with the
 //                         running-max correction.
-// V is stored transposed ([seq*H][64][Lp], Lp = L rounded up to 8) so both MMAs
-// read canonical K-major operands.  The epilogue multiplies by the sigmoid gate
+// V keeps the [seq][H][L][64] layout of q and k: its 128-key tile is the
+// MN-major B operand of the P.V product.  The epilogue multiplies by the sigmoid gate
 // and writes the merged-head row of each token (apply_gates_and_merge_heads).
 // All waits are bounded (error word instead of a hang).
 #include <cuda.h>
@@ -38,7 +38,7 @@ struct AttnSmem {
     static constexpr int K0 = 16384;
     static constexpr int K1 = 32768;
     static constexpr int V = 49152;
-    static constexpr int P = 65536;  // two 16 KB K-blocks
+    static constexpr int P = 65536;  // two 16 KB K-blocks (keys 0-63, 64-127)
     static constexpr int BAR = 98304;
     static constexpr int TOTAL = BAR + 128 + 1024;  // + barriers + alignment slack
 };
@@ -133,11 +133,10 @@ __global__ void __launch_bounds__(160, 2)
                 uint8_t* dst = sm + AttnSmem::V;
                 mbar_arrive_expect_tx(bar_v, 16384);
                 if (PACK) {
-                    tma_load_2d(dst, &tmV, 0, sh0 * DH, bar_v);
-                    tma_load_2d(dst + 8192, &tmV, 0, sh1 * DH, bar_v);
+                    tma_load_2d(dst, &tmV, 0, sh0 * L, bar_v);
+                    tma_load_2d(dst + 8192, &tmV, 0, sh1 * L, bar_v);
                 } else {
-                    tma_load_2d(dst, &tmV, j * KB, sh0 * DH, bar_v);
-                    tma_load_2d(dst + 8192, &tmV, j * KB + 64, sh0 * DH, bar_v);
+                    tma_load_2d(dst, &tmV, 0, sh0 * L + j * KB, bar_v);
                 }
             };
             mbar_arrive_expect_tx(bar_q, 16384);
@@ -151,7 +150,7 @@ __global__ void __launch_bounds__(160, 2)
             load_v(0);
             if (nkv > 1) load_k(1);
             constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
-            constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value);
+            constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
             const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sV = smem_u32(sm + AttnSmem::V),
                            sP = smem_u32(sm + AttnSmem::P);
             for (int j = 0; j < nkv; ++j) {
@@ -170,8 +169,9 @@ __global__ void __launch_bounds__(160, 2)
 #pragma unroll
                 for (int k = 0; k < KB / 16; ++k) {
                     const uint32_t blk = k >> 2, kk = k & 3;
-                    mma_f16(tO, sdesc_sw128(sP + blk * 16384 + 32 * kk), sdesc_sw128(sV + blk * 8192 + 32 * kk),
-                            idO, k > 0);
+                    // A: P rows (K-major, 64 keys per 16 KB block); B: V keys 16k..16k+15 (MN-major)
+                    mma_f16(tO, sdesc_sw128(sP + blk * 16384 + 32 * kk), sdesc_sw128_mn(sV + 2048 * k), idO,
+                            k > 0);
                 }
                 mma_commit(bar_o);
                 if (j + 1 < nkv) {
@@ -349,9 +349,7 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
 
 bool attention_supported(int dim_head) { return dim_head == DH; }
 
-int64_t vt_pitch(int L) { return round_up(L, 8); }
-
-void attention(const void* q, const void* k, const void* vt, int64_t nseq, int H, int L, int dh, float scale,
+void attention(const void* q, const void* k, const void* v, int64_t nseq, int H, int L, int dh, float scale,
                const float* gates, int mode, int NB, int T, void* merged, int dtype, int* d_err, cudaStream_t st) {
     MBR_CHECK(dh == DH, "tc attention: dim_head must be 64");
     MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "tc attention: fp16 or bf16 only");
@@ -362,7 +360,7 @@ void attention(const void* q, const void* k, const void* vt, int64_t nseq, int H
     const int qrows = pack ? 64 : QT;
     make_map(&mq, q, nsh * L, DH, DH, qrows, dtype);
     make_map(&mk, k, nsh * L, DH, DH, pack ? 64 : KB, dtype);
-    make_map(&mv, vt, nsh * DH, vt_pitch(L), 64, DH, dtype);
+    make_map(&mv, v, nsh * L, DH, DH, pack ? 64 : KB, dtype);
     const float scale_log2 = scale * 1.4426950408889634f;
     if (dtype == DT_BF16) {
         if (pack) launch<__nv_bfloat16, true>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);

@@ -79,7 +79,9 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
                 c4[j] = o;
             }
         } else {
-            for (int j = 0; j < nvalid; ++j) c[j] = EPI == ops::EPI_ADD_F32 ? c[j] + v[j] : v[j];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nvalid) c[j] = EPI == ops::EPI_ADD_F32 ? c[j] + v[j] : v[j];
         }
     } else if constexpr (EPI == ops::EPI_GLU_F32) {
         float o[16];
@@ -92,7 +94,9 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
 #pragma unroll
             for (int j = 0; j < 4; ++j) c4[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
         } else {
-            for (int i = 0; i < ovalid; ++i) c[i] = o[i];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (i < ovalid) c[i] = o[i];
         }
     } else {
         if constexpr (EPI == ops::EPI_GELU_T) {
@@ -111,15 +115,67 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
                                    pack2(v[8 * j + 4], v[8 * j + 5], (T*)nullptr),
                                    pack2(v[8 * j + 6], v[8 * j + 7], (T*)nullptr));
         } else {
-            for (int j = 0; j < nvalid; ++j) c[j] = from_f32<T>(v[j]);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nvalid) c[j] = from_f32<T>(v[j]);
         }
     }
 }
 
+// QKV epilogue: RoPE on q and k (interleaved pairs, src/mbr_cuda_tile.cu:3928-3943)
+// and scatter of the 32 columns [n0, n0+32) of token `row` into the
+// per-sequence head-major q / k / v tensors [seq][H][L][64].
+template <typename T>
+__device__ __forceinline__ void epilogue_qkv(const EpiQKV& e, int row, int n0, const uint32_t (&r)[32]) {
+    const int DI = e.H * 64;
+    const int sec = n0 / DI, rem = n0 - sec * DI;
+    const int h = rem >> 6, d0 = rem & 63;
+    int64_t s;
+    int pos, L;
+    if (e.mode == ops::SEQ_TIME) {
+        const int k = row % e.NB;
+        const int64_t bt = row / e.NB;
+        pos = (int)(bt % e.T);
+        s = (bt / e.T) * e.NB + k;
+        L = e.T;
+    } else {
+        s = row / e.NB;
+        pos = row % e.NB;
+        L = e.NB;
+    }
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (sec < 2) {
+        const float* cs = e.cos_t + pos * 32 + (d0 >> 1);
+        const float* sn = e.sin_t + pos * 32 + (d0 >> 1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float c = __ldg(cs + i), si = __ldg(sn + i);
+            const float x0 = v[2 * i], x1 = v[2 * i + 1];
+            v[2 * i] = x0 * c - x1 * si;
+            v[2 * i + 1] = x0 * si + x1 * c;
+        }
+    }
+    T* base = (T*)(sec == 0 ? e.q : sec == 1 ? e.k : e.v);
+    uint4* dst = reinterpret_cast<uint4*>(base + ((s * e.H + h) * L + pos) * 64 + d0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        dst[j] = make_uint4(pack2(v[8 * j], v[8 * j + 1], (T*)nullptr), pack2(v[8 * j + 2], v[8 * j + 3], (T*)nullptr),
+                            pack2(v[8 * j + 4], v[8 * j + 5], (T*)nullptr),
+                            pack2(v[8 * j + 6], v[8 * j + 7], (T*)nullptr));
+}
+
+// Epilogue warps: warps 2..9; warp w drains TMEM lane quarter (w % 4) for the
+// column half (w - 2) / 4 of the tile.
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+
 template <typename T, int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const ops::GemmGroup* __restrict__ groups, const int4* __restrict__ tiles, int ntiles, int* err) {
+                   const ops::GemmGroup* __restrict__ groups, const int4* __restrict__ tiles, int ntiles, int* err,
+                   const EpiQKV qkv) {
     using Cfg = TileCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -139,7 +195,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
+            mbar_init(&acc_empty[b], kEpiWarps);
         }
         fence_barrier_init();
     }
@@ -210,6 +266,8 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int half = (warp - 2) >> 2;
+        constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp
         int tcount = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tcount) {
             const int4 tl = tiles[t];
@@ -220,14 +278,18 @@ __global__ void __launch_bounds__(192, 1)
             tc_fence_after();
             const int row = tl.y + q * 32 + lane;
             const bool rv = row < g.M;
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + half * (BN / 2);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                const int n0 = tl.z + c * 32;
+            for (int c = 0; c < kChunks; ++c) {
+                const int n0 = tl.z + half * (BN / 2) + c * 32;
                 if (n0 >= g.N) break;
                 uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, r);
+                tmem_ld32(taddr + c * 32, r);
                 tmem_ld_wait();
-                if (rv) epilogue_chunk<T, EPI>(g, row, n0, r);
+                if (rv) {
+                    if constexpr (EPI == ops::EPI_QKV) epilogue_qkv<T>(qkv, row, n0, r);
+                    else epilogue_chunk<T, EPI>(g, row, n0, r);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -297,7 +359,7 @@ void launch_one(const GemmLaunch& L, int* d_err, cudaStream_t st) {
         attr[dev] = true;
     }
     int grid = std::min(L.ntiles, sms[dev]);
-    kern<<<grid, 192, TileCfg<BN>::SMEM, st>>>(L.tmA, L.tmB, L.groups, L.tiles, L.ntiles, d_err);
+    kern<<<grid, kGemmThreads, TileCfg<BN>::SMEM, st>>>(L.tmA, L.tmB, L.groups, L.tiles, L.ntiles, d_err, L.qkv);
     MBR_CUDA(cudaGetLastError());
 }
 
@@ -310,6 +372,7 @@ void launch_bn(const GemmLaunch& L, int* d_err, cudaStream_t st) {
         case ops::EPI_GELU_T: launch_one<T, BN, ops::EPI_GELU_T>(L, d_err, st); break;
         case ops::EPI_TANH_T: launch_one<T, BN, ops::EPI_TANH_T>(L, d_err, st); break;
         case ops::EPI_GLU_F32: launch_one<T, BN, ops::EPI_GLU_F32>(L, d_err, st); break;
+        case ops::EPI_QKV: launch_one<T, BN, ops::EPI_QKV>(L, d_err, st); break;
         default: throw Error(ERR_INVALID, "tc gemm: bad epilogue");
     }
 }
@@ -323,7 +386,7 @@ void launch_t(const GemmLaunch& L, int* d_err, cudaStream_t st) {
 
 }  // namespace
 
-bool gemm_supported(int epi) { return epi >= ops::EPI_F32 && epi <= ops::EPI_GLU_F32; }
+bool gemm_supported(int epi) { return epi >= ops::EPI_F32 && epi <= ops::EPI_QKV; }
 
 void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, GemmLaunch& L, size_t& L_first) {
     MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "tc gemm needs fp16 or bf16 operands");
@@ -335,6 +398,10 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
     else bn = 256;
     L.bn = bn;
     L.epi = p.epi;
+    if (p.epi == ops::EPI_QKV)
+        MBR_CHECK(L.qkv.q && L.qkv.k && L.qkv.v && L.qkv.cos_t && L.qkv.H > 0 && p.maxN == 3 * L.qkv.H * 64 &&
+                      bn % 64 == 0,
+                  "tc gemm: QKV epilogue needs head dim 64 and its q/k/v/rope buffers");
     make_map(&L.tmA, p.a_base, p.a_rows, p.a_cols, BM, dtype);
     make_map(&L.tmB, p.b_base, p.b_rows, p.b_cols, bn, dtype);
     L_first = tiles.size();

@@ -33,6 +33,17 @@ struct GemmPlanTC {
     int64_t b_rows = 0, b_cols = 0;
 };
 
+// Parameters of the fused QKV epilogue (ops::EPI_QKV): RoPE on q/k with the
+// position of each token in its sequence, and scatter into [seq][H][L][64].
+struct EpiQKV {
+    int mode = 0, NB = 0, T = 0, H = 0;
+    const float* cos_t = nullptr;  // [L][32]
+    const float* sin_t = nullptr;
+    void* q = nullptr;
+    void* k = nullptr;
+    void* v = nullptr;
+};
+
 // Prepared launch: tensor maps and the tile list (built once per workspace).
 struct GemmLaunch {
     CUtensorMap tmA, tmB;
@@ -41,6 +52,7 @@ struct GemmLaunch {
     int bn = 128;
     int epi = 0;
     const ops::GemmGroup* groups = nullptr;
+    EpiQKV qkv;
     bool ok = false;
 };
 

@@ -389,11 +389,7 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
     take(&ws->qkv, es * M * 3 * DI_);
     take(&ws->q, es * M * DI_);
     take(&ws->k, es * M * DI_);
-    // v holds [seq][H][L][dh] (CUDA-core attention) or V^T [seq*H][dh][round_up(L, 8)]
-    // (tensor-core attention) for both the time (L = T) and band (L = NB) passes
-    int64_t v_elems = std::max<int64_t>({M * DI_, (int64_t)B * NB_ * H_ * dh_ * round_up(T, 8),
-                                         MT * H_ * dh_ * round_up(NB_, 8)});
-    take(&ws->v, es * v_elems);
+    take(&ws->v, es * M * DI_);
     take(&ws->merged, es * M * DI_);
     take(&ws->hf, es * M * hid_);
     take(&ws->rm, es * M * D_);
@@ -455,6 +451,19 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
             tp.b_rows = p->b_rows;
             tp.b_cols = p->b_cols;
             tc::GemmLaunch L;
+            if (p->qkv_mode >= 0 && dh_ == 64) {
+                // fused RoPE + head scatter epilogue (replaces rope_scatter)
+                tp.epi = ops::EPI_QKV;
+                L.qkv.mode = p->qkv_mode;
+                L.qkv.NB = NB_;
+                L.qkv.T = (int)ws->T;
+                L.qkv.H = H_;
+                L.qkv.cos_t = p->qkv_mode == ops::SEQ_TIME ? ws->rope_t_cos : ws->rope_f_cos;
+                L.qkv.sin_t = p->qkv_mode == ops::SEQ_TIME ? ws->rope_t_sin : ws->rope_f_sin;
+                L.qkv.q = ws->q;
+                L.qkv.k = ws->k;
+                L.qkv.v = ws->v;
+            }
             size_t first = 0;
             tc::gemm_prepare(tp, dtype_, tiles, L, first);
             p->launch = (int)ws->launches.size();
@@ -524,6 +533,7 @@ void MelBandRoformer::build_plans(Workspace& ws) {
             for (const LayerW& lw : tw.layers) {
                 Plan p[4];
                 begin(p[0], ops::EPI_T);
+                p[0].qkv_mode = kind;
                 p[0].a_base = ws.xn, p[0].a_rows = M, p[0].a_cols = D_;
                 p[0].b_base = lw.wqkv, p[0].b_rows = 3 * DI_, p[0].b_cols = D_;
                 push(p[0], mk(ws.xn, D_, lw.wqkv, D_, ws.qkv, 3 * DI_, nullptr, M, 3 * DI_, D_));
@@ -658,11 +668,14 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
         MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.attn_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, lw.wg,
                                           lw.bg, H_, ws.gates, st));
         run_gemm(ws, p[0], PK_GEMM_QKV, st);
+        // the tensor-core QKV GEMM applies RoPE and scatters q/k/v in its epilogue
+        const bool fused_qkv = gemm_backend_ == BACKEND_TC && p[0].launch >= 0 &&
+                               ws.launches[p[0].launch].epi == ops::EPI_QKV;
+        if (!fused_qkv)
+            MBR_LAUNCH(PK_ROPE, ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k, ws.v,
+                                                  dtype_, st));
         const bool tc_attn = attn_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::attention_supported(dh_);
-        MBR_LAUNCH(PK_ROPE, ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k,
-                                              tc_attn ? nullptr : ws.v, dtype_, st));
         if (tc_attn) {
-            MBR_LAUNCH(PK_ROPE, ops::scatter_vt(ws.qkv, M, H_, mode, NB_, (int)ws.T, ws.v, dtype_, st));
             MBR_LAUNCH(attn_kind, tc::attention(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode, NB_,
                                                 (int)ws.T, ws.merged, dtype_, d_err_, st));
         } else {

@@ -124,6 +124,7 @@ private:
         size_t first = 0;  // index into the workspace's group array
         int n = 0, maxM = 0, maxN = 0, maxK = 0, epi = 0;
         int launch = -1;  // index into Workspace::launches (tensor-core path)
+        int qkv_mode = -1;  // QKV projection of a time (0) / band (1) transformer
         // operand tensor shapes for the tensor-core path (rows x cols, elements)
         const void* a_base = nullptr;
         int64_t a_rows = 0, a_cols = 0;

@@ -41,9 +41,6 @@ void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale,
 // q, k (rotated) and, if v is non-null, v -> [nseq][H][L][dh].
 void rope_scatter(const void* qkv, int64_t M, int H, int dh, const float* cos_t, const float* sin_t, int mode,
                   int NB, int T, void* q, void* k, void* v, int dtype, cudaStream_t st);
-// v -> V^T [nseq*H][64][lp] (lp = L rounded up to 8, padding zeroed), the
-// K-major B operand of the tensor-core P.V product.  dh = 64, 16-bit.
-void scatter_vt(const void* qkv, int64_t M, int H, int mode, int NB, int T, void* vt, int dtype, cudaStream_t st);
 
 void attention_simt(const void* q, const void* k, const void* v, int64_t nseq, int H, int L, int dh, float scale,
                     const float* gates, int mode, int NB, int T, void* merged, int dtype, cudaStream_t st);
@@ -67,6 +64,7 @@ enum Epilogue {
     EPI_GELU_T = 3,   // C (dtype) = gelu(acc + bias)
     EPI_TANH_T = 4,   // C (dtype) = tanh(acc + bias)
     EPI_GLU_F32 = 5,  // C[m][n/2] (fp32) = (acc_n + b_n) * sigmoid(acc_{n+1} + b_{n+1}), n even
+    EPI_QKV = 6,      // RoPE(q, k) + scatter of q, k, v into [seq][H][L][64] (tensor-core path only)
 };
 void gemm_simt(const GemmGroup* d_groups, int ngroups, int maxM, int maxN, int dtype, int epi, cudaStream_t st);
 

@@ -239,44 +239,6 @@ __global__ void rope_scatter_kernel(const T* __restrict__ qkv, int64_t M, int H,
     }
 }
 
-// V of the packed qkv rows -> V^T [seq*H][64][lp] (lp = L rounded up to 8,
-// padding written as zeros) through a 32-position shared-memory tile so both
-// the gather and the transposed store are 16-byte coalesced.
-template <typename T>
-__global__ void __launch_bounds__(256) scatter_vt_kernel(const T* __restrict__ qkv, int H, int mode, int NB, int Tn,
-                                                         int L, int64_t lp, T* __restrict__ vt) {
-    __shared__ T tile[64][40];
-    const int64_t sh = blockIdx.y;
-    const int64_t s = sh / H;
-    const int h = (int)(sh % H);
-    const int p0 = blockIdx.x * 32;
-    const int DI = H * 64;
-    const int t = threadIdx.x;
-    {
-        const int p = t >> 3, dc = t & 7;
-        uint4 u = make_uint4(0, 0, 0, 0);
-        if (p0 + p < L) {
-            const int64_t tok = token_of(s, p0 + p, mode, NB, Tn);
-            u = *reinterpret_cast<const uint4*>(qkv + tok * 3 * DI + 2 * DI + h * 64 + 8 * dc);
-        }
-        const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) tile[8 * dc + i][p] = e[i];
-    }
-    __syncthreads();
-    {
-        const int d = t >> 2, pc = t & 3;
-        const int p = p0 + 8 * pc;
-        if (p < lp) {
-            uint4 u;
-            T* e = reinterpret_cast<T*>(&u);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) e[i] = tile[d][8 * pc + i];
-            *reinterpret_cast<uint4*>(vt + (sh * 64 + d) * lp + p) = u;
-        }
-    }
-}
-
 // Simple online-softmax attention: one thread per query row, K/V tiles of 64
 // keys staged in shared memory.  Used for fp32 compute and as the first
 // correct path; the tensor-core kernel replaces it for 16-bit dtypes.
@@ -576,19 +538,6 @@ void rope_scatter(const void* qkv, int64_t M, int H, int dh, const float* cos_t,
     MBR_CUDA(cudaGetLastError());
 }
 
-void scatter_vt(const void* qkv, int64_t M, int H, int mode, int NB, int T, void* vt, int dtype, cudaStream_t st) {
-    MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "scatter_vt: 16-bit only");
-    const int L = mode == SEQ_TIME ? T : NB;
-    const int64_t lp = round_up(L, 8);
-    const int64_t nsh = M / L * H;
-    dim3 grid((unsigned)ceil_div(lp, 32), (unsigned)nsh);
-    if (dtype == DT_F16)
-        scatter_vt_kernel<__half><<<grid, 256, 0, st>>>((const __half*)qkv, H, mode, NB, T, L, lp, (__half*)vt);
-    else
-        scatter_vt_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)qkv, H, mode, NB, T, L, lp,
-                                                               (__nv_bfloat16*)vt);
-    MBR_CUDA(cudaGetLastError());
-}
 
 void attention_simt(const void* q, const void* k, const void* v, int64_t nseq, int H, int L, int dh, float scale,
                     const float* gates, int mode, int NB, int T, void* merged, int dtype, cudaStream_t st) {

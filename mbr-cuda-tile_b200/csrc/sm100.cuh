@@ -99,12 +99,27 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor of tcgen05.mma kind::f16 with fp32 accumulation,
-// both operands K-major.  ab_bf16 selects bf16 (else fp16) for A and B.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool ab_bf16) {
+// Shared-memory matrix descriptor for an MN-major operand tile with the
+// 128-byte swizzle: rows are K (128 bytes = 64 16-bit MN elements each), 8-row
+// K groups 1024 bytes apart.  Valid for an MN extent of 64 (one swizzle atom).
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3ffffu) >> 4);  // start address
+    d |= (uint64_t)1 << 16;                    // leading byte offset (next 64-wide MN atom; unused)
+    d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset: 8 K rows x 128 B
+    d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                    // layout: SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16 with fp32 accumulation.
+// ab_bf16 selects bf16 (else fp16) for A and B; A is K-major, B is K-major
+// unless b_mn_major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool ab_bf16, bool b_mn_major = false) {
     return (1u << 4)                          // D format: f32
            | ((ab_bf16 ? 1u : 0u) << 7)       // A format
            | ((ab_bf16 ? 1u : 0u) << 10)      // B format
+           | ((b_mn_major ? 1u : 0u) << 16)   // B major-ness
            | ((uint32_t)(N >> 3) << 17)       // N / 8
            | ((uint32_t)(M >> 4) << 24);      // M / 16
 }
