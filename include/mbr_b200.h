@@ -160,6 +160,63 @@ MBR_API int mbr_sync_check(mbr_handle* h);
 MBR_API int mbr_profile_enable(mbr_handle* h, int on);
 MBR_API int mbr_profile_read(mbr_handle* h, int kind, double* ms, int64_t* count);
 
+/* ---- stand-alone ops in the reference op library's layouts ------------
+ * All buffers are device memory; dtype is MBR_FP32 / MBR_FP16 / MBR_BF16;
+ * element counts of the elementwise ops are multiples of 8. */
+
+/* y = x * rsqrt(sum_d x^2 + 1e-12) * gamma * scale over rows of `dim`
+ * (x, y: dtype; gamma: fp32).  Replaces mbr_tile::rms_norm
+ * (src/mbr_cuda_tile.h:34; kernels src/mbr_cuda_tile.cu:4791-5091). */
+MBR_API int mbr_op_rms_norm(const void* d_x, const float* d_gamma, void* d_y, int64_t rows, int dim, float scale,
+                            int dtype, void* stream);
+
+/* y = a + b (residual add).  Replaces Tensor::add_ (src/tensor.h:117) and
+ * try_residual_add_bf16_cutile (src/mbr_residual_cutile.cu:71-94). */
+MBR_API int mbr_op_add(const void* d_a, const void* d_b, void* d_y, int64_t n, int dtype, void* stream);
+
+/* y = 0.5 x (1 + erf(x / sqrt 2)).  The activation of mbr_tile::linear_gelu
+ * (src/mbr_cuda_tile.h:78; the reference evaluates erf with polynomial fits,
+ * src/mbr_cuda_tile.cu:566-690). */
+MBR_API int mbr_op_gelu(const void* d_x, void* d_y, int64_t n, int dtype, void* stream);
+
+/* y[r][h*dh + d] = x[r][h*dh + d] * gate[r][h] (gate already sigmoid'ed).
+ * Replaces apply_gates_and_merge_heads (src/mbr_cuda_tile.h:29-30). */
+MBR_API int mbr_op_sigmoid_gate(const void* d_x, const void* d_gate, void* d_y, int64_t rows, int heads,
+                                int dim_head, int dtype, void* stream);
+
+/* RoPE over positions: x [seqs][L][heads][64], interleaved pairs (2i, 2i+1) of
+ * position p rotated by (d_cos, d_sin)[p][i] ([L][32] fp32).  Replaces the
+ * rotary part of split_qkv_heads_rotary (src/mbr_cuda_tile.h:8-10). */
+MBR_API int mbr_op_rope(const void* d_x, const float* d_cos, const float* d_sin, void* d_y, int64_t seqs, int L,
+                        int heads, int dtype, void* stream);
+
+/* Host tables of MelBandRoformer::compute_rotary_cos_sin
+ * (src/model_mel_band_roformer.cu:270-300): h_cos, h_sin [L][dim_head/2]. */
+MBR_API int mbr_rope_tables(int L, int dim_head, float* h_cos, float* h_sin);
+
+/* Band gather with the handle's band map: d_spec [B][C][1025][T] complex ->
+ * d_x [B][T][2J] (the stereo merge of src/model_mel_band_roformer.cu:714-725
+ * folded in).  Replaces gather_freqs_fold_complex (src/mbr_cuda_tile.h:12). */
+MBR_API int mbr_op_band_gather(mbr_handle* h, const float* d_spec, int B, int T, void* d_x, int dtype,
+                               void* stream);
+
+/* Mask scatter-average with the handle's band map: d_masks [S][B*T][2J]
+ * (dtype), d_spec [B][C][1025][T] complex -> d_out [B][S][C][1025][T]
+ * complex (fp32).  Replaces apply_mask_and_scatter (src/mbr_cuda_tile.h:230-242). */
+MBR_API int mbr_op_mask_scatter(mbr_handle* h, const float* d_spec, const void* d_masks, int B, int S, int T,
+                                float* d_out, int dtype, void* stream);
+
+/* STFT (n_fft 2048, periodic Hann, center reflect pad, onesided):
+ * d_sig [n][L] -> d_spec [n][1025][T][2], T = L / hop + 1.  Replaces
+ * stft_tile::stft (src/stft_cuda_tile.h:9-15). */
+MBR_API int mbr_op_stft(const float* d_sig, int64_t n, int64_t L, int hop, float* d_spec, void* stream);
+
+/* iSTFT: d_spec [n][1025][T][2] -> d_out [n][lout], lout = length > 0 ? length
+ * : (T - 1) * hop.  Its n*T*2048-float frame scratch comes from the
+ * stream-ordered allocator.  Replaces stft_tile::istft (src/stft_cuda_tile.h:17-24). */
+MBR_API int mbr_op_istft(const float* d_spec, int64_t n, int T, int hop, int64_t length, float* d_out,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,6 +1,7 @@
 // capi.cpp — extern "C" boundary (include/mbr_b200.h).  No C++ exception crosses it.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <memory>
 #include <string>
 #include <thread>
@@ -9,6 +10,7 @@
 #include "../../include/mbr_b200.h"
 #include "common.h"
 #include "model.h"
+#include "ops_api.h"
 #include "separator.h"
 #include "weights.h"
 
@@ -343,6 +345,102 @@ MBR_API int mbr_profile_read(mbr_handle* h, int kind, double* ms, int64_t* count
     return guard([&] {
         need(h && ms && count, "null argument");
         h->model->profile_read(kind, ms, count);
+    });
+}
+
+// ---- stand-alone ops ----
+MBR_API int mbr_op_rms_norm(const void* d_x, const float* d_gamma, void* d_y, int64_t rows, int dim, float scale,
+                            int dtype, void* stream) {
+    return guard([&] {
+        need(d_x && d_gamma && d_y && rows >= 0, "bad argument");
+        if (rows > 0) mbr::opsapi::rms_norm(d_x, d_gamma, d_y, rows, dim, scale, dtype, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_op_add(const void* d_a, const void* d_b, void* d_y, int64_t n, int dtype, void* stream) {
+    return guard([&] {
+        need(d_a && d_b && d_y && n >= 0, "bad argument");
+        if (n > 0) mbr::opsapi::add(d_a, d_b, d_y, n, dtype, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_op_gelu(const void* d_x, void* d_y, int64_t n, int dtype, void* stream) {
+    return guard([&] {
+        need(d_x && d_y && n >= 0, "bad argument");
+        if (n > 0) mbr::opsapi::gelu(d_x, d_y, n, dtype, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_op_sigmoid_gate(const void* d_x, const void* d_gate, void* d_y, int64_t rows, int heads,
+                                int dim_head, int dtype, void* stream) {
+    return guard([&] {
+        need(d_x && d_gate && d_y && rows >= 0 && heads > 0 && dim_head > 0, "bad argument");
+        if (rows > 0) mbr::opsapi::sigmoid_gate(d_x, d_gate, d_y, rows, heads, dim_head, dtype, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_op_rope(const void* d_x, const float* d_cos, const float* d_sin, void* d_y, int64_t seqs, int L,
+                        int heads, int dtype, void* stream) {
+    return guard([&] {
+        need(d_x && d_cos && d_sin && d_y && seqs >= 0 && L > 0 && heads > 0, "bad argument");
+        if (seqs > 0) mbr::opsapi::rope(d_x, d_cos, d_sin, d_y, seqs, L, heads, dtype, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_rope_tables(int L, int dim_head, float* h_cos, float* h_sin) {
+    return guard([&] {
+        need(h_cos && h_sin && L > 0 && dim_head > 0 && dim_head % 2 == 0, "bad argument");
+        std::vector<float> cs, sn;
+        mbr::rotary_tables(L, dim_head, cs, sn);
+        std::copy(cs.begin(), cs.end(), h_cos);
+        std::copy(sn.begin(), sn.end(), h_sin);
+    });
+}
+
+MBR_API int mbr_op_band_gather(mbr_handle* h, const float* d_spec, int B, int T, void* d_x, int dtype,
+                               void* stream) {
+    return guard([&] {
+        need(h && d_spec && d_x && B > 0 && T > 0, "bad argument");
+        MBR_CUDA(cudaSetDevice(h->device));
+        mbr::opsapi::band_gather((const float2*)d_spec, B, h->model->channels(), 1025, T, h->model->d_freq_indices(),
+                                 h->model->band_freqs(), d_x, dtype, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_op_mask_scatter(mbr_handle* h, const float* d_spec, const void* d_masks, int B, int S, int T,
+                                float* d_out, int dtype, void* stream) {
+    return guard([&] {
+        need(h && d_spec && d_masks && d_out && B > 0 && S > 0 && T > 0, "bad argument");
+        MBR_CUDA(cudaSetDevice(h->device));
+        mbr::opsapi::mask_scatter((const float2*)d_spec, d_masks, B, S, h->model->channels(), 1025, T,
+                                  h->model->d_rev_off(), h->model->d_rev_idx(), h->model->d_bands_per_freq(),
+                                  h->model->band_freqs(), (float2*)d_out, dtype, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_op_stft(const float* d_sig, int64_t n, int64_t L, int hop, float* d_spec, void* stream) {
+    return guard([&] {
+        need(d_sig && d_spec && n > 0, "bad argument");
+        mbr::opsapi::stft(d_sig, n, L, hop, (float2*)d_spec, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_op_istft(const float* d_spec, int64_t n, int T, int hop, int64_t length, float* d_out,
+                         void* stream) {
+    return guard([&] {
+        need(d_spec && d_out && n > 0 && T > 0 && hop > 0, "bad argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        int64_t lout = length > 0 ? length : (int64_t)(T - 1) * hop;
+        need(lout > 0, "empty output");
+        float* frames = nullptr;
+        MBR_CUDA(cudaMallocAsync((void**)&frames, sizeof(float) * (size_t)n * T * 2048, st));
+        try {
+            mbr::opsapi::istft((const float2*)d_spec, n, T, hop, frames, lout, d_out, st);
+        } catch (...) {
+            cudaFreeAsync(frames, st);
+            throw;
+        }
+        MBR_CUDA(cudaFreeAsync(frames, st));
     });
 }
 

@@ -77,6 +77,8 @@ std::vector<float> to_floats(const HostTensor& t) {
     return v;
 }
 
+}  // namespace
+
 // compute_rotary_cos_sin (src/model_mel_band_roformer.cu:270-300), fp32 host math.
 void rotary_tables(int n, int dim, std::vector<float>& cs, std::vector<float>& sn) {
     int half = dim / 2;
@@ -90,8 +92,6 @@ void rotary_tables(int n, int dim, std::vector<float>& cs, std::vector<float>& s
             sn[(size_t)p * half + i] = std::sin(ang);
         }
 }
-
-}  // namespace
 
 MelBandRoformer::MelBandRoformer(const ModelWeights& w, int device, int dtype) : device_(device), dtype_(dtype) {
     MBR_CHECK(dtype == DT_F32 || dtype == DT_F16 || dtype == DT_BF16, "dtype must be fp32, fp16 or bf16");

@@ -50,6 +50,10 @@ struct MBRConfig {
     static MBRConfig from_json(const JsonValue& j);
 };
 
+// Rotary cos/sin tables [n][dim/2] exactly as compute_rotary_cos_sin
+// (src/model_mel_band_roformer.cu:270-300): fp32 host arithmetic.
+void rotary_tables(int n, int dim, std::vector<float>& cs, std::vector<float>& sn);
+
 // Kernel backends selectable per model (the tensor-core path is the default for
 // fp16/bf16; the CUDA-core path is the fp32 path and a cross-check).
 enum Backend { BACKEND_SIMT = 0, BACKEND_TC = 1 };
@@ -88,6 +92,11 @@ public:
     int dtype() const { return dtype_; }
     int channels() const { return C_; }
     int64_t band_freqs() const { return J_; }
+    // device band maps (for the stand-alone band ops)
+    const int* d_freq_indices() const { return d_fi_; }
+    const int* d_rev_off() const { return d_rev_off_; }
+    const int* d_rev_idx() const { return d_rev_idx_; }
+    const float* d_bands_per_freq() const { return d_nbpf_; }
     int64_t frames(int64_t L) const;      // STFT frames T of an L-sample input
     int64_t out_length(int64_t L) const;  // output samples of an L-sample input
 

@@ -1,0 +1,38 @@
+// ops_api.h — stand-alone ops in the reference op library's layouts
+// (mbr_tile / stft_tile, src/mbr_cuda_tile.h:6-257, src/stft_cuda_tile.h:5-26).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mbr {
+namespace opsapi {
+
+// y = a + b (n % 8 == 0)
+void add(const void* a, const void* b, void* y, int64_t n, int dtype, cudaStream_t st);
+// y = gelu(x) with the exact erf form (n % 8 == 0)
+void gelu(const void* x, void* y, int64_t n, int dtype, cudaStream_t st);
+// y[r][h*dh + d] = x[r][h*dh + d] * g[r][h]
+void sigmoid_gate(const void* x, const void* g, void* y, int64_t rows, int H, int dh, int dtype, cudaStream_t st);
+// y = x * rsqrt(sum x^2 + 1e-12) * gamma * scale per row of D
+void rms_norm(const void* x, const float* gamma, void* y, int64_t rows, int D, float scale, int dtype,
+              cudaStream_t st);
+// x [seqs][L][H][64] rotated by cos/sin [L][32] (interleaved pairs)
+void rope(const void* x, const float* cs, const float* sn, void* y, int64_t seqs, int L, int H, int dtype,
+          cudaStream_t st);
+// spec [B][C][F][T] complex -> x [B][T][2J]
+void band_gather(const float2* spec, int B, int C, int F, int T, const int* fi, int64_t J, void* x, int dtype,
+                 cudaStream_t st);
+// masks [S][B*T][2J] (dtype), spec [B][C][F][T] complex -> out [B][S][C][F][T] complex
+void mask_scatter(const float2* spec, const void* masks, int B, int S, int C, int F, int T, const int* rev_off,
+                  const int* rev_idx, const float* nbpf, int64_t J, float2* out, int dtype, cudaStream_t st);
+// STFT frames of an L-sample signal (center, reflect pad n_fft/2)
+int64_t stft_frames(int64_t L, int hop);
+// sig [n][L] -> out [n][1025][T] complex (n_fft 2048, periodic Hann, onesided)
+void stft(const float* sig, int64_t nsig, int64_t L, int hop, float2* out, cudaStream_t st);
+// spec [n][1025][T] complex -> out [n][lout]; frames is scratch of n*T*2048 floats
+void istft(const float2* spec, int64_t nsig, int T, int hop, float* frames, int64_t lout, float* out,
+           cudaStream_t st);
+
+}  // namespace opsapi
+}  // namespace mbr

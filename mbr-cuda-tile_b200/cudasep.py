@@ -29,6 +29,8 @@ EXPORTS = [
     "mbr_forward_chunk", "mbr_forward_tap", "mbr_separate_device", "mbr_separate", "mbr_shard_info",
     "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_backend", "mbr_last_launches",
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
+    "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_rope_tables",
+    "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft",
 ]
 
 # Kernel classes of mbr_profile_read.
@@ -73,6 +75,16 @@ def lib():
         L.mbr_sync_check.argtypes = [vp]
         L.mbr_profile_enable.argtypes = [vp, c_int]
         L.mbr_profile_read.argtypes = [vp, c_int, ctypes.POINTER(ctypes.c_double), i64p]
+        L.mbr_op_rms_norm.argtypes = [fp, fp, fp, i64, c_int, c_float, c_int, vp]
+        L.mbr_op_add.argtypes = [fp, fp, fp, i64, c_int, vp]
+        L.mbr_op_gelu.argtypes = [fp, fp, i64, c_int, vp]
+        L.mbr_op_sigmoid_gate.argtypes = [fp, fp, fp, i64, c_int, c_int, c_int, vp]
+        L.mbr_op_rope.argtypes = [fp, fp, fp, fp, i64, c_int, c_int, c_int, vp]
+        L.mbr_rope_tables.argtypes = [c_int, c_int, fp, fp]
+        L.mbr_op_band_gather.argtypes = [vp, fp, c_int, c_int, fp, c_int, vp]
+        L.mbr_op_mask_scatter.argtypes = [vp, fp, fp, c_int, c_int, c_int, fp, c_int, vp]
+        L.mbr_op_stft.argtypes = [fp, i64, i64, c_int, fp, vp]
+        L.mbr_op_istft.argtypes = [fp, i64, c_int, c_int, i64, fp, vp]
         _lib = L
     return _lib
 
@@ -94,6 +106,90 @@ def _stream(stream):
         import torch
         return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     return ctypes.c_void_p(stream if isinstance(stream, int) else stream.cuda_stream)
+
+
+def _dt(t) -> int:
+    """C-ABI dtype code of a torch tensor."""
+    import torch
+
+    return {torch.float32: FP32, torch.float16: FP16, torch.bfloat16: BF16}[t.dtype]
+
+
+# ---- stand-alone ops (device tensors; reference op-library layouts) ----
+def op_rms_norm(x, gamma, scale, y=None, stream=None):
+    import torch
+
+    y = torch.empty_like(x) if y is None else y
+    rows, dim = x.shape[0], x.shape[-1]
+    rows = x.numel() // dim
+    _check(lib().mbr_op_rms_norm(_ptr(x), _ptr(gamma), _ptr(y), rows, dim, float(scale), _dt(x), _stream(stream)))
+    return y
+
+
+def op_add(a, b, y=None, stream=None):
+    import torch
+
+    y = torch.empty_like(a) if y is None else y
+    _check(lib().mbr_op_add(_ptr(a), _ptr(b), _ptr(y), a.numel(), _dt(a), _stream(stream)))
+    return y
+
+
+def op_gelu(x, y=None, stream=None):
+    import torch
+
+    y = torch.empty_like(x) if y is None else y
+    _check(lib().mbr_op_gelu(_ptr(x), _ptr(y), x.numel(), _dt(x), _stream(stream)))
+    return y
+
+
+def op_sigmoid_gate(x, gate, heads, y=None, stream=None):
+    """x [rows, heads*dh], gate [rows, heads] -> x * gate (broadcast over dh)."""
+    import torch
+
+    y = torch.empty_like(x) if y is None else y
+    rows = gate.numel() // heads
+    dh = x.numel() // (rows * heads)
+    _check(lib().mbr_op_sigmoid_gate(_ptr(x), _ptr(gate), _ptr(y), rows, heads, dh, _dt(x), _stream(stream)))
+    return y
+
+
+def rope_tables(L: int, dim_head: int = 64):
+    c = np.empty((L, dim_head // 2), np.float32)
+    s = np.empty((L, dim_head // 2), np.float32)
+    _check(lib().mbr_rope_tables(L, dim_head, _ptr(c), _ptr(s)))
+    return c, s
+
+
+def op_rope(x, cos_t, sin_t, y=None, stream=None):
+    """x [seqs, L, heads, 64] rotated by position."""
+    import torch
+
+    y = torch.empty_like(x) if y is None else y
+    seqs, L, heads = x.shape[0], x.shape[1], x.shape[2]
+    _check(lib().mbr_op_rope(_ptr(x), _ptr(cos_t), _ptr(sin_t), _ptr(y), seqs, L, heads, _dt(x), _stream(stream)))
+    return y
+
+
+def op_stft(sig, hop=441, stream=None):
+    """sig [n, L] float32 CUDA -> [n, 1025, T, 2]."""
+    import torch
+
+    n, L = sig.shape
+    T = L // hop + 1
+    out = torch.empty((n, 1025, T, 2), dtype=torch.float32, device=sig.device)
+    _check(lib().mbr_op_stft(_ptr(sig), n, L, hop, _ptr(out), _stream(stream)))
+    return out
+
+
+def op_istft(spec, hop=441, length=-1, stream=None):
+    """spec [n, 1025, T, 2] float32 CUDA -> [n, lout]."""
+    import torch
+
+    n, _, T, _ = spec.shape
+    lout = length if length > 0 else (T - 1) * hop
+    out = torch.empty((n, lout), dtype=torch.float32, device=spec.device)
+    _check(lib().mbr_op_istft(_ptr(spec), n, T, hop, length, _ptr(out), _stream(stream)))
+    return out
 
 
 class Model:
@@ -198,6 +294,28 @@ class Model:
         if out is None:
             out = np.empty((S, C, N), dtype=np.float32)
         _check(lib().mbr_separate(self.h, _ptr(track), N, float(overlap), int(chunk_batch), int(n_gpus), _ptr(out)))
+        return out
+
+    # ---- band ops with this checkpoint's band map ----
+    def op_band_gather(self, spec, out_dtype=None, stream=None):
+        """spec [B, C, 1025, T, 2] float32 -> [B, T, 2J]."""
+        import torch
+
+        B, C, F, T, _ = spec.shape
+        J = self.info("band_freqs")
+        out = torch.empty((B, T, 2 * J), dtype=out_dtype or torch.float32, device=spec.device)
+        _check(lib().mbr_op_band_gather(self.h, _ptr(spec), B, T, _ptr(out), _dt(out), _stream(stream)))
+        return out
+
+    def op_mask_scatter(self, spec, masks, stream=None):
+        """spec [B, C, 1025, T, 2] float32, masks [S, B*T, 2J] -> [B, S, C, 1025, T, 2]."""
+        import torch
+
+        B, C, F, T, _ = spec.shape
+        S = masks.shape[0]
+        out = torch.empty((B, S, C, F, T, 2), dtype=torch.float32, device=spec.device)
+        _check(lib().mbr_op_mask_scatter(self.h, _ptr(spec), _ptr(masks), B, S, T, _ptr(out), _dt(masks),
+                                         _stream(stream)))
         return out
 
     # ---- sharded (one process per GPU) ----

@@ -1,0 +1,176 @@
+"""GPU parity of the stand-alone op entry points (the reference op library's
+ops, BASELINE op-sweep shapes) against CPU references.
+
+Inputs are seeded N(0, 1) activations of shape [B*801*60, D].  The CPU
+reference evaluates in fp64 from the same (already rounded) inputs; tolerances:
+fp32 max abs err <= 1e-5 * max|ref| (+1e-6), fp16 <= 2^-10 relative to the
+output magnitude, bf16 <= 2^-7 (one rounding of the output).  STFT / iSTFT are
+checked against the CPU oracle; band gather / mask scatter bit-exact (gather)
+and 1e-6 relative (scatter) against numpy on the checkpoint's band map.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+T = 801
+NB = 60
+TOL = {"fp32": 1e-5, "fp16": 2.0 ** -10, "bf16": 2.0 ** -7}
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def _tdt(torch, name):
+    return {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}[name]
+
+
+def _inputs(torch, rows, D, dtype, seed=0, n=1):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(rows, D, generator=g).to(_tdt(torch, dtype)) for _ in range(n)]
+
+
+def _close(got, ref, dtype, what):
+    got = got.double().cpu().numpy() if hasattr(got, "cpu") else np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    tol = TOL[dtype]
+    err = np.abs(got - ref)
+    bound = tol * np.maximum(np.abs(ref), 1.0) * 1.01 + (1e-6 if dtype == "fp32" else 0)
+    assert np.all(err <= bound), f"{what}/{dtype}: max err {err.max():.3e}"
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "fp16", "bf16"])
+@pytest.mark.parametrize("D", [192, 384, 512])
+def test_rms_norm_add_gelu(torch_cuda, dtype, D):
+    torch = torch_cuda
+    import cudasep
+
+    rows = 1 * T * NB
+    x, y = _inputs(torch, rows, D, dtype, seed=D, n=2)
+    gamma = torch.linspace(0.5, 1.5, D)
+    scale = float(np.sqrt(np.float32(D)))
+    xd, yd, gd = x.cuda(), y.cuda(), gamma.cuda()
+    xr = x.double().numpy()
+    ref = xr / np.sqrt((xr ** 2).sum(-1, keepdims=True) + 1e-12) * gamma.double().numpy() * scale
+    _close(cudasep.op_rms_norm(xd, gd, scale), ref, dtype, "rms_norm")
+    _close(cudasep.op_add(xd, yd), xr + y.double().numpy(), dtype, "add")
+    from scipy.special import erf
+
+    _close(cudasep.op_gelu(xd), 0.5 * xr * (1 + erf(xr / np.sqrt(2))), dtype, "gelu")
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "fp16", "bf16"])
+def test_sigmoid_gate_and_rope(torch_cuda, dtype):
+    torch = torch_cuda
+    import cudasep
+
+    H = 8
+    rows = T * NB
+    (x,) = _inputs(torch, rows, H * 64, dtype, seed=5)
+    g = torch.sigmoid(torch.randn(rows, H, generator=torch.Generator().manual_seed(6))).to(x.dtype)
+    ref = x.double().numpy().reshape(rows, H, 64) * g.double().numpy()[:, :, None]
+    _close(cudasep.op_sigmoid_gate(x.cuda(), g.cuda(), H), ref.reshape(rows, -1), dtype, "gate")
+    # RoPE over T: x viewed as [60 sequences][T][H][64]
+    c, s = cudasep.rope_tables(T, 64)
+    xs = x.reshape(NB, T, H, 64)
+    got = cudasep.op_rope(xs.cuda(), torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda())
+    xr = xs.double().numpy()
+    x0, x1 = xr[..., 0::2], xr[..., 1::2]
+    cc, ss = c.astype(np.float64)[None, :, None, :], s.astype(np.float64)[None, :, None, :]
+    ref = np.empty_like(xr)
+    ref[..., 0::2] = x0 * cc - x1 * ss
+    ref[..., 1::2] = x0 * ss + x1 * cc
+    _close(got, ref, dtype, "rope")
+
+
+def test_rope_tables_match_reference_formula():
+    import cudasep
+
+    c, s = cudasep.rope_tables(801, 64)
+    # compute_rotary_cos_sin: fp32 freq = 1 / 10000^(2i/dim), angle = n * freq (fp32)
+    i = np.arange(32, dtype=np.float32)
+    freq = (np.float32(1.0) / np.power(np.float32(10000.0), (2 * i).astype(np.float32) / np.float32(64))).astype(
+        np.float32)
+    ang = (np.arange(801, dtype=np.float32)[:, None] * freq[None, :]).astype(np.float32)
+    assert np.abs(c - np.cos(ang.astype(np.float64))).max() < 2e-7
+    assert np.abs(s - np.sin(ang.astype(np.float64))).max() < 2e-7
+
+
+def test_stft_istft_match_oracle(torch_cuda):
+    torch = torch_cuda
+    import cudasep
+    import oracle
+
+    rng = np.random.default_rng(3)
+    x = rng.uniform(-0.5, 0.5, (3, 44100 + 123)).astype(np.float32)
+    S = cudasep.op_stft(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = oracle.stft(x)
+    assert S.shape == ref.shape
+    assert np.abs(S - ref).max() <= 1e-5 * np.abs(ref).max()
+    y = cudasep.op_istft(torch.from_numpy(ref).cuda()).cpu().numpy()
+    yr = oracle.istft(ref)
+    assert y.shape == yr.shape
+    assert np.abs(y - yr).max() <= 1e-5
+    y2 = cudasep.op_istft(torch.from_numpy(ref).cuda(), length=x.shape[1]).cpu().numpy()
+    assert y2.shape == x.shape and np.abs(y2[:, : yr.shape[1]] - yr).max() <= 1e-5
+
+
+@pytest.mark.parametrize("B,dtype", [(1, "fp32"), (2, "fp16"), (1, "bf16")])
+def test_band_gather_and_mask_scatter(torch_cuda, make_csm, B, dtype):
+    torch = torch_cuda
+    import csm_tool
+    import cudasep
+
+    path = make_csm("tiny", seed=31)
+    _, t = csm_tool.read_csm(path)
+    fi = t["__precomputed__.freq_indices"]
+    nbpf = t["__precomputed__.num_bands_per_freq"]
+    J = fi.shape[0]
+    m = cudasep.Model(path, 0, "fp32")
+    rng = np.random.default_rng(B)
+    spec = rng.standard_normal((B, 2, 1025, T, 2)).astype(np.float32)
+    xd = m.op_band_gather(torch.from_numpy(spec).cuda(), out_dtype=_tdt(torch, dtype))
+    ch, f = fi % 2, fi // 2
+    ref = spec[:, ch, f, :, :].transpose(0, 2, 1, 3).reshape(B, T, 2 * J)
+    assert np.array_equal(xd.float().cpu().numpy(), torch.from_numpy(ref).to(_tdt(torch, dtype)).float().numpy())
+    # mask scatter-average, S = 2
+    S = 2
+    masks = torch.from_numpy(rng.standard_normal((S, B * T, 2 * J)).astype(np.float32)).to(_tdt(torch, dtype))
+    got = m.op_mask_scatter(torch.from_numpy(spec).cuda(), masks.cuda()).cpu().numpy()
+    mk = masks.double().numpy().reshape(S, B, T, J, 2)
+    sc = spec.astype(np.float64)[..., 0] + 1j * spec.astype(np.float64)[..., 1]  # [B, 2, F, T]
+    mc = mk[..., 0] + 1j * mk[..., 1]  # [S, B, T, J]
+    out = np.zeros((B, S, 2, 1025, T), np.complex128)
+    for j in range(J):
+        c, fr = fi[j] % 2, fi[j] // 2
+        out[:, :, c, fr, :] += (sc[:, None, c, fr, :] * mc[:, :, :, j].transpose(1, 0, 2)) / nbpf[fr]
+    ref = np.stack([out.real, out.imag], -1)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_full_size_sweep_properties(torch_cuda, dtype):
+    """BASELINE's largest sweep shape (B = 8, D = 512): add then subtract returns
+    the input (to one rounding), RMSNorm rows have RMS == gamma-weighted scale."""
+    torch = torch_cuda
+    import cudasep
+
+    rows, D = 8 * T * NB, 512
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(rows, D, generator=g, device="cuda").to(_tdt(torch, dtype))
+    y = torch.randn(rows, D, generator=g, device="cuda").to(_tdt(torch, dtype))
+    s = cudasep.op_add(x, y)
+    assert torch.isfinite(s.float()).all()
+    back = cudasep.op_add(s, (-y).contiguous())
+    tol = TOL[dtype] * 4
+    assert ((back.float() - x.float()).abs() <= tol * (x.float().abs() + y.float().abs() + 1)).all()
+    gamma = torch.ones(D, device="cuda")
+    n = cudasep.op_rms_norm(x, gamma, 1.0)
+    nrm = n.float().pow(2).sum(-1).sqrt()
+    assert ((nrm - 1).abs() < 8 * TOL[dtype]).all()
