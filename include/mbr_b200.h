@@ -217,6 +217,27 @@ MBR_API int mbr_op_stft(const float* d_sig, int64_t n, int64_t L, int hop, float
 MBR_API int mbr_op_istft(const float* d_spec, int64_t n, int T, int hop, int64_t length, float* d_out,
                          void* stream);
 
+/* iSTFT that allocates no device memory; same arguments and result as
+ * mbr_op_istft.  No counterpart in the reference: it is for callers that may
+ * not call cudaMalloc or the stream-ordered allocator at run time, such as a
+ * real-time audio host whose processing thread must not block on an allocator
+ * (cudaMalloc can synchronise the device) or a service that reserves all GPU
+ * memory up front and forbids later allocations.
+ * Limits and rules:
+ *  - the frame scratch is a fixed 16 MiB array inside the library, so
+ *    n * T <= 2048 (e.g. one stereo 8 s chunk, 2 x 801 frames); larger calls
+ *    fail with MBR_ERR_INVALID.  Every GPU that loads the library holds this
+ *    array until the process exits.
+ *  - the first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - all calls share the one array: calls whose work overlaps on the GPU
+ *    (different streams without ordering, or different host threads) race.
+ *    Every frame the call reads is written by the same call first, so nothing
+ *    needs clearing between calls. */
+MBR_API int mbr_op_istft_noalloc(const float* d_spec, int64_t n, int T, int hop, int64_t length, float* d_out,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

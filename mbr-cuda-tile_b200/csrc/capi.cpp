@@ -444,4 +444,23 @@ MBR_API int mbr_op_istft(const float* d_spec, int64_t n, int T, int hop, int64_t
     });
 }
 
+// Same result as mbr_op_istft, for callers that must not allocate device
+// memory: the frame scratch is a fixed array compiled into the library (see
+// the header for the limits and the sharing rules).
+MBR_API int mbr_op_istft_noalloc(const float* d_spec, int64_t n, int T, int hop, int64_t length, float* d_out,
+                                 void* stream) {
+    return guard([&] {
+        need(d_spec && d_out && n > 0 && T > 0 && hop > 0, "bad argument");
+        int64_t lout = length > 0 ? length : (int64_t)(T - 1) * hop;
+        need(lout > 0, "empty output");
+        if (n * (int64_t)T * 2048 > mbr::opsapi::kIstftStaticFloats)
+            throw mbr::Error(MBR_ERR_INVALID,
+                             "mbr_op_istft_noalloc: n * T = " + std::to_string(n * (int64_t)T) +
+                                 " frames exceeds the static scratch of " +
+                                 std::to_string(mbr::opsapi::kIstftStaticFloats / 2048) + " frames");
+        float* frames = mbr::opsapi::istft_static_scratch();
+        mbr::opsapi::istft((const float2*)d_spec, n, T, hop, frames, lout, d_out, (cudaStream_t)stream);
+    });
+}
+
 }  // extern "C"

@@ -4,6 +4,8 @@
 // mask scatter-average, STFT and iSTFT.  Memory-bound kernels: 16-byte
 // vectorised, coalesced, one pass over HBM, reductions in registers.
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "common.cuh"
 #include "ops_api.h"
@@ -320,7 +322,30 @@ unsigned grid_for(int64_t work, int threads) {
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>(nblk(work, threads), (int64_t)sm_count() * 16));
 }
 
+// Frame scratch of the allocation-free iSTFT entry point: a fixed 16 MiB array
+// that every device loading this library reserves for the life of the process.
+__device__ __align__(256) float g_istft_frames[kIstftStaticFloats];
+
 }  // namespace
+
+float* istft_static_scratch() {
+    // Host code cannot take the array's address directly (the symbol is a host
+    // stand-in); ask the runtime once per device, with that device current.
+    static std::mutex mu;
+    static float* ptrs[kMaxDevices] = {};
+    int dev = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    MBR_CHECK(dev >= 0 && dev < kMaxDevices, "device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_istft_frames);
+        if (e != cudaSuccess)
+            throw Error(ERR_CUDA, std::string("cudaGetSymbolAddress(istft scratch) failed: ") + cudaGetErrorString(e));
+        ptrs[dev] = (float*)p;
+    }
+    return ptrs[dev];
+}
 
 void add(const void* a, const void* b, void* y, int64_t n, int dtype, cudaStream_t st) {
     MBR_CHECK(n % 8 == 0, "add: element count must be a multiple of 8");

@@ -34,5 +34,13 @@ void stft(const float* sig, int64_t nsig, int64_t L, int hop, float2* out, cudaS
 void istft(const float2* spec, int64_t nsig, int T, int hop, float* frames, int64_t lout, float* out,
            cudaStream_t st);
 
+// Size of the file-scope frame scratch of the allocation-free iSTFT: 16 MiB,
+// i.e. n * T <= 2048 frames of 2048 samples per call.
+constexpr int64_t kIstftStaticFloats = (int64_t)4 << 20;
+constexpr int kMaxDevices = 64;
+// Device address of that scratch on the current device (looked up once per
+// device with cudaGetSymbolAddress).
+float* istft_static_scratch();
+
 }  // namespace opsapi
 }  // namespace mbr

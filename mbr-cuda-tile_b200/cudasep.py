@@ -30,7 +30,7 @@ EXPORTS = [
     "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_backend", "mbr_last_launches",
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
     "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_rope_tables",
-    "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft",
+    "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft", "mbr_op_istft_noalloc",
 ]
 
 # Kernel classes of mbr_profile_read.
@@ -85,6 +85,7 @@ def lib():
         L.mbr_op_mask_scatter.argtypes = [vp, fp, fp, c_int, c_int, c_int, fp, c_int, vp]
         L.mbr_op_stft.argtypes = [fp, i64, i64, c_int, fp, vp]
         L.mbr_op_istft.argtypes = [fp, i64, c_int, c_int, i64, fp, vp]
+        L.mbr_op_istft_noalloc.argtypes = [fp, i64, c_int, c_int, i64, fp, vp]
         _lib = L
     return _lib
 
@@ -189,6 +190,16 @@ def op_istft(spec, hop=441, length=-1, stream=None):
     lout = length if length > 0 else (T - 1) * hop
     out = torch.empty((n, lout), dtype=torch.float32, device=spec.device)
     _check(lib().mbr_op_istft(_ptr(spec), n, T, hop, length, _ptr(out), _stream(stream)))
+    return out
+
+
+def op_istft_noalloc(spec, out, hop=441, length=-1, stream=None):
+    """Allocation-free iSTFT for callers that must not allocate device memory:
+    spec [n, 1025, T, 2] and the caller's out [n, lout] (float32, CUDA).  Its
+    frame scratch is a fixed 16 MiB array inside the library (n * T <= 2048);
+    calls that overlap on the GPU share that array and race."""
+    n, _, T, _ = spec.shape
+    _check(lib().mbr_op_istft_noalloc(_ptr(spec), n, T, hop, length, _ptr(out), _stream(stream)))
     return out
 
 
