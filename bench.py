@@ -250,10 +250,15 @@ def main():
     ap.add_argument("--workload", default="std", choices=sorted(WORKLOADS))
     ap.add_argument("--cpu-excerpt", type=float, default=1.0, help="seconds of audio in the CPU sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--single-chunk", action="store_true",
+                    help="profiling aid: run exactly warmup+steps forwards of one chunk batch and print their time "
+                         "(not the benchmark line)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return run_reference(args, wl)
+    if args.single_chunk:
+        return run_single_chunk(args, wl)
 
     import torch
 
@@ -426,6 +431,38 @@ def main():
         os.rmdir(tmpdir)
     except OSError:
         pass
+    return 0
+
+
+def run_single_chunk(args, wl):
+    """warmup + steps forwards of one chunk batch of the workload (for ncu)."""
+    import torch
+
+    import csm_tool
+    import cudasep
+
+    cfg = csm_tool.base_config(**csm_tool.PRESETS[wl["preset"]])
+    with tempfile.TemporaryDirectory() as d:
+        csm = os.path.join(d, "model.csm")
+        csm_tool.write_csm(csm, cfg, csm_tool.random_weights(cfg, 0))
+        m = cudasep.Model(csm, 0, wl["dtype"])
+        x = torch.from_numpy(np.stack([pink_noise(cfg["chunk_size"] / SR, 99 + i) for i in range(wl["chunk_batch"])]))
+        x = x.cuda().contiguous()
+        out = None
+        for _ in range(args.warmup):
+            out = m.forward(x, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            out = m.forward(x, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        m.sync_check()
+        print(json.dumps({"mode": "single_chunk", "workload": wl["desc"], "forwards": args.steps,
+                          "ms_per_forward": e0.elapsed_time(e1) / max(args.steps, 1),
+                          "launches_per_forward": m.last_launches()}), flush=True)
+        m.close()
     return 0
 
 
