@@ -125,6 +125,11 @@ MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float o
  * [out_lo, out_hi) it finalises.  Values are written to info[0..7] as
  * c0, c1, lo, hi, send_lo, out_lo, out_hi, n_chunks. */
 MBR_API int mbr_shard_info(mbr_handle* h, int64_t N, float overlap, int rank, int world, int64_t* info);
+/* The same shard plan without a handle or GPU (host arithmetic only), for a
+ * track of N samples, the checkpoint's chunk_size and default num_overlap:
+ * info[0..7] as in mbr_shard_info, info[8..10] = step, border, padded length. */
+MBR_API int mbr_plan_shard(int64_t N, int chunk_size, float overlap, int default_overlap, int rank, int world,
+                           int64_t* info);
 /* Runs the shard's chunks: d_acc [S*C][hi-lo], d_wsum [hi-lo] (overwritten). */
 MBR_API int mbr_shard_run(mbr_handle* h, const float* d_track, int64_t N, float overlap, int chunk_batch, int rank,
                           int world, float* d_acc, float* d_wsum, void* stream);

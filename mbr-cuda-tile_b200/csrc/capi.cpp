@@ -271,6 +271,19 @@ MBR_API int mbr_shard_info(mbr_handle* h, int64_t N, float overlap, int rank, in
     });
 }
 
+MBR_API int mbr_plan_shard(int64_t N, int chunk_size, float overlap, int default_overlap, int rank, int world,
+                           int64_t* info) {
+    return guard([&] {
+        need(info && N > 0 && chunk_size > 0, "bad argument");
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, chunk_size, overlap, default_overlap);
+        need(!p.single, "track fits one chunk: nothing to shard");
+        mbr::Shard s = mbr::make_shard(p, rank, world);
+        int64_t v[11] = {s.c0,     s.c1,     s.lo,     s.hi,     s.send_lo,
+                         s.out_lo, s.out_hi, (int64_t)p.starts.size(), p.step, p.border, p.total};
+        for (int i = 0; i < 11; ++i) info[i] = v[i];
+    });
+}
+
 MBR_API int mbr_shard_run(mbr_handle* h, const float* d_track, int64_t N, float overlap, int chunk_batch, int rank,
                           int world, float* d_acc, float* d_wsum, void* stream) {
     return guard([&] {

@@ -31,6 +31,7 @@ EXPORTS = [
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
     "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_rope_tables",
     "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft", "mbr_op_istft_noalloc",
+    "mbr_plan_shard",
 ]
 
 # Kernel classes of mbr_profile_read.
@@ -86,6 +87,7 @@ def lib():
         L.mbr_op_stft.argtypes = [fp, i64, i64, c_int, fp, vp]
         L.mbr_op_istft.argtypes = [fp, i64, c_int, c_int, i64, fp, vp]
         L.mbr_op_istft_noalloc.argtypes = [fp, i64, c_int, c_int, i64, fp, vp]
+        L.mbr_plan_shard.argtypes = [i64, c_int, c_float, c_int, c_int, c_int, i64p]
         _lib = L
     return _lib
 
@@ -191,6 +193,16 @@ def op_istft(spec, hop=441, length=-1, stream=None):
     out = torch.empty((n, lout), dtype=torch.float32, device=spec.device)
     _check(lib().mbr_op_istft(_ptr(spec), n, T, hop, length, _ptr(out), _stream(stream)))
     return out
+
+
+SHARD_KEYS = ["c0", "c1", "lo", "hi", "send_lo", "out_lo", "out_hi", "n_chunks", "step", "border", "total"]
+
+
+def plan_shard(N: int, chunk_size: int, overlap: float, default_overlap: int, rank: int, world: int) -> dict:
+    """Host-only shard plan (no GPU): chunk range and sample windows of `rank`."""
+    info = (ctypes.c_int64 * 11)()
+    _check(lib().mbr_plan_shard(int(N), int(chunk_size), float(overlap), int(default_overlap), rank, world, info))
+    return dict(zip(SHARD_KEYS, list(info)))
 
 
 def op_istft_noalloc(spec, out, hop=441, length=-1, stream=None):
