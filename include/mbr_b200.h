@@ -165,6 +165,15 @@ MBR_API int mbr_sync_check(mbr_handle* h);
 MBR_API int mbr_profile_enable(mbr_handle* h, int on);
 MBR_API int mbr_profile_read(mbr_handle* h, int kind, double* ms, int64_t* count);
 
+/* ---- WAV I/O (host only) -------------------------------------------------
+ * Replaces load_wav / save_wav (src/audio_io.h:14-18, src/audio_io.cpp:59-334):
+ * PCM 16/24/32-bit and float32 input (WAVE_FORMAT_EXTENSIBLE included),
+ * integer PCM scaled by 1/2^(bits-1); output is float32 WAV.  Samples are
+ * planar [channels][frames]. */
+MBR_API int mbr_wav_info(const char* path, int* sample_rate, int* channels, int64_t* frames);
+MBR_API int mbr_wav_read(const char* path, float* h_planar, int64_t capacity);
+MBR_API int mbr_wav_write(const char* path, const float* h_planar, int channels, int64_t frames, int sample_rate);
+
 /* ---- stand-alone ops in the reference op library's layouts ------------
  * All buffers are device memory; dtype is MBR_FP32 / MBR_FP16 / MBR_BF16;
  * element counts of the elementwise ops are multiples of 8. */

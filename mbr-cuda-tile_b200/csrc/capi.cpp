@@ -10,6 +10,7 @@
 #include "../../include/mbr_b200.h"
 #include "common.h"
 #include "model.h"
+#include "audio_io.h"
 #include "ops_api.h"
 #include "separator.h"
 #include "weights.h"
@@ -358,6 +359,33 @@ MBR_API int mbr_profile_read(mbr_handle* h, int kind, double* ms, int64_t* count
     return guard([&] {
         need(h && ms && count, "null argument");
         h->model->profile_read(kind, ms, count);
+    });
+}
+
+// ---- WAV I/O ----
+MBR_API int mbr_wav_info(const char* path, int* sample_rate, int* channels, int64_t* frames) {
+    return guard([&] {
+        need(path && sample_rate && channels && frames, "null argument");
+        cudasep::HostAudio a = cudasep::read_wav_host(path);
+        *sample_rate = a.sample_rate;
+        *channels = a.channels;
+        *frames = a.frames;
+    });
+}
+
+MBR_API int mbr_wav_read(const char* path, float* h_planar, int64_t capacity) {
+    return guard([&] {
+        need(path && h_planar, "null argument");
+        cudasep::HostAudio a = cudasep::read_wav_host(path);
+        need((int64_t)a.planar.size() <= capacity, "mbr_wav_read: buffer too small");
+        std::copy(a.planar.begin(), a.planar.end(), h_planar);
+    });
+}
+
+MBR_API int mbr_wav_write(const char* path, const float* h_planar, int channels, int64_t frames, int sample_rate) {
+    return guard([&] {
+        need(path && h_planar && channels > 0 && frames >= 0 && sample_rate > 0, "bad argument");
+        cudasep::write_wav_host(path, h_planar, channels, frames, sample_rate);
     });
 }
 
