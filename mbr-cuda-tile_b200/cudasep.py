@@ -31,7 +31,7 @@ EXPORTS = [
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
     "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_rope_tables",
     "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft", "mbr_op_istft_noalloc",
-    "mbr_plan_shard",
+    "mbr_plan_shard", "mbr_wav_info", "mbr_wav_read", "mbr_wav_write",
 ]
 
 # Kernel classes of mbr_profile_read.
@@ -88,6 +88,9 @@ def lib():
         L.mbr_op_istft.argtypes = [fp, i64, c_int, c_int, i64, fp, vp]
         L.mbr_op_istft_noalloc.argtypes = [fp, i64, c_int, c_int, i64, fp, vp]
         L.mbr_plan_shard.argtypes = [i64, c_int, c_float, c_int, c_int, c_int, i64p]
+        L.mbr_wav_info.argtypes = [ctypes.c_char_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), i64p]
+        L.mbr_wav_read.argtypes = [ctypes.c_char_p, fp, i64]
+        L.mbr_wav_write.argtypes = [ctypes.c_char_p, fp, c_int, i64, c_int]
         _lib = L
     return _lib
 
