@@ -63,6 +63,7 @@ extern "C" {
 /* kernel backends for mbr_set_backend */
 #define MBR_BACKEND_SIMT 0 /* CUDA-core kernels (fp32 path, cross-check) */
 #define MBR_BACKEND_TC 1   /* tcgen05 tensor-core kernels (fp16 / bf16) */
+#define MBR_BACKEND_TC_DIRECT 2 /* GEMMs only: tensor cores, epilogue stores from registers */
 
 typedef struct mbr_handle mbr_handle;
 

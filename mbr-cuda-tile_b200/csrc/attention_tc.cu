@@ -65,6 +65,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// 2^x with the hardware approximation (relative error ~2^-22; the
+// probabilities are rounded to 16 bits right after).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <typename T, bool PACK>
 __global__ void __launch_bounds__(160, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -207,43 +215,71 @@ __global__ void __launch_bounds__(160, 2)
                 break;
             }
             tc_fence_after();
-            // pass 1: row max of the valid keys
+            // valid key columns of this row in block j: [kbeg, kend) (warp-uniform)
+            int kbeg, kend;
+            if (PACK) {
+                kbeg = seg * 64;
+                kend = kbeg + min(L, 64);
+            } else {
+                kbeg = 0;
+                kend = min(KB, L - j * KB);
+            }
+            // pass 1: row max of the raw scores (the scale is positive)
             float mx = -INFINITY;
 #pragma unroll 1
             for (int c = 0; c < KB / 32; ++c) {
+                const int c0 = c * 32;
+                if (c0 + 32 <= kbeg || c0 >= kend) continue;
                 uint32_t v[32];
-                tmem_ld32(tS + lane_off + c * 32, v);
+                tmem_ld32(tS + lane_off + c0, v);
                 tmem_ld_wait();
+                if (c0 >= kbeg && c0 + 32 <= kend) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int kc = c * 32 + i;
-                    bool kv = PACK ? ((kc >> 6) == seg && (kc & 63) < L) : (j * KB + kc < L);
-                    if (kv) mx = fmaxf(mx, __uint_as_float(v[i]) * scale_log2);
+                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (c0 + i >= kbeg && c0 + i < kend) mx = fmaxf(mx, __uint_as_float(v[i]));
                 }
             }
-            float m_new = fmaxf(m, mx);
+            float m_new = fmaxf(m, mx * scale_log2);
             if (m_new == -INFINITY) m_new = 0.f;  // fully masked row (padding rows only)
-            const float alpha = exp2f(m - m_new);
-            // pass 2: probabilities -> shared memory (swizzled K-major rows)
+            const float alpha = fast_exp2(m - m_new);
+            // pass 2: probabilities -> shared memory (swizzled K-major rows);
+            // chunks outside the valid range get zeros without touching TMEM
             float rs = 0.f;
 #pragma unroll 1
             for (int c = 0; c < KB / 32; ++c) {
+                const int c0 = c * 32;
+                // keys [c0, c0+32) = 4 chunks of 8 in K-block c0/64
+                uint8_t* blk = sP + (c0 >> 6) * 16384 + r * 128;
+                if (c0 + 32 <= kbeg || c0 >= kend) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int ch = ((c0 & 63) >> 3) + q;
+                        *reinterpret_cast<uint4*>(blk + ((ch ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+                    }
+                    continue;
+                }
                 uint32_t v[32];
-                tmem_ld32(tS + lane_off + c * 32, v);
+                tmem_ld32(tS + lane_off + c0, v);
                 tmem_ld_wait();
                 float p[32];
+                if (c0 >= kbeg && c0 + 32 <= kend) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int kc = c * 32 + i;
-                    bool kv = PACK ? ((kc >> 6) == seg && (kc & 63) < L) : (j * KB + kc < L);
-                    p[i] = kv ? exp2f(__uint_as_float(v[i]) * scale_log2 - m_new) : 0.f;
-                    rs += p[i];
+                    for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(__uint_as_float(v[i]), scale_log2, -m_new));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        p[i] = (c0 + i >= kbeg && c0 + i < kend)
+                                   ? fast_exp2(fmaf(__uint_as_float(v[i]), scale_log2, -m_new))
+                                   : 0.f;
                 }
-                // keys [32c, 32c+32) = 4 chunks of 8 in K-block (32c)/64
-                uint8_t* blk = sP + ((c * 32) >> 6) * 16384 + r * 128;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) rs += p[i];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const int ch = (((c * 32) & 63) >> 3) + q;
+                    const int ch = ((c0 & 63) >> 3) + q;
                     uint4 u = make_uint4(pack2(p[8 * q], p[8 * q + 1], (T*)nullptr),
                                          pack2(p[8 * q + 2], p[8 * q + 3], (T*)nullptr),
                                          pack2(p[8 * q + 4], p[8 * q + 5], (T*)nullptr),

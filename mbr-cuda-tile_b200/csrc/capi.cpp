@@ -327,7 +327,8 @@ MBR_API int mbr_shard_finalize(mbr_handle* h, int64_t N, float overlap, int rank
 MBR_API int mbr_set_backend(mbr_handle* h, int gemm, int attention) {
     return guard([&] {
         need(h, "null argument");
-        need((gemm == 0 || gemm == 1) && (attention == 0 || attention == 1), "backend must be 0 or 1");
+        need(gemm >= 0 && gemm <= 2 && (attention == 0 || attention == 1),
+             "gemm backend must be 0, 1 or 2 and attention backend 0 or 1");
         h->model->set_backend(gemm, attention);
     });
 }

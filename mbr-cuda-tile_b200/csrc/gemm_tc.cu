@@ -1,12 +1,15 @@
 // gemm_tc.cu — persistent, warp-specialised tcgen05 grouped GEMM (sm_100a).
 //
-// Warp roles (192 threads): warp 0 lane 0 issues the TMA loads, warp 1 lane 0
-// issues tcgen05.mma (and owns the TMEM allocation), warps 2-5 run the
+// Warp roles (320 threads): warp 0 lane 0 issues the TMA loads, warp 1 lane 0
+// issues tcgen05.mma (and owns the TMEM allocation), warps 2-9 run the
 // epilogue.  Operand tiles are 128 x 64 (A) and BN x 64 (B) 16-bit elements
 // with the 128-byte swizzle, so every MMA descriptor addresses a canonical
 // K-major layout.  The accumulator is double buffered in TMEM so the epilogue
-// of tile i overlaps the MMAs of tile i+1.  Every wait is bounded: on timeout
-// the kernel records an error word and unwinds instead of hanging.
+// of tile i overlaps the MMAs of tile i+1.  Plans with an output view stage
+// each warp's 32 x 128-byte slab in shared memory and write it with one TMA
+// store (or TMA reduce-add into the fp32 residual stream).  Every wait is
+// bounded: on timeout the kernel records an error word and unwinds instead of
+// hanging.
 #include <cuda.h>
 
 #include <algorithm>
@@ -25,15 +28,39 @@ namespace {
 
 constexpr int BM = 128, BK = 64;
 
+// Epilogue warps: warps 2..9; warp w drains TMEM lane quarter (w % 4) for the
+// column half (w - 2) / 4 of the tile.
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kStageRowBytes = 128;                    // one swizzled 128-byte row per lane
+constexpr int kStagingPerWarp = 32 * kStageRowBytes;   // 32 rows x 128 B
+
 template <int BN>
 struct TileCfg {
-    static constexpr int STAGES = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
+    static constexpr int STAGES = BN == 128 ? 6 : 4;
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGING_OFF = STAGES * STAGE_BYTES;  // 1024-aligned
+    static constexpr int BAR_OFF = STAGING_OFF + kEpiWarps * kStagingPerWarp;
     static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
+
+// erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7): one reciprocal, one
+// exponential and a degree-5 polynomial.
+__device__ __forceinline__ float erf_as7126(float x) {
+    const float ax = fabsf(x);
+    const float t = __frcp_rn(fmaf(0.3275911f, ax, 1.0f));
+    float p = fmaf(1.061405429f, t, -1.453152027f);
+    p = fmaf(p, t, 1.421413741f);
+    p = fmaf(p, t, -0.284496736f);
+    p = fmaf(p, t, 0.254829592f);
+    p *= t;
+    const float y = 1.0f - p * __expf(-ax * ax);
+    return copysignf(y, x);
+}
+__device__ __forceinline__ float gelu_fast(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
 
 template <typename T>
 struct IsBf16 {
@@ -101,7 +128,7 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
     } else {
         if constexpr (EPI == ops::EPI_GELU_T) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+            for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
         } else if constexpr (EPI == ops::EPI_TANH_T) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
@@ -147,14 +174,22 @@ __device__ __forceinline__ void epilogue_qkv(const EpiQKV& e, int row, int n0, c
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
     if (sec < 2) {
-        const float* cs = e.cos_t + pos * 32 + (d0 >> 1);
-        const float* sn = e.sin_t + pos * 32 + (d0 >> 1);
+        // 16 consecutive table entries (64 bytes, 64-byte aligned) per lane as
+        // four 16-byte loads: along the band axis every lane has its own
+        // position, so scalar loads would cost one L1 wavefront per lane each
+        const float4* cs = reinterpret_cast<const float4*>(e.cos_t + pos * 32 + (d0 >> 1));
+        const float4* sn = reinterpret_cast<const float4*>(e.sin_t + pos * 32 + (d0 >> 1));
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const float c = __ldg(cs + i), si = __ldg(sn + i);
-            const float x0 = v[2 * i], x1 = v[2 * i + 1];
-            v[2 * i] = x0 * c - x1 * si;
-            v[2 * i + 1] = x0 * si + x1 * c;
+        for (int i4 = 0; i4 < 4; ++i4) {
+            const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+            const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = 4 * i4 + u;
+                const float x0 = v[2 * i], x1 = v[2 * i + 1];
+                v[2 * i] = x0 * cc[u] - x1 * ss[u];
+                v[2 * i + 1] = x0 * ss[u] + x1 * cc[u];
+            }
         }
     }
     T* base = (T*)(sec == 0 ? e.q : sec == 1 ? e.k : e.v);
@@ -166,22 +201,58 @@ __device__ __forceinline__ void epilogue_qkv(const EpiQKV& e, int row, int n0, c
                             pack2(v[8 * j + 6], v[8 * j + 7], (T*)nullptr));
 }
 
-// Epilogue warps: warps 2..9; warp w drains TMEM lane quarter (w % 4) for the
-// column half (w - 2) / 4 of the tile.
-constexpr int kEpiWarps = 8;
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+// Stages 32 accumulator columns of this lane's row through the warp's
+// shared-memory tile (128-byte swizzled rows): fp32 outputs fill a whole row,
+// 16-bit outputs fill half of it (the other half comes from the next chunk).
+template <typename T, int EPI>
+__device__ __forceinline__ void stage_chunk(uint8_t* stg, int lane, int half16, const float (&v)[32]) {
+    uint8_t* row = stg + lane * kStageRowBytes;
+    if constexpr (EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4*>(row + ((c ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int ch = half16 * 4 + c;
+            *reinterpret_cast<uint4*>(row + ((ch ^ (lane & 7)) << 4)) =
+                make_uint4(pack2(v[8 * c], v[8 * c + 1], (T*)nullptr), pack2(v[8 * c + 2], v[8 * c + 3], (T*)nullptr),
+                           pack2(v[8 * c + 4], v[8 * c + 5], (T*)nullptr),
+                           pack2(v[8 * c + 6], v[8 * c + 7], (T*)nullptr));
+        }
+    }
+}
+
+// acc + bias and the activation of the epilogue, in place.
+template <int EPI>
+__device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float (&v)[32]) {
+    const int nvalid = min(32, g.N - n0);
+    if (g.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < nvalid) v[j] += __ldg(g.bias + n0 + j);
+    }
+    if constexpr (EPI == ops::EPI_GELU_T) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+    } else if constexpr (EPI == ops::EPI_TANH_T) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+    }
+}
 
 template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const ops::GemmGroup* __restrict__ groups, const int4* __restrict__ tiles, int ntiles, int* err,
-                   const EpiQKV qkv) {
+                   const __grid_constant__ CUtensorMap tmC, int c_tma, const ops::GemmGroup* __restrict__ groups,
+                   const int4* __restrict__ tiles, int ntiles, int* err, const EpiQKV qkv) {
     using Cfg = TileCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
     uint8_t* sB = smem + Cfg::STAGES * Cfg::A_BYTES;
-    uint64_t* full = (uint64_t*)(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* full = (uint64_t*)(smem + Cfg::BAR_OFF);
     uint64_t* empty = full + Cfg::STAGES;
     uint64_t* acc_full = empty + Cfg::STAGES;
     uint64_t* acc_empty = acc_full + 2;
@@ -279,22 +350,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int row = tl.y + q * 32 + lane;
             const bool rv = row < g.M;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + half * (BN / 2);
+            constexpr bool kStoresViaTma = EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32 ||
+                                           EPI == ops::EPI_T || EPI == ops::EPI_GELU_T || EPI == ops::EPI_TANH_T;
+            if (kStoresViaTma && c_tma) {
+                // stage through this warp's 32-row tile; one TMA store (or
+                // reduce-add into the fp32 residual) per 128-byte row group
+                constexpr bool k16 = !(EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32);
+                uint8_t* stg = smem + Cfg::STAGING_OFF + (warp - 2) * kStagingPerWarp;
+                const int yrow = tl.y + q * 32;
 #pragma unroll 1
-            for (int c = 0; c < kChunks; ++c) {
-                const int n0 = tl.z + half * (BN / 2) + c * 32;
-                if (n0 >= g.N) break;
-                uint32_t r[32];
-                tmem_ld32(taddr + c * 32, r);
-                tmem_ld_wait();
-                if (rv) {
-                    if constexpr (EPI == ops::EPI_QKV) epilogue_qkv<T>(qkv, row, n0, r);
-                    else epilogue_chunk<T, EPI>(g, row, n0, r);
+                for (int c = 0; c < kChunks; ++c) {
+                    const int n0 = tl.z + half * (BN / 2) + c * 32;
+                    if (n0 >= g.N) break;
+                    uint32_t r[32];
+                    tmem_ld32(taddr + c * 32, r);
+                    tmem_ld_wait();
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                    apply_epi<EPI>(g, n0, v);
+                    const int h16 = k16 ? (c & 1) : 0;
+                    if (h16 == 0) {  // the staging tile is free once the previous store has read it
+                        if (lane == 0) bulk_wait_read_all();
+                        __syncwarp();
+                    }
+                    stage_chunk<T, EPI>(stg, lane, h16, v);
+                    const bool flush = !k16 || h16 == 1 || c + 1 == kChunks || n0 + 32 >= g.N;
+                    if (flush) {
+                        fence_async_smem();
+                        __syncwarp();
+                        if (lane == 0 && yrow < g.M) {  // boxes wholly below the last row are skipped
+                            const int x = k16 ? n0 - 32 * h16 : n0;
+                            const int y = c_tma == 2 ? g.c_group : yrow;
+                            const int z = c_tma == 2 ? yrow : g.c_group;
+                            if constexpr (EPI == ops::EPI_ADD_F32) tma_reduce_add_3d(&tmC, stg, x, y, z);
+                            else tma_store_3d(&tmC, stg, x, y, z);
+                            bulk_commit();
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kChunks; ++c) {
+                    const int n0 = tl.z + half * (BN / 2) + c * 32;
+                    if (n0 >= g.N) break;
+                    uint32_t r[32];
+                    tmem_ld32(taddr + c * 32, r);
+                    tmem_ld_wait();
+                    if (rv) {
+                        if constexpr (EPI == ops::EPI_QKV) epilogue_qkv<T>(qkv, row, n0, r);
+                        else epilogue_chunk<T, EPI>(g, row, n0, r);
+                    }
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
+        if (lane == 0) bulk_wait_all();  // outstanding TMA stores complete before exit
     }
     tc_fence_before();
     __syncthreads();
@@ -338,6 +451,34 @@ void make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
     if (r != CUDA_SUCCESS) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 
+// Output map C[group][row][col] for the staged TMA stores: box = one warp's
+// 32 rows x 128 bytes, 128-byte swizzle (the layout stage_chunk writes).
+// The two outer dimensions are ordered by increasing stride; `swapped` tells
+// the kernel that the group dimension comes before the row dimension.
+void make_out_map(CUtensorMap* m, const GemmPlanTC& p, bool& swapped) {
+    const int64_t es = p.c_dtype == DT_F32 ? 4 : 2;
+    MBR_CHECK(((uintptr_t)p.c_base & 15) == 0, "TMA output base must be 16-byte aligned");
+    MBR_CHECK((p.c_row_stride * es) % 16 == 0 && (p.c_group_stride * es) % 16 == 0,
+              "TMA output strides must be multiples of 16 bytes");
+    swapped = p.c_groups > 1 && p.c_group_stride < p.c_row_stride;
+    cuuint64_t dims[3] = {(cuuint64_t)p.c_cols, (cuuint64_t)p.c_rows, (cuuint64_t)p.c_groups};
+    cuuint64_t strides[2] = {(cuuint64_t)(p.c_row_stride * es), (cuuint64_t)(p.c_group_stride * es)};
+    cuuint32_t box[3] = {(cuuint32_t)(kStageRowBytes / es), 32, 1};
+    if (swapped) {
+        std::swap(dims[1], dims[2]);
+        std::swap(strides[0], strides[1]);
+        std::swap(box[1], box[2]);
+    }
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUtensorMapDataType t = p.c_dtype == DT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                            : p.c_dtype == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                   : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = encode_fn()(m, t, 3, const_cast<void*>(p.c_base), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled (output) failed: " + std::to_string((int)r));
+}
+
 int num_sms() {
     int dev = 0, n = 0;
     MBR_CUDA(cudaGetDevice(&dev));
@@ -359,7 +500,8 @@ void launch_one(const GemmLaunch& L, int* d_err, cudaStream_t st) {
         attr[dev] = true;
     }
     int grid = std::min(L.ntiles, sms[dev]);
-    kern<<<grid, kGemmThreads, TileCfg<BN>::SMEM, st>>>(L.tmA, L.tmB, L.groups, L.tiles, L.ntiles, d_err, L.qkv);
+    kern<<<grid, kGemmThreads, TileCfg<BN>::SMEM, st>>>(L.tmA, L.tmB, L.tmC, L.c_tma, L.groups, L.tiles, L.ntiles,
+                                                         d_err, L.qkv);
     MBR_CUDA(cudaGetLastError());
 }
 
@@ -418,6 +560,27 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
     }
     L.ntiles = (int)(tiles.size() - L_first);
     L.groups = p.groups;
+    L.c_tma = 0;
+    const bool staged_epi = p.epi == ops::EPI_F32 || p.epi == ops::EPI_ADD_F32 || p.epi == ops::EPI_T ||
+                            p.epi == ops::EPI_GELU_T || p.epi == ops::EPI_TANH_T;
+    if (p.c_dtype >= 0 && staged_epi) {
+        const bool f32 = p.epi == ops::EPI_F32 || p.epi == ops::EPI_ADD_F32;
+        MBR_CHECK(f32 ? p.c_dtype == DT_F32 : p.c_dtype == dtype, "tc gemm: output view dtype mismatch");
+        const int64_t es = f32 ? 4 : 2;
+        // The staged stores write whole 32-row x 128-byte boxes and rely on the
+        // map's bounds for clipping, so every group must cover its output block
+        // exactly and agree with its own C / ldc.
+        for (int gi = 0; gi < p.ngroups; ++gi) {
+            const ops::GemmGroup& g = p.h_groups[gi];
+            MBR_CHECK(g.M == p.c_rows && g.N == p.c_cols && g.c_group >= 0 && g.c_group < p.c_groups &&
+                          g.ldc == p.c_row_stride &&
+                          (const char*)g.C == (const char*)p.c_base + (int64_t)g.c_group * p.c_group_stride * es,
+                      "tc gemm: group does not match the output view");
+        }
+        bool swapped = false;
+        make_out_map(&L.tmC, p, swapped);
+        L.c_tma = swapped ? 2 : 1;
+    }
     L.ok = true;
 }
 

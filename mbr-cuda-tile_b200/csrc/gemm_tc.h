@@ -4,7 +4,7 @@
 // are row blocks of one K-major 2-D tensor each.  A persistent kernel walks a
 // host-built tile list; TMA streams 128 x 64 A tiles and BN x 64 B tiles
 // (128-byte swizzle) through a shared-memory ring, one thread issues
-// tcgen05.mma into a double-buffered TMEM accumulator, and four epilogue warps
+// tcgen05.mma into a double-buffered TMEM accumulator, and eight epilogue warps
 // drain TMEM (tcgen05.ld) through the fused epilogue while the next tile's
 // MMAs run.
 #pragma once
@@ -31,6 +31,13 @@ struct GemmPlanTC {
     int64_t a_rows = 0, a_cols = 0;
     const void* b_base = nullptr;
     int64_t b_rows = 0, b_cols = 0;
+    // Optional output view C[group][row][col] = c_base[group*c_group_stride +
+    // row*c_row_stride + col] written by TMA stores / reduce-adds from shared
+    // memory (rows beyond c_rows and columns beyond c_cols are clipped); group
+    // g's block is its c_group.  c_dtype < 0: the epilogue stores from registers.
+    const void* c_base = nullptr;
+    int64_t c_rows = 0, c_cols = 0, c_groups = 1, c_row_stride = 0, c_group_stride = 0;
+    int c_dtype = -1;
 };
 
 // Parameters of the fused QKV epilogue (ops::EPI_QKV): RoPE on q/k with the
@@ -46,7 +53,8 @@ struct EpiQKV {
 
 // Prepared launch: tensor maps and the tile list (built once per workspace).
 struct GemmLaunch {
-    CUtensorMap tmA, tmB;
+    CUtensorMap tmA, tmB, tmC;
+    int c_tma = 0;  // epilogue writes C through tmC
     const int4* tiles = nullptr;  // device: (group, m0, n0, k-blocks)
     int ntiles = 0;
     int bn = 128;

@@ -450,6 +450,13 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
             tp.b_base = p->b_base;
             tp.b_rows = p->b_rows;
             tp.b_cols = p->b_cols;
+            tp.c_base = p->c_base;
+            tp.c_rows = p->c_rows;
+            tp.c_cols = p->c_cols;
+            tp.c_groups = p->c_groups;
+            tp.c_row_stride = p->c_row_stride;
+            tp.c_group_stride = p->c_group_stride;
+            tp.c_dtype = p->c_dtype;
             tc::GemmLaunch L;
             if (p->qkv_mode >= 0 && dh_ == 64) {
                 // fused RoPE + head scatter epilogue (replaces rope_scatter)
@@ -495,6 +502,16 @@ void MelBandRoformer::build_plans(Workspace& ws) {
         p.maxN = std::max(p.maxN, g.N);
         p.maxK = std::max(p.maxK, g.K);
     };
+    auto view = [](Plan& p, const void* base, int64_t rows, int64_t cols, int64_t groups, int64_t row_stride,
+                   int64_t group_stride, int cdt) {
+        p.c_base = base;
+        p.c_rows = rows;
+        p.c_cols = cols;
+        p.c_groups = groups;
+        p.c_row_stride = row_stride;
+        p.c_group_stride = group_stride;
+        p.c_dtype = cdt;
+    };
     auto mk = [](const void* A, int64_t lda, const void* B, int64_t ldb, void* Cp, int64_t ldc, const float* bias,
                  int64_t M, int N, int K) {
         ops::GemmGroup g{};
@@ -518,11 +535,13 @@ void MelBandRoformer::build_plans(Workspace& ws) {
     ws.band_split.b_base = d_wbs_;
     ws.band_split.b_rows = D_;
     ws.band_split.b_cols = KP_;
+    view(ws.band_split, ws.R, MT, D_, NB_, (int64_t)NB_ * D_, D_, DT_F32);
     for (int b = 0; b < NB_; ++b) {
         int k0 = band_kofs_[b], kn = band_kofs_[b + 1] - k0;
         ops::GemmGroup g = mk((uint8_t*)ws.xb + es * k0, KP_, (uint8_t*)d_wbs_ + es * k0, KP_, ws.R + (size_t)b * D_,
                               (int64_t)NB_ * D_, d_bs_bias_ + (size_t)b * D_, MT, D_, kn);
         g.k_col0 = k0;
+        g.c_group = b;
         push(ws.band_split, g);
     }
     // transformer layers
@@ -540,14 +559,17 @@ void MelBandRoformer::build_plans(Workspace& ws) {
                 begin(p[1], ops::EPI_ADD_F32);
                 p[1].a_base = ws.merged, p[1].a_rows = M, p[1].a_cols = DI_;
                 p[1].b_base = lw.wo, p[1].b_rows = D_, p[1].b_cols = DI_;
+                view(p[1], ws.R, M, D_, 1, D_, M * D_, DT_F32);
                 push(p[1], mk(ws.merged, DI_, lw.wo, DI_, ws.R, D_, nullptr, M, D_, DI_));
                 begin(p[2], ops::EPI_GELU_T);
                 p[2].a_base = ws.xn, p[2].a_rows = M, p[2].a_cols = D_;
                 p[2].b_base = lw.w1, p[2].b_rows = hid_, p[2].b_cols = D_;
+                view(p[2], ws.hf, M, hid_, 1, hid_, M * hid_, dtype_);
                 push(p[2], mk(ws.xn, D_, lw.w1, D_, ws.hf, hid_, lw.b1, M, hid_, D_));
                 begin(p[3], ops::EPI_ADD_F32);
                 p[3].a_base = ws.hf, p[3].a_rows = M, p[3].a_cols = hid_;
                 p[3].b_base = lw.w2, p[3].b_rows = D_, p[3].b_cols = hid_;
+                view(p[3], ws.R, M, D_, 1, D_, M * D_, DT_F32);
                 push(p[3], mk(ws.hf, hid_, lw.w2, hid_, ws.R, D_, lw.b2, M, D_, hid_));
                 for (auto& q : p) ws.layer_plans.push_back(q);
             }
@@ -566,6 +588,7 @@ void MelBandRoformer::build_plans(Workspace& ws) {
             p.b_base = mask_[s].w[i];
             p.b_rows = last ? 2 * (int64_t)band_boff_[NB_] : (int64_t)NB_ * hid_;
             p.b_cols = in;
+            if (!last) view(p, ws.mh[i & 1], MT, hid_, NB_, hid_, MT * hid_, dtype_);
             for (int b = 0; b < NB_; ++b) {
                 const uint8_t* Ab = (const uint8_t*)A + es * (size_t)b * MT * in;
                 ops::GemmGroup g;
@@ -574,6 +597,7 @@ void MelBandRoformer::build_plans(Workspace& ws) {
                            (uint8_t*)ws.mh[i & 1] + es * (size_t)b * MT * hid_, hid_,
                            mask_[s].b[i] + (size_t)b * hid_, MT, hid_, in);
                     g.b_row0 = b * hid_;
+                    g.c_group = b;
                 } else {
                     int r0 = 2 * band_boff_[b];
                     g = mk(Ab, in, (uint8_t*)mask_[s].w[i] + es * (size_t)r0 * in, in,
@@ -645,8 +669,14 @@ void MelBandRoformer::profile_read(int kind, double* ms, int64_t* count) {
     } while (0)
 
 void MelBandRoformer::run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st) {
-    if (gemm_backend_ == BACKEND_TC && dtype_ != DT_F32 && p.launch >= 0) {
-        MBR_LAUNCH(kind, tc::gemm_launch(ws.launches[p.launch], dtype_, d_err_, st));
+    if (gemm_backend_ != BACKEND_SIMT && dtype_ != DT_F32 && p.launch >= 0) {
+        if (gemm_backend_ == BACKEND_TC_DIRECT && ws.launches[p.launch].c_tma) {
+            tc::GemmLaunch L = ws.launches[p.launch];
+            L.c_tma = 0;  // epilogue stores from registers
+            MBR_LAUNCH(kind, tc::gemm_launch(L, dtype_, d_err_, st));
+        } else {
+            MBR_LAUNCH(kind, tc::gemm_launch(ws.launches[p.launch], dtype_, d_err_, st));
+        }
     } else {
         MBR_LAUNCH(kind, ops::gemm_simt(ws.d_groups + p.first, p.n, p.maxM, p.maxN, dtype_, p.epi, st));
     }
@@ -669,7 +699,7 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
                                           lw.bg, H_, ws.gates, st));
         run_gemm(ws, p[0], PK_GEMM_QKV, st);
         // the tensor-core QKV GEMM applies RoPE and scatters q/k/v in its epilogue
-        const bool fused_qkv = gemm_backend_ == BACKEND_TC && p[0].launch >= 0 &&
+        const bool fused_qkv = gemm_backend_ != BACKEND_SIMT && p[0].launch >= 0 &&
                                ws.launches[p[0].launch].epi == ops::EPI_QKV;
         if (!fused_qkv)
             MBR_LAUNCH(PK_ROPE, ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k, ws.v,

@@ -56,7 +56,9 @@ void rotary_tables(int n, int dim, std::vector<float>& cs, std::vector<float>& s
 
 // Kernel backends selectable per model (the tensor-core path is the default for
 // fp16/bf16; the CUDA-core path is the fp32 path and a cross-check).
-enum Backend { BACKEND_SIMT = 0, BACKEND_TC = 1 };
+// BACKEND_TC_DIRECT: tensor-core GEMMs whose epilogues store from registers
+// instead of staging through shared memory for TMA stores (A/B comparisons).
+enum Backend { BACKEND_SIMT = 0, BACKEND_TC = 1, BACKEND_TC_DIRECT = 2 };
 
 // Kernel classes timed by the optional per-launch profiler (CUDA events on the
 // launching stream).
@@ -139,6 +141,11 @@ private:
         int64_t a_rows = 0, a_cols = 0;
         const void* b_base = nullptr;
         int64_t b_rows = 0, b_cols = 0;
+        // output view C[group][row][col] for TMA-staged epilogue stores
+        // (c_dtype < 0: stores from registers)
+        const void* c_base = nullptr;
+        int64_t c_rows = 0, c_cols = 0, c_groups = 1, c_row_stride = 0, c_group_stride = 0;
+        int c_dtype = -1;
     };
     struct LayerW {
         float* attn_gamma;

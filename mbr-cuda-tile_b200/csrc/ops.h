@@ -55,7 +55,7 @@ struct GemmGroup {
     int M, N, K;
     int a_row0, b_row0;  // row offsets of this group inside the A / B tensor maps
     int k_col0;          // column offset of this group's K range inside A and B
-    int pad_;
+    int c_group;         // index of this group's C block in a [groups][rows][cols] output map
 };
 enum Epilogue {
     EPI_F32 = 0,      // C (fp32) = acc + bias

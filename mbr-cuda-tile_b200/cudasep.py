@@ -18,7 +18,7 @@ LIB_PATH = os.path.join(HERE, "libmbr_b200.so")
 
 FP32, FP16, BF16 = 0, 1, 3
 DTYPES = {"fp32": FP32, "float32": FP32, "fp16": FP16, "float16": FP16, "bf16": BF16, "bfloat16": BF16}
-BACKEND_SIMT, BACKEND_TC = 0, 1
+BACKEND_SIMT, BACKEND_TC, BACKEND_TC_DIRECT = 0, 1, 2
 
 INFO = dict(dim=0, depth=1, num_stems=2, channels=3, num_bands=4, sample_rate=5, chunk_size=6, num_overlap=7,
             heads=8, dim_head=9, band_freqs=10, dtype=11, device=12, hop=13)

@@ -159,6 +159,26 @@ def test_tensor_core_gemm_matches_cuda_core_gemm(torch_cuda, make_csm, preset, d
     assert s >= FP16_SNR_DB if dtype == "fp16" else s >= BF16_SNR_DB
 
 
+@pytest.mark.parametrize("preset,dtype,L", [("tiny2", "fp16", 44100), ("mid", "bf16", 100000)])
+def test_staged_tma_epilogue_matches_register_stores(torch_cuda, make_csm, preset, dtype, L):
+    """The GEMM epilogue that stages tiles in shared memory and writes them with
+    TMA stores / reduce-adds (ragged row and column edges clipped by the tensor
+    map) computes exactly what the per-thread register stores compute."""
+    torch = torch_cuda
+    import cudasep
+
+    path = make_csm(preset, seed=21)
+    m = _model(path, dtype)
+    x = torch.from_numpy(_audio(22, 1, 2, L)).cuda()
+    m.set_backend(cudasep.BACKEND_TC, cudasep.BACKEND_TC)
+    a = m.forward(x).cpu().numpy()
+    m.sync_check()
+    m.set_backend(cudasep.BACKEND_TC_DIRECT, cudasep.BACKEND_TC)
+    b = m.forward(x).cpu().numpy()
+    m.sync_check()
+    assert np.array_equal(a, b)
+
+
 def test_mid_fp16_forward_snr(torch_cuda, make_csm):
     """std layer shapes (dim 384, 8x64 heads): fp16 forward vs the oracle."""
     torch = torch_cuda
