@@ -33,14 +33,17 @@ constexpr int DH = 64;
 constexpr int QT = 128;  // queries per tile
 constexpr int KB = 128;  // keys per block
 
+// Two CTAs share an SM, so the layout carries no alignment slack: the kernel
+// checks that the dynamic window is 1024-byte aligned instead.
 struct AttnSmem {
     static constexpr int Q = 0;
-    static constexpr int K0 = 16384;
+    static constexpr int K0 = 16384;  // K and V blocks are double buffered
     static constexpr int K1 = 32768;
-    static constexpr int V = 49152;
-    static constexpr int P = 65536;  // two 16 KB K-blocks (keys 0-63, 64-127)
-    static constexpr int BAR = 98304;
-    static constexpr int TOTAL = BAR + 128 + 1024;  // + barriers + alignment slack
+    static constexpr int V0 = 49152;
+    static constexpr int V1 = 65536;
+    static constexpr int P = 81920;  // two 16 KB K-blocks (keys 0-63, 64-127)
+    static constexpr int BAR = 114688;
+    static constexpr int TOTAL = BAR + 128;
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
@@ -78,16 +81,17 @@ __global__ void __launch_bounds__(160, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, float scale_log2,
                    const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    if (!smem_aligned_or_flag(smem_raw, err)) return;  // uniform over the CTA
+    uint8_t* sm = smem_raw;
     uint64_t* bar = (uint64_t*)(sm + AttnSmem::BAR);
     uint64_t* bar_q = bar + 0;
     uint64_t* bar_k = bar + 1;  // [2]
-    uint64_t* bar_v = bar + 3;
-    uint64_t* bar_s = bar + 4;
-    uint64_t* bar_p = bar + 5;
-    uint64_t* bar_o = bar + 6;
-    uint32_t* tmem_slot = (uint32_t*)(bar + 7);
+    uint64_t* bar_v = bar + 3;  // [2]
+    uint64_t* bar_s = bar + 5;
+    uint64_t* bar_p = bar + 6;
+    uint64_t* bar_o = bar + 7;
+    uint32_t* tmem_slot = (uint32_t*)(bar + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // tile decode
@@ -106,7 +110,8 @@ __global__ void __launch_bounds__(160, 2)
         mbar_init(bar_q, 1);
         mbar_init(&bar_k[0], 1);
         mbar_init(&bar_k[1], 1);
-        mbar_init(bar_v, 1);
+        mbar_init(&bar_v[0], 1);
+        mbar_init(&bar_v[1], 1);
         mbar_init(bar_s, 1);
         mbar_init(bar_p, 4);
         mbar_init(bar_o, 1);
@@ -138,13 +143,13 @@ __global__ void __launch_bounds__(160, 2)
                 }
             };
             auto load_v = [&](int j) {
-                uint8_t* dst = sm + AttnSmem::V;
-                mbar_arrive_expect_tx(bar_v, 16384);
+                uint8_t* dst = sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0);
+                mbar_arrive_expect_tx(&bar_v[j & 1], 16384);
                 if (PACK) {
-                    tma_load_2d(dst, &tmV, 0, sh0 * L, bar_v);
-                    tma_load_2d(dst + 8192, &tmV, 0, sh1 * L, bar_v);
+                    tma_load_2d(dst, &tmV, 0, sh0 * L, &bar_v[j & 1]);
+                    tma_load_2d(dst + 8192, &tmV, 0, sh1 * L, &bar_v[j & 1]);
                 } else {
-                    tma_load_2d(dst, &tmV, 0, sh0 * L + j * KB, bar_v);
+                    tma_load_2d(dst, &tmV, 0, sh0 * L + j * KB, &bar_v[j & 1]);
                 }
             };
             mbar_arrive_expect_tx(bar_q, 16384);
@@ -156,24 +161,38 @@ __global__ void __launch_bounds__(160, 2)
             }
             load_k(0);
             load_v(0);
-            if (nkv > 1) load_k(1);
+            if (nkv > 1) {
+                load_k(1);
+                load_v(1);
+            }
             constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
             constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
-            const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sV = smem_u32(sm + AttnSmem::V),
-                           sP = smem_u32(sm + AttnSmem::P);
-            for (int j = 0; j < nkv; ++j) {
-                if (j == 0 && !mbar_wait(bar_q, 0, err)) break;
-                if (!mbar_wait(&bar_k[j & 1], (j >> 1) & 1, err)) break;
-                tc_fence_after();
+            const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sP = smem_u32(sm + AttnSmem::P);
+            auto issue_s = [&](int j) {  // S = Q K(j)^T -> tS
                 const uint32_t sK = smem_u32(sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0));
 #pragma unroll
                 for (int k = 0; k < DH / 16; ++k)
                     mma_f16(tS, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idS, k > 0);
                 mma_commit(bar_s);
-                if (j >= 1 && j + 1 < nkv) load_k(j + 1);  // its buffer's S(j-1) is complete
-                if (!mbar_wait(bar_p, j & 1, err)) break;
-                if (!mbar_wait(bar_v, j & 1, err)) break;
+            };
+            // Pipeline: S(j+1) is issued as soon as the softmax has turned S(j)
+            // into P(j), right behind P(j).V(j), so the softmax warps find the
+            // next scores ready once they have folded O(j).  Buffer reuse:
+            //  K(j&1) is free once P(j) exists (S(j) was consumed)   -> load K(j+2);
+            //  V((j+1)&1) held V(j-1), whose P.V finished before the softmax
+            //  produced P(j) (it waits for O(j-1) first)              -> load V(j+1).
+            bool alive = mbar_wait(bar_q, 0, err) && mbar_wait(&bar_k[0], 0, err);
+            if (alive) {
                 tc_fence_after();
+                issue_s(0);
+            }
+            for (int j = 0; j < nkv && alive; ++j) {
+                if (!mbar_wait(bar_p, j & 1, err)) break;
+                tc_fence_after();
+                if (j >= 1 && j + 1 < nkv) load_v(j + 1);
+                if (!mbar_wait(&bar_v[j & 1], (j >> 1) & 1, err)) break;
+                tc_fence_after();
+                const uint32_t sV = smem_u32(sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0));
 #pragma unroll
                 for (int k = 0; k < KB / 16; ++k) {
                     const uint32_t blk = k >> 2, kk = k & 3;
@@ -183,8 +202,10 @@ __global__ void __launch_bounds__(160, 2)
                 }
                 mma_commit(bar_o);
                 if (j + 1 < nkv) {
-                    if (!mbar_wait(bar_o, j & 1, err)) break;  // P.V(j) done reading V
-                    load_v(j + 1);
+                    if (!mbar_wait(&bar_k[(j + 1) & 1], ((j + 1) >> 1) & 1, err)) break;
+                    tc_fence_after();
+                    issue_s(j + 1);
+                    if (j + 2 < nkv) load_k(j + 2);
                 }
             }
         }

@@ -43,6 +43,41 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 
+// Single-instruction approximations (PTX rcp.approx / ex2.approx, ~1-2 ulp).
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Exact-erf GELU for the tensor-core epilogues: erf by Abramowitz & Stegun
+// 7.1.26, erf(z) = 1 - (a1 t + ... + a5 t^5) e^{-z^2}, t = 1 / (1 + p z),
+// |error| <= 1.5e-7.  With q = 0.5 x (1 - erf(|x| / sqrt 2)) (the tail, kept
+// as a product so it does not cancel) gelu(x) = x - q for x >= 0, q otherwise.
+__device__ __forceinline__ float gelu_as(float x) {
+    const float z = fabsf(x) * 0.70710678118654752f;
+    const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+    float p = fmaf(1.061405429f, t, -1.453152027f);
+    p = fmaf(p, t, 1.421413741f);
+    p = fmaf(p, t, -0.284496736f);
+    p = fmaf(p, t, 0.254829592f);
+    const float e = ex2_approx(x * x * -0.72134752044448170f);  // e^{-x^2/2} = 2^{-x^2 log2(e) / 2}
+    const float q = 0.5f * x * (p * t) * e;
+    return x >= 0.0f ? x - q : q;
+}
+
+// tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)); absolute error ~1e-7.
+__device__ __forceinline__ float tanh_fast(float x) {
+    const float e = ex2_approx(fabsf(x) * 2.8853900817779268f);  // e^{2|x|}
+    const float r = fmaf(-2.0f, rcp_approx(e + 1.0f), 1.0f);
+    return copysignf(r, x);
+}
+
 // torch / Tensor::pad_reflect index (no edge repeat), valid for pad < n.
 __host__ __device__ __forceinline__ int64_t reflect_idx(int64_t p, int64_t n) {
     if (n <= 1) return 0;

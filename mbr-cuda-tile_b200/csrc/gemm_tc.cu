@@ -47,21 +47,6 @@ struct TileCfg {
     static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
 
-// erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7): one reciprocal, one
-// exponential and a degree-5 polynomial.
-__device__ __forceinline__ float erf_as7126(float x) {
-    const float ax = fabsf(x);
-    const float t = __frcp_rn(fmaf(0.3275911f, ax, 1.0f));
-    float p = fmaf(1.061405429f, t, -1.453152027f);
-    p = fmaf(p, t, 1.421413741f);
-    p = fmaf(p, t, -0.284496736f);
-    p = fmaf(p, t, 0.254829592f);
-    p *= t;
-    const float y = 1.0f - p * __expf(-ax * ax);
-    return copysignf(y, x);
-}
-__device__ __forceinline__ float gelu_fast(float x) { return 0.5f * x * (1.0f + erf_as7126(x * 0.70710678118654752f)); }
-
 template <typename T>
 struct IsBf16 {
     static constexpr bool value = false;
@@ -128,10 +113,10 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
     } else {
         if constexpr (EPI == ops::EPI_GELU_T) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+            for (int j = 0; j < 32; ++j) v[j] = gelu_as(v[j]);
         } else if constexpr (EPI == ops::EPI_TANH_T) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+            for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
         }
         T* c = (T*)g.C + (int64_t)row * g.ldc + n0;
         if (nvalid == 32 && ((uintptr_t)c & 15) == 0) {
@@ -229,16 +214,25 @@ template <int EPI>
 __device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float (&v)[32]) {
     const int nvalid = min(32, g.N - n0);
     if (g.bias) {
+        const float* b = g.bias + n0;
+        if (nvalid == 32 && ((uintptr_t)b & 15) == 0) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (j < nvalid) v[j] += __ldg(g.bias + n0 + j);
+            for (int j = 0; j < 8; ++j) {
+                const float4 b4 = __ldg(reinterpret_cast<const float4*>(b) + j);
+                v[4 * j] += b4.x, v[4 * j + 1] += b4.y, v[4 * j + 2] += b4.z, v[4 * j + 3] += b4.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nvalid) v[j] += __ldg(b + j);
+        }
     }
     if constexpr (EPI == ops::EPI_GELU_T) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+        for (int j = 0; j < 32; ++j) v[j] = gelu_as(v[j]);
     } else if constexpr (EPI == ops::EPI_TANH_T) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+        for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
     }
 }
 

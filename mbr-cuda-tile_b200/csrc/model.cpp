@@ -349,6 +349,7 @@ void MelBandRoformer::check_device_error() {
     MBR_CUDA(cudaMemcpy(&e, d_err_, sizeof(int), cudaMemcpyDeviceToHost));
     if (e != 0) {
         MBR_CUDA(cudaMemset(d_err_, 0, sizeof(int)));
+        if (e == 2) throw Error(ERR_CUDA, "a tensor-core kernel found its shared memory window misaligned");
         throw Error(ERR_TIMEOUT, "a tensor-core kernel timed out waiting on a pipeline barrier (error " +
                                      std::to_string(e) + ")");
     }

@@ -10,7 +10,17 @@ namespace mbr {
 namespace sm100 {
 
 // Error codes a kernel writes to its error word when a bounded wait gives up.
-enum KernelError { KERR_NONE = 0, KERR_TIMEOUT = 1 };
+enum KernelError { KERR_NONE = 0, KERR_TIMEOUT = 1, KERR_SMEM_ALIGN = 2 };
+
+// Kernels that size their dynamic shared memory without alignment slack call
+// this first: if the window is not 1024-byte aligned (needed by the 128-byte
+// swizzle) they record KERR_SMEM_ALIGN and the whole CTA returns before any
+// TMA, TMEM or barrier operation.
+__device__ __forceinline__ bool smem_aligned_or_flag(const void* smem, int* err) {
+    if (((uint32_t)__cvta_generic_to_shared(smem) & 1023u) == 0) return true;
+    if (threadIdx.x == 0) atomicExch(err, KERR_SMEM_ALIGN);
+    return false;
+}
 
 // Upper bound on mbarrier polls before a wait is declared dead (each poll is a
 // try_wait that itself suspends for a hardware-defined interval).
