@@ -205,6 +205,18 @@ MBR_API int mbr_op_sigmoid_gate(const void* d_x, const void* d_gate, void* d_y, 
 MBR_API int mbr_op_rope(const void* d_x, const float* d_cos, const float* d_sin, void* d_y, int64_t seqs, int L,
                         int heads, int dtype, void* stream);
 
+/* Multi-head attention with the head merge: q, k, v [B][heads][N][dim_head]
+ * (dtype), out [B][N][heads*dim_head] = softmax(q k^T * scale) v, multiplied
+ * by gates [B][N][heads] (fp32, already sigmoid'ed) when d_gates is non-null.
+ * scale 0 means 1/sqrt(dim_head).  Replaces scaled_dot_product_attention
+ * (src/mbr_cuda_tile.h:42-45, src/mbr_cuda_tile.cu:6530) followed by
+ * apply_gates_and_merge_heads (src/mbr_cuda_tile.h:28-29).  fp16/bf16 with
+ * dim_head 64 run the tcgen05 flash-attention kernel and return after the
+ * stream drains (a pipeline timeout is MBR_ERR_TIMEOUT); fp32 or dim_head 32
+ * run the CUDA-core kernel asynchronously. */
+MBR_API int mbr_op_attention(const void* d_q, const void* d_k, const void* d_v, int64_t B, int heads, int N,
+                             int dim_head, float scale, const float* d_gates, void* d_out, int dtype, void* stream);
+
 /* Host tables of MelBandRoformer::compute_rotary_cos_sin
  * (src/model_mel_band_roformer.cu:270-300): h_cos, h_sin [L][dim_head/2]. */
 MBR_API int mbr_rope_tables(int L, int dim_head, float* h_cos, float* h_sin);

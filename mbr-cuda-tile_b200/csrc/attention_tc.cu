@@ -2,17 +2,19 @@
 // 128-key blocks) and the band axis (L <= 64 bands, two sequences packed per
 // 128-row tile with a block-diagonal mask), head dim 64, fp16/bf16.
 //
-// One CTA = one 128-query tile of one (sequence, head) [or two packed band
-// sequences].  Warp 4 lane 0 issues TMA loads and tcgen05.mma; warps 0-3 (one
-// thread per query row, TMEM lane = row) run the online softmax:
+// One CTA (4 warps, two CTAs per SM) = one 128-query tile of one (sequence,
+// head) [or two packed band sequences]; thread r owns query row r (TMEM lane
+// r).  Per 128-key block j:
 //   S = Q K^T          -> TMEM (128 x 128 fp32)
 //   P = exp2(S*c - m)  -> shared memory (16-bit, 128-byte swizzled K-major)
-//   O_blk = P V        -> TMEM (128 x 64 fp32), folded into registers with the
-//                         running-max correction.
+//   O += P V           -> TMEM (128 x 64 fp32)
+// Thread 0 issues the TMA loads and, after the CTA barrier that publishes
+// P(j), the MMAs P.V(j) and S(j+1); K and V blocks are double buffered.
 // V keeps the [seq][H][L][64] layout of q and k: its 128-key tile is the
-// MN-major B operand of the P.V product.  The epilogue multiplies by the sigmoid gate
-// and writes the merged-head row of each token (apply_gates_and_merge_heads).
-// All waits are bounded (error word instead of a hang).
+// MN-major B operand of the P.V product.  The epilogue multiplies by the
+// sigmoid gate and writes the merged-head row of each token
+// (apply_gates_and_merge_heads).  All waits are bounded (error word instead of
+// a hang).
 #include <cuda.h>
 
 #include <mutex>
@@ -32,6 +34,9 @@ namespace {
 constexpr int DH = 64;
 constexpr int QT = 128;  // queries per tile
 constexpr int KB = 128;  // keys per block
+// O and l are rescaled only when a block's row max (log2 units) exceeds the
+// running offset by more than this, bounding the probabilities by 2^8.
+constexpr float kRescaleLog2 = 8.0f;
 
 // Two CTAs share an SM, so the layout carries no alignment slack: the kernel
 // checks that the dynamic window is 1024-byte aligned instead.
@@ -77,7 +82,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 template <typename T, bool PACK>
-__global__ void __launch_bounds__(160, 2)
+__global__ void __launch_bounds__(128, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, float scale_log2,
                    const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
@@ -89,11 +94,11 @@ __global__ void __launch_bounds__(160, 2)
     uint64_t* bar_k = bar + 1;  // [2]
     uint64_t* bar_v = bar + 3;  // [2]
     uint64_t* bar_s = bar + 5;
-    uint64_t* bar_p = bar + 6;
-    uint64_t* bar_o = bar + 7;
-    uint32_t* tmem_slot = (uint32_t*)(bar + 8);
+    uint64_t* bar_o = bar + 6;
+    uint32_t* tmem_slot = (uint32_t*)(bar + 7);
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const bool leader = threadIdx.x == 0;
     // tile decode
     int sh0, sh1 = 0, q0 = 0, nkv;
     if (PACK) {
@@ -106,18 +111,17 @@ __global__ void __launch_bounds__(160, 2)
         nkv = (L + KB - 1) / KB;
     }
 
-    if (threadIdx.x == 0) {
+    if (leader) {
         mbar_init(bar_q, 1);
-        mbar_init(&bar_k[0], 1);
-        mbar_init(&bar_k[1], 1);
-        mbar_init(&bar_v[0], 1);
-        mbar_init(&bar_v[1], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bar_k[i], 1);
+            mbar_init(&bar_v[i], 1);
+        }
         mbar_init(bar_s, 1);
-        mbar_init(bar_p, 4);
         mbar_init(bar_o, 1);
         fence_barrier_init();
     }
-    if (warp == 4) {
+    if (warp == 0) {
         tmem_alloc(tmem_slot, 256);
         tmem_relinquish();
     }
@@ -127,149 +131,150 @@ __global__ void __launch_bounds__(160, 2)
     const uint32_t tmem = *tmem_slot;
     const uint32_t tS = tmem, tO = tmem + 128;
 
-    if (warp == 4) {
-        if (lane == 0) {
-            prefetch_tensormap(&tmQ);
-            prefetch_tensormap(&tmK);
-            prefetch_tensormap(&tmV);
-            auto load_k = [&](int j) {
-                uint8_t* dst = sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0);
-                mbar_arrive_expect_tx(&bar_k[j & 1], 16384);
-                if (PACK) {
-                    tma_load_2d(dst, &tmK, 0, sh0 * L, &bar_k[j & 1]);
-                    tma_load_2d(dst + 8192, &tmK, 0, sh1 * L, &bar_k[j & 1]);
-                } else {
-                    tma_load_2d(dst, &tmK, 0, sh0 * L + j * KB, &bar_k[j & 1]);
-                }
-            };
-            auto load_v = [&](int j) {
-                uint8_t* dst = sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0);
-                mbar_arrive_expect_tx(&bar_v[j & 1], 16384);
-                if (PACK) {
-                    tma_load_2d(dst, &tmV, 0, sh0 * L, &bar_v[j & 1]);
-                    tma_load_2d(dst + 8192, &tmV, 0, sh1 * L, &bar_v[j & 1]);
-                } else {
-                    tma_load_2d(dst, &tmV, 0, sh0 * L + j * KB, &bar_v[j & 1]);
-                }
-            };
-            mbar_arrive_expect_tx(bar_q, 16384);
-            if (PACK) {
-                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L, bar_q);
-                tma_load_2d(sm + AttnSmem::Q + 8192, &tmQ, 0, sh1 * L, bar_q);
-            } else {
-                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L + q0, bar_q);
-            }
-            load_k(0);
-            load_v(0);
-            if (nkv > 1) {
-                load_k(1);
-                load_v(1);
-            }
-            constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
-            constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
-            const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sP = smem_u32(sm + AttnSmem::P);
-            auto issue_s = [&](int j) {  // S = Q K(j)^T -> tS
-                const uint32_t sK = smem_u32(sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0));
-#pragma unroll
-                for (int k = 0; k < DH / 16; ++k)
-                    mma_f16(tS, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idS, k > 0);
-                mma_commit(bar_s);
-            };
-            // Pipeline: S(j+1) is issued as soon as the softmax has turned S(j)
-            // into P(j), right behind P(j).V(j), so the softmax warps find the
-            // next scores ready once they have folded O(j).  Buffer reuse:
-            //  K(j&1) is free once P(j) exists (S(j) was consumed)   -> load K(j+2);
-            //  V((j+1)&1) held V(j-1), whose P.V finished before the softmax
-            //  produced P(j) (it waits for O(j-1) first)              -> load V(j+1).
-            bool alive = mbar_wait(bar_q, 0, err) && mbar_wait(&bar_k[0], 0, err);
-            if (alive) {
-                tc_fence_after();
-                issue_s(0);
-            }
-            for (int j = 0; j < nkv && alive; ++j) {
-                if (!mbar_wait(bar_p, j & 1, err)) break;
-                tc_fence_after();
-                if (j >= 1 && j + 1 < nkv) load_v(j + 1);
-                if (!mbar_wait(&bar_v[j & 1], (j >> 1) & 1, err)) break;
-                tc_fence_after();
-                const uint32_t sV = smem_u32(sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0));
-#pragma unroll
-                for (int k = 0; k < KB / 16; ++k) {
-                    const uint32_t blk = k >> 2, kk = k & 3;
-                    // A: P rows (K-major, 64 keys per 16 KB block); B: V keys 16k..16k+15 (MN-major)
-                    mma_f16(tO, sdesc_sw128(sP + blk * 16384 + 32 * kk), sdesc_sw128_mn(sV + 2048 * k), idO,
-                            k > 0);
-                }
-                mma_commit(bar_o);
-                if (j + 1 < nkv) {
-                    if (!mbar_wait(&bar_k[(j + 1) & 1], ((j + 1) >> 1) & 1, err)) break;
-                    tc_fence_after();
-                    issue_s(j + 1);
-                    if (j + 2 < nkv) load_k(j + 2);
-                }
-            }
-        }
-    } else {
-        // softmax / epilogue warps: thread r owns query row r (TMEM lane r)
-        const int r = threadIdx.x;
-        int seg = 0, pos, sh = sh0;
-        bool valid;
+    // ---- leader-thread producer / MMA helpers ----
+    auto load_k = [&](int j) {
+        uint8_t* dst = sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0);
+        mbar_arrive_expect_tx(&bar_k[j & 1], 16384);
         if (PACK) {
-            seg = r >> 6;
-            pos = r & 63;
-            sh = seg ? sh1 : sh0;
-            valid = pos < L && (seg == 0 || sh0 + 1 < nsh);
+            tma_load_2d(dst, &tmK, 0, sh0 * L, &bar_k[j & 1]);
+            tma_load_2d(dst + 8192, &tmK, 0, sh1 * L, &bar_k[j & 1]);
         } else {
-            pos = q0 + r;
-            valid = pos < L;
+            tma_load_2d(dst, &tmK, 0, sh0 * L + j * KB, &bar_k[j & 1]);
         }
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        float o[DH];
+    };
+    auto load_v = [&](int j) {
+        uint8_t* dst = sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0);
+        mbar_arrive_expect_tx(&bar_v[j & 1], 16384);
+        if (PACK) {
+            tma_load_2d(dst, &tmV, 0, sh0 * L, &bar_v[j & 1]);
+            tma_load_2d(dst + 8192, &tmV, 0, sh1 * L, &bar_v[j & 1]);
+        } else {
+            tma_load_2d(dst, &tmV, 0, sh0 * L + j * KB, &bar_v[j & 1]);
+        }
+    };
+    constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
+    constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
+    const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sPa = smem_u32(sm + AttnSmem::P);
+    auto issue_s = [&](int j) {  // S = Q K(j)^T -> tS
+        const uint32_t sK = smem_u32(sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0));
 #pragma unroll
-        for (int d = 0; d < DH; ++d) o[d] = 0.f;
-        float m = -INFINITY, l = 0.f;
-        uint8_t* sP = sm + AttnSmem::P;
-        bool ok = true;
-        for (int j = 0; j < nkv && ok; ++j) {
-            if (!mbar_wait(bar_s, j & 1, err)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            // valid key columns of this row in block j: [kbeg, kend) (warp-uniform)
-            int kbeg, kend;
-            if (PACK) {
-                kbeg = seg * 64;
-                kend = kbeg + min(L, 64);
-            } else {
-                kbeg = 0;
-                kend = min(KB, L - j * KB);
-            }
-            // pass 1: row max of the raw scores (the scale is positive)
+        for (int k = 0; k < DH / 16; ++k) mma_f16(tS, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idS, k > 0);
+        mma_commit(bar_s);
+    };
+    auto issue_pv = [&](int j) {  // O (+)= P V(j) -> tO
+        const uint32_t sV = smem_u32(sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0));
+#pragma unroll
+        for (int k = 0; k < KB / 16; ++k) {
+            const uint32_t blk = k >> 2, kk = k & 3;
+            // A: P rows (K-major, 64 keys per 16 KB block); B: V keys 16k..16k+15 (MN-major)
+            mma_f16(tO, sdesc_sw128(sPa + blk * 16384 + 32 * kk), sdesc_sw128_mn(sV + 2048 * k), idO, (j | k) != 0);
+        }
+        mma_commit(bar_o);
+    };
+
+    bool ok = true;  // warp-uniform: TMEM loads and stores are warp-collective
+    if (leader) {
+        prefetch_tensormap(&tmQ);
+        prefetch_tensormap(&tmK);
+        prefetch_tensormap(&tmV);
+        mbar_arrive_expect_tx(bar_q, 16384);
+        if (PACK) {
+            tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L, bar_q);
+            tma_load_2d(sm + AttnSmem::Q + 8192, &tmQ, 0, sh1 * L, bar_q);
+        } else {
+            tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L + q0, bar_q);
+        }
+        load_k(0);
+        load_v(0);
+        if (nkv > 1) {
+            load_k(1);
+            load_v(1);
+        }
+        ok = mbar_wait(bar_q, 0, err) && mbar_wait(&bar_k[0], 0, err);
+        if (ok) issue_s(0);
+    }
+
+    // ---- softmax: thread r owns query row r (TMEM lane r) ----
+    // O accumulates in TMEM over the key blocks.  The exponent offset m is the
+    // first block's row max and is raised (O and l rescaled in place) only
+    // when a later block's max exceeds it by more than kRescaleLog2, so
+    // P <= 2^kRescaleLog2 and O / l is the same softmax.
+    const int r = threadIdx.x;
+    int seg = 0, pos, sh = sh0;
+    bool valid;
+    if (PACK) {
+        seg = r >> 6;
+        pos = r & 63;
+        sh = seg ? sh1 : sh0;
+        valid = pos < L && (seg == 0 || sh0 + 1 < nsh);
+    } else {
+        pos = q0 + r;
+        valid = pos < L;
+    }
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    float m = 0.f, l = 0.f;
+    uint8_t* sP = sm + AttnSmem::P;
+    for (int j = 0; j < nkv; ++j) {
+        // every thread reaches every __syncthreads below, also after a timeout
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(bar_s, j & 1, err));
+        tc_fence_after();
+        // valid key columns of this row in block j: [kbeg, kend) (warp-uniform)
+        int kbeg, kend;
+        if (PACK) {
+            kbeg = seg * 64;
+            kend = kbeg + min(L, 64);
+        } else {
+            kbeg = 0;
+            kend = min(KB, L - j * KB);
+        }
+        if (ok) {
+            uint32_t sv[KB / 32][32];
+#pragma unroll
+            for (int c = 0; c < KB / 32; ++c)
+                if (c * 32 + 32 > kbeg && c * 32 < kend) tmem_ld32(tS + lane_off + c * 32, sv[c]);
+            tmem_ld_wait();
             float mx = -INFINITY;
-#pragma unroll 1
+#pragma unroll
             for (int c = 0; c < KB / 32; ++c) {
                 const int c0 = c * 32;
                 if (c0 + 32 <= kbeg || c0 >= kend) continue;
-                uint32_t v[32];
-                tmem_ld32(tS + lane_off + c0, v);
-                tmem_ld_wait();
                 if (c0 >= kbeg && c0 + 32 <= kend) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[i]));
+                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (c0 + i >= kbeg && c0 + i < kend) mx = fmaxf(mx, __uint_as_float(v[i]));
+                        if (c0 + i >= kbeg && c0 + i < kend) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
                 }
             }
-            float m_new = fmaxf(m, mx * scale_log2);
-            if (m_new == -INFINITY) m_new = 0.f;  // fully masked row (padding rows only)
-            const float alpha = fast_exp2(m - m_new);
-            // pass 2: probabilities -> shared memory (swizzled K-major rows);
-            // chunks outside the valid range get zeros without touching TMEM
-            float rs = 0.f;
+            const float m_blk = mx * scale_log2;  // the scale is positive
+            if (j == 0) {
+                m = m_blk == -INFINITY ? 0.f : m_blk;
+            } else {
+                // O holds P.V of blocks < j: S(j) was issued after P.V(j-1)
+                const bool need = m_blk > m + kRescaleLog2;
+                if (__any_sync(0xffffffffu, need)) {
+                    const float alpha = need ? fast_exp2(m - m_blk) : 1.0f;
+                    if (need) {
+                        m = m_blk;
+                        l *= alpha;
+                    }
 #pragma unroll 1
+                    for (int c = 0; c < DH / 16; ++c) {  // 16 columns at a time: S is still live
+                        uint32_t ov[16];
+                        tmem_ld16(tO + lane_off + c * 16, ov);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                        tmem_st16(tO + lane_off + c * 16, ov);
+                    }
+                    tmem_st_wait();
+                }
+            }
+            // probabilities -> shared memory (swizzled K-major rows); chunks
+            // outside the valid range get zeros
+            float rs = 0.f;
+#pragma unroll
             for (int c = 0; c < KB / 32; ++c) {
                 const int c0 = c * 32;
                 // keys [c0, c0+32) = 4 chunks of 8 in K-block c0/64
@@ -282,18 +287,15 @@ __global__ void __launch_bounds__(160, 2)
                     }
                     continue;
                 }
-                uint32_t v[32];
-                tmem_ld32(tS + lane_off + c0, v);
-                tmem_ld_wait();
                 float p[32];
                 if (c0 >= kbeg && c0 + 32 <= kend) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(__uint_as_float(v[i]), scale_log2, -m_new));
+                    for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         p[i] = (c0 + i >= kbeg && c0 + i < kend)
-                                   ? fast_exp2(fmaf(__uint_as_float(v[i]), scale_log2, -m_new))
+                                   ? fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m))
                                    : 0.f;
                 }
 #pragma unroll
@@ -308,45 +310,58 @@ __global__ void __launch_bounds__(160, 2)
                     *reinterpret_cast<uint4*>(blk + ((ch ^ (r & 7)) << 4)) = u;
                 }
             }
-            l = l * alpha + rs;
-            m = m_new;
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_p);
-            if (!mbar_wait(bar_o, j & 1, err)) {
-                ok = false;
-                break;
-            }
+            l += rs;
+        }
+        fence_proxy_async_smem();  // P visible to the tensor cores
+        tc_fence_before();         // S reads / O stores ordered before the next MMAs
+        __syncthreads();
+        if (leader && ok) {
+            // P.V(j), then S(j+1) behind it.  Buffer reuse: V((j+1)&1) held
+            // V(j-1), whose P.V finished before S(j) did; K(j&1) held K(j),
+            // consumed by S(j).
             tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < DH / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tO + lane_off + c * 32, v);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha + __uint_as_float(v[i]);
+            if (j >= 1 && j + 1 < nkv) load_v(j + 1);
+            ok = mbar_wait(&bar_v[j & 1], (j >> 1) & 1, err);
+            if (ok) issue_pv(j);
+            if (ok && j + 1 < nkv) {
+                ok = mbar_wait(&bar_k[(j + 1) & 1], ((j + 1) >> 1) & 1, err);
+                if (ok) {
+                    issue_s(j + 1);
+                    if (j + 2 < nkv) load_k(j + 2);
+                }
             }
         }
-        if (ok && valid) {
+    }
+    // S(j+1) is issued after P(j).V(j), so only the last P.V is waited for
+    // here (its phase is the only one that can still be open)
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(bar_o, (nkv - 1) & 1, err));
+    if (ok) {
+        tc_fence_after();
+        uint32_t ov[DH / 32][32];
+#pragma unroll
+        for (int c = 0; c < DH / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov[c]);
+        tmem_ld_wait();
+        if (valid) {
             const int h = sh % H;
             const int64_t s = sh / H;
             int64_t tok;
             if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
             else tok = s * NB + pos;
-            const float g = gates[tok * H + h] / l;
+            const float g = (gates ? gates[tok * H + h] : 1.0f) / l;
             uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + h * DH);
 #pragma unroll
-            for (int q = 0; q < DH / 8; ++q)
-                dst[q] = make_uint4(pack2(o[8 * q] * g, o[8 * q + 1] * g, (T*)nullptr),
-                                    pack2(o[8 * q + 2] * g, o[8 * q + 3] * g, (T*)nullptr),
-                                    pack2(o[8 * q + 4] * g, o[8 * q + 5] * g, (T*)nullptr),
-                                    pack2(o[8 * q + 6] * g, o[8 * q + 7] * g, (T*)nullptr));
+            for (int q = 0; q < DH / 8; ++q) {
+                const uint32_t* o = &ov[q >> 2][(q & 3) * 8];
+                dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * g, __uint_as_float(o[1]) * g, (T*)nullptr),
+                                    pack2(__uint_as_float(o[2]) * g, __uint_as_float(o[3]) * g, (T*)nullptr),
+                                    pack2(__uint_as_float(o[4]) * g, __uint_as_float(o[5]) * g, (T*)nullptr),
+                                    pack2(__uint_as_float(o[6]) * g, __uint_as_float(o[7]) * g, (T*)nullptr));
+            }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == 0) {
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, 256);
@@ -397,7 +412,7 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
         attr[dev] = true;
     }
     dim3 grid = PACK ? dim3((unsigned)((nsh + 1) / 2)) : dim3((unsigned)((L + QT - 1) / QT), (unsigned)nsh);
-    kern<<<grid, 160, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
+    kern<<<grid, 128, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
                                               err);
     MBR_CUDA(cudaGetLastError());
 }

@@ -429,6 +429,17 @@ MBR_API int mbr_op_rope(const void* d_x, const float* d_cos, const float* d_sin,
     });
 }
 
+MBR_API int mbr_op_attention(const void* d_q, const void* d_k, const void* d_v, int64_t B, int heads, int N,
+                             int dim_head, float scale, const float* d_gates, void* d_out, int dtype, void* stream) {
+    return guard([&] {
+        need(d_q && d_k && d_v && d_out && B >= 0 && heads > 0 && N > 0 && (dim_head == 32 || dim_head == 64),
+             "bad argument");
+        if (B > 0)
+            mbr::opsapi::attention(d_q, d_k, d_v, B, heads, N, dim_head, scale, d_gates, d_out, dtype,
+                                   (cudaStream_t)stream);
+    });
+}
+
 MBR_API int mbr_rope_tables(int L, int dim_head, float* h_cos, float* h_sin) {
     return guard([&] {
         need(h_cos && h_sin && L > 0 && dim_head > 0 && dim_head % 2 == 0, "bad argument");

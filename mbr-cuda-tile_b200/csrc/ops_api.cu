@@ -4,11 +4,14 @@
 // mask scatter-average, STFT and iSTFT.  Memory-bound kernels: 16-byte
 // vectorised, coalesced, one pass over HBM, reductions in registers.
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <string>
 
 #include "common.cuh"
 #include "ops_api.h"
+#include "attention_tc.h"
+#include "ops.h"
 
 namespace mbr {
 namespace opsapi {
@@ -326,6 +329,24 @@ unsigned grid_for(int64_t work, int threads) {
 // that every device loading this library reserves for the life of the process.
 __device__ __align__(256) float g_istft_frames[kIstftStaticFloats];
 
+// Error word of the tensor-core kernels launched by the stand-alone ops.
+__device__ int g_op_error;
+
+int* op_error_word() {
+    static std::mutex mu;
+    static int* ptrs[kMaxDevices] = {};
+    int dev = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    MBR_CHECK(dev >= 0 && dev < kMaxDevices, "device index out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        MBR_CUDA(cudaGetSymbolAddress(&p, g_op_error));
+        ptrs[dev] = (int*)p;
+    }
+    return ptrs[dev];
+}
+
 }  // namespace
 
 float* istft_static_scratch() {
@@ -345,6 +366,27 @@ float* istft_static_scratch() {
         ptrs[dev] = (float*)p;
     }
     return ptrs[dev];
+}
+
+void attention(const void* q, const void* k, const void* v, int64_t B, int H, int N, int D, float scale,
+               const float* gates, void* out, int dtype, cudaStream_t st) {
+    MBR_CHECK(B > 0 && H > 0 && N > 0 && (D == 32 || D == 64), "attention: bad shape (head dim 32 or 64)");
+    if (scale == 0.0f) scale = 1.0f / std::sqrt((float)D);  // reference default
+    // sequence s = b, position = token within it: the band-axis token map with NB = N
+    if (dtype != DT_F32 && tc::attention_supported(D)) {
+        int* err = op_error_word();
+        tc::attention(q, k, v, B, H, N, D, scale, gates, ops::SEQ_FREQ, N, 1, out, dtype, err, st);
+        MBR_CUDA(cudaStreamSynchronize(st));
+        int e = 0;
+        MBR_CUDA(cudaMemcpy(&e, err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (e != 0) {
+            const int zero = 0;
+            MBR_CUDA(cudaMemcpy(err, &zero, sizeof(int), cudaMemcpyHostToDevice));
+            throw Error(e == 2 ? ERR_CUDA : ERR_TIMEOUT, "attention: tensor-core kernel error " + std::to_string(e));
+        }
+    } else {
+        ops::attention_simt(q, k, v, B, H, N, D, scale, gates, ops::SEQ_FREQ, N, 1, out, dtype, st);
+    }
 }
 
 void add(const void* a, const void* b, void* y, int64_t n, int dtype, cudaStream_t st) {

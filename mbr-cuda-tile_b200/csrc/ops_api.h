@@ -26,6 +26,12 @@ void band_gather(const float2* spec, int B, int C, int F, int T, const int* fi, 
 // masks [S][B*T][2J] (dtype), spec [B][C][F][T] complex -> out [B][S][C][F][T] complex
 void mask_scatter(const float2* spec, const void* masks, int B, int S, int C, int F, int T, const int* rev_off,
                   const int* rev_idx, const float* nbpf, int64_t J, float2* out, int dtype, cudaStream_t st);
+// q, k, v [B][H][N][D] -> out [B][N][H*D] = softmax(q k^T * scale) v, times
+// gates [B][N][H] when non-null (scaled_dot_product_attention followed by
+// apply_gates_and_merge_heads).  16-bit dtypes with D = 64 run the tcgen05
+// kernel and return after the stream drains (a pipeline timeout throws).
+void attention(const void* q, const void* k, const void* v, int64_t B, int H, int N, int D, float scale,
+               const float* gates, void* out, int dtype, cudaStream_t st);
 // STFT frames of an L-sample signal (center, reflect pad n_fft/2)
 int64_t stft_frames(int64_t L, int hop);
 // sig [n][L] -> out [n][1025][T] complex (n_fft 2048, periodic Hann, onesided)

@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(128) attention_simt_kernel(const T* __restrict
     }
     if (!valid) return;
     int64_t tok = token_of(s, qi, mode, NB, Tn);
-    float g = gates[tok * H + h] / l;
+    float g = (gates ? gates[tok * H + h] : 1.0f) / l;
     T* dst = merged + tok * (int64_t)H * DH + h * DH;
 #pragma unroll
     for (int d = 0; d < DH; ++d) dst[d] = from_f32<T>(o[d] * g);

@@ -174,3 +174,69 @@ def test_full_size_sweep_properties(torch_cuda, dtype):
     n = cudasep.op_rms_norm(x, gamma, 1.0)
     nrm = n.float().pow(2).sum(-1).sqrt()
     assert ((nrm - 1).abs() < 8 * TOL[dtype]).all()
+
+
+def _attention_ref(q, k, v, scale, gates):
+    """fp64 softmax attention + head merge, and sum_i p_i |v_i| / l (error scale)."""
+    qd, kd, vd = (t.double().cpu().numpy() for t in (q, k, v))
+    s = np.einsum("bhnd,bhmd->bhnm", qd, kd) * scale
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    o = np.einsum("bhnm,bhmd->bhnd", p, vd)
+    a = np.einsum("bhnm,bhmd->bhnd", p, np.abs(vd))
+    if gates is not None:
+        g = gates.double().cpu().numpy().transpose(0, 2, 1)[..., None]  # [B, H, N, 1]
+        o, a = o * g, a * np.abs(g)
+    B, H, N, D = o.shape
+    merge = lambda t: t.transpose(0, 2, 1, 3).reshape(B, N, H * D)
+    return merge(o), merge(a)
+
+
+@pytest.mark.parametrize(
+    "dtype,B,H,N,D,ramp,gated",
+    [
+        ("fp16", 2, 4, 1301, 64, 12.0, False),  # time path, 11 key blocks, 21-key tail, rescales
+        ("bf16", 1, 3, 801, 64, 12.0, True),  # the std chunk length
+        ("fp16", 1, 2, 801, 64, -12.0, False),  # max in the first block (no rescale)
+        ("fp16", 3, 3, 60, 64, 0.0, True),  # band axis: two sequences per tile, odd count
+        ("bf16", 2, 2, 64, 64, 4.0, False),  # largest packed length
+        ("fp16", 2, 2, 65, 64, 4.0, False),  # smallest blocked length
+        ("fp16", 2, 2, 128, 64, 0.0, True),  # one full key block
+        ("bf16", 1, 2, 1, 64, 0.0, False),  # a single token
+        ("fp32", 1, 2, 300, 64, 6.0, True),  # CUDA-core path
+        ("fp16", 1, 2, 300, 32, 6.0, False),  # head dim 32: CUDA-core path in 16 bits
+    ],
+)
+def test_attention_op(torch_cuda, dtype, B, H, N, D, ramp, gated):
+    """mbr_op_attention (scaled_dot_product_attention + apply_gates_and_merge_heads)
+    against fp64 softmax attention of the same rounded inputs.  The key ramp
+    makes the row max grow (or, negative, shrink) block by block so the
+    tensor-core kernel's deferred rescaling of O runs.  Error bound per output:
+    2u (sum p|v| / l + |ref|), u the unit roundoff of the 16-bit probabilities
+    and outputs (one rounding each); fp32: 1e-5 of max |ref|."""
+    torch = torch_cuda
+    import cudasep
+
+    g = torch.Generator().manual_seed(N * 7 + H)
+    u = torch.randn(D, generator=g)
+    u /= u.norm()
+    q = torch.randn(B, H, N, D, generator=g) + abs(ramp) * u
+    pos = torch.linspace(0.0, 1.0, N)[:, None]
+    k = torch.randn(B, H, N, D, generator=g) + np.sign(ramp) * abs(ramp) * pos * u
+    v = torch.randn(B, H, N, D, generator=g)
+    gates = torch.rand(B, N, H, generator=g) if gated else None
+    tq, tk, tv = (t.to(_tdt(torch, dtype)) for t in (q, k, v))
+    ref, amag = _attention_ref(tq, tk, tv, 1.0 / np.sqrt(D), gates)
+    got = cudasep.op_attention(tq.cuda(), tk.cuda(), tv.cuda(), 0.0,
+                               gates.cuda() if gated else None).double().cpu().numpy()
+    assert got.shape == (B, N, H * D)
+    err = np.abs(got - ref)
+    if dtype == "fp32":
+        assert err.max() <= 1e-5 * np.abs(ref).max(), f"max err {err.max():.3e}"
+    else:
+        u16 = {"fp16": 2.0 ** -11, "bf16": 2.0 ** -8}[dtype]
+        bound = 2 * u16 * (amag + np.abs(ref)) + 1e-7
+        worst = (err / bound).max()
+        print(f"attention {dtype} B{B} H{H} N{N} D{D} ramp {ramp}: worst err/bound {worst:.3f}")
+        assert worst <= 1.0
