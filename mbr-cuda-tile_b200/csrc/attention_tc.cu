@@ -2,9 +2,10 @@
 // 128-key blocks) and the band axis (L <= 64 bands, two sequences packed per
 // 128-row tile with a block-diagonal mask), head dim 64, fp16/bf16.
 //
-// One CTA (4 warps, two CTAs per SM) = one 128-query tile of one (sequence,
-// head) [or two packed band sequences]; thread r owns query row r (TMEM lane
-// r).  Per 128-key block j:
+// One CTA (8 warps, two CTAs per SM) = one 128-query tile of one (sequence,
+// head) [or two packed band sequences]; warps q and q+4 share query rows
+// 32q..32q+31 (TMEM lanes), each taking 64 of the 128 keys of a block and 32
+// of the 64 output columns.  Per 128-key block j:
 //   S = Q K^T          -> TMEM (128 x 128 fp32)
 //   P = exp2(S*c - m)  -> shared memory (16-bit, 128-byte swizzled K-major)
 //   O += P V           -> TMEM (128 x 64 fp32)
@@ -69,6 +70,11 @@ struct IsBf16<__nv_bfloat16> {
     static constexpr bool value = true;
 };
 
+// Barrier `id` (1..15) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -82,7 +88,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 template <typename T, bool PACK>
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(256, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, float scale_log2,
                    const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
@@ -194,12 +200,15 @@ __global__ void __launch_bounds__(128, 2)
         if (ok) issue_s(0);
     }
 
-    // ---- softmax: thread r owns query row r (TMEM lane r) ----
+    // ---- softmax: warps q and q + 4 share query rows 32q..32q+31 (TMEM lane
+    // r = row r); warp half hf = warp / 4 owns key columns [64 hf, 64 hf + 64)
+    // of S (= P block hf) and O columns [32 hf, 32 hf + 32).
     // O accumulates in TMEM over the key blocks.  The exponent offset m is the
     // first block's row max and is raised (O and l rescaled in place) only
     // when a later block's max exceeds it by more than kRescaleLog2, so
     // P <= 2^kRescaleLog2 and O / l is the same softmax.
-    const int r = threadIdx.x;
+    const int q4 = warp & 3, hf = warp >> 2;
+    const int r = q4 * 32 + (threadIdx.x & 31);
     int seg = 0, pos, sh = sh0;
     bool valid;
     if (PACK) {
@@ -211,11 +220,15 @@ __global__ void __launch_bounds__(128, 2)
         pos = q0 + r;
         valid = pos < L;
     }
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    float m = 0.f, l = 0.f;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     uint8_t* sP = sm + AttnSmem::P;
+    // Row-r exchange slots between the two halves: each half writes into the
+    // other half's P row r, which that half overwrites only after reading it.
+    volatile float* x_mine = (volatile float*)(sP + (hf ^ 1) * 16384 + r * 128);
+    volatile float* x_part = (volatile float*)(sP + hf * 16384 + r * 128);
+    float m = 0.f, lh = 0.f;  // lh: this half's share of the row sum
     for (int j = 0; j < nkv; ++j) {
-        // every thread reaches every __syncthreads below, also after a timeout
+        // every thread reaches every barrier below, also after a timeout
         ok = __all_sync(0xffffffffu, ok && mbar_wait(bar_s, j & 1, err));
         tc_fence_after();
         // valid key columns of this row in block j: [kbeg, kend) (warp-uniform)
@@ -227,64 +240,77 @@ __global__ void __launch_bounds__(128, 2)
             kbeg = 0;
             kend = min(KB, L - j * KB);
         }
+        uint32_t sv[2][32];
+        float mx = -INFINITY;
         if (ok) {
-            uint32_t sv[KB / 32][32];
 #pragma unroll
-            for (int c = 0; c < KB / 32; ++c)
-                if (c * 32 + 32 > kbeg && c * 32 < kend) tmem_ld32(tS + lane_off + c * 32, sv[c]);
+            for (int c = 0; c < 2; ++c) {
+                const int c0 = hf * 64 + c * 32;
+                if (c0 + 32 > kbeg && c0 < kend) tmem_ld32(tS + lane_off + c0, sv[c]);
+            }
             tmem_ld_wait();
-            float mx = -INFINITY;
+            float mxp[8];  // 8 independent partial maxima
 #pragma unroll
-            for (int c = 0; c < KB / 32; ++c) {
-                const int c0 = c * 32;
+            for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int c0 = hf * 64 + c * 32;
                 if (c0 + 32 <= kbeg || c0 >= kend) continue;
                 if (c0 >= kbeg && c0 + 32 <= kend) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
+                    for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (c0 + i >= kbeg && c0 + i < kend) mx = fmaxf(mx, __uint_as_float(sv[c][i]));
+                        if (c0 + i >= kbeg && c0 + i < kend) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
                 }
             }
-            const float m_blk = mx * scale_log2;  // the scale is positive
+            mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        }
+        // P.V(j-1) finished before S(j) did, so the P rows are free for the exchange
+        *x_mine = mx;
+        named_barrier_sync(1 + q4, 64);
+        const float mx_row = fmaxf(mx, *x_part);  // same value in both halves
+        if (ok) {
+            const float m_blk = mx_row * scale_log2;  // the scale is positive
             if (j == 0) {
                 m = m_blk == -INFINITY ? 0.f : m_blk;
             } else {
-                // O holds P.V of blocks < j: S(j) was issued after P.V(j-1)
+                // O holds P.V of blocks < j
                 const bool need = m_blk > m + kRescaleLog2;
-                if (__any_sync(0xffffffffu, need)) {
+                if (__any_sync(0xffffffffu, need)) {  // TMEM access is warp-collective
                     const float alpha = need ? fast_exp2(m - m_blk) : 1.0f;
                     if (need) {
                         m = m_blk;
-                        l *= alpha;
+                        lh *= alpha;
                     }
 #pragma unroll 1
-                    for (int c = 0; c < DH / 16; ++c) {  // 16 columns at a time: S is still live
+                    for (int c = 0; c < 2; ++c) {  // this half's 32 O columns, 16 at a time
                         uint32_t ov[16];
-                        tmem_ld16(tO + lane_off + c * 16, ov);
+                        const uint32_t ta = tO + lane_off + hf * 32 + c * 16;
+                        tmem_ld16(ta, ov);
                         tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st16(tO + lane_off + c * 16, ov);
+                        tmem_st16(ta, ov);
                     }
                     tmem_st_wait();
                 }
             }
-            // probabilities -> shared memory (swizzled K-major rows); chunks
+            // probabilities -> P block hf row r (swizzled K-major); chunks
             // outside the valid range get zeros
-            float rs = 0.f;
+            float rsp[8];  // 8 independent partial sums
 #pragma unroll
-            for (int c = 0; c < KB / 32; ++c) {
-                const int c0 = c * 32;
-                // keys [c0, c0+32) = 4 chunks of 8 in K-block c0/64
-                uint8_t* blk = sP + (c0 >> 6) * 16384 + r * 128;
+            for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
+            uint8_t* prow = sP + hf * 16384 + r * 128;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const int c0 = hf * 64 + c * 32;
                 if (c0 + 32 <= kbeg || c0 >= kend) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int ch = ((c0 & 63) >> 3) + q;
-                        *reinterpret_cast<uint4*>(blk + ((ch ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
-                    }
+                    for (int q = 0; q < 4; ++q)
+                        *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
                     continue;
                 }
                 float p[32];
@@ -299,18 +325,17 @@ __global__ void __launch_bounds__(128, 2)
                                    : 0.f;
                 }
 #pragma unroll
-                for (int i = 0; i < 32; ++i) rs += p[i];
+                for (int i = 0; i < 32; ++i) rsp[i & 7] += p[i];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const int ch = ((c0 & 63) >> 3) + q;
                     uint4 u = make_uint4(pack2(p[8 * q], p[8 * q + 1], (T*)nullptr),
                                          pack2(p[8 * q + 2], p[8 * q + 3], (T*)nullptr),
                                          pack2(p[8 * q + 4], p[8 * q + 5], (T*)nullptr),
                                          pack2(p[8 * q + 6], p[8 * q + 7], (T*)nullptr));
-                    *reinterpret_cast<uint4*>(blk + ((ch ^ (r & 7)) << 4)) = u;
+                    *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = u;
                 }
             }
-            l += rs;
+            lh += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
         }
         fence_proxy_async_smem();  // P visible to the tensor cores
         tc_fence_before();         // S reads / O stores ordered before the next MMAs
@@ -333,25 +358,29 @@ __global__ void __launch_bounds__(128, 2)
         }
     }
     // S(j+1) is issued after P(j).V(j), so only the last P.V is waited for
-    // here (its phase is the only one that can still be open)
+    // here (its phase is the only one that can still be open); after it the
+    // P rows are free again for the row-sum exchange.
     ok = __all_sync(0xffffffffu, ok && mbar_wait(bar_o, (nkv - 1) & 1, err));
+    *x_mine = lh;
+    named_barrier_sync(1 + q4, 64);
+    const float lo = *x_part;
+    const float l = hf == 0 ? lh + lo : lo + lh;
     if (ok) {
         tc_fence_after();
-        uint32_t ov[DH / 32][32];
-#pragma unroll
-        for (int c = 0; c < DH / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov[c]);
+        uint32_t ov[32];
+        tmem_ld32(tO + lane_off + hf * 32, ov);
         tmem_ld_wait();
         if (valid) {
-            const int h = sh % H;
+            const int hd = sh % H;
             const int64_t s = sh / H;
             int64_t tok;
             if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
             else tok = s * NB + pos;
-            const float g = (gates ? gates[tok * H + h] : 1.0f) / l;
-            uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + h * DH);
+            const float g = (gates ? gates[tok * H + hd] : 1.0f) / l;
+            uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH + hf * 32);
 #pragma unroll
-            for (int q = 0; q < DH / 8; ++q) {
-                const uint32_t* o = &ov[q >> 2][(q & 3) * 8];
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t* o = &ov[q * 8];
                 dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * g, __uint_as_float(o[1]) * g, (T*)nullptr),
                                     pack2(__uint_as_float(o[2]) * g, __uint_as_float(o[3]) * g, (T*)nullptr),
                                     pack2(__uint_as_float(o[4]) * g, __uint_as_float(o[5]) * g, (T*)nullptr),
@@ -412,7 +441,7 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
         attr[dev] = true;
     }
     dim3 grid = PACK ? dim3((unsigned)((nsh + 1) / 2)) : dim3((unsigned)((L + QT - 1) / QT), (unsigned)nsh);
-    kern<<<grid, 128, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
+    kern<<<grid, 256, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
                                               err);
     MBR_CUDA(cudaGetLastError());
 }
