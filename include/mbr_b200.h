@@ -205,6 +205,19 @@ MBR_API int mbr_op_sigmoid_gate(const void* d_x, const void* d_gate, void* d_y, 
 MBR_API int mbr_op_rope(const void* d_x, const float* d_cos, const float* d_sin, void* d_y, int64_t seqs, int L,
                         int heads, int dtype, void* stream);
 
+/* Linear layer: y [rows][out] = act(x [rows][in] . w[out][in]^T + bias[out])
+ * with act MBR_ACT_NONE / MBR_ACT_GELU (exact erf form) / MBR_ACT_TANH; d_bias
+ * (fp32) may be null; x, w, y have the given dtype.  Replaces linear and
+ * linear_gelu (src/mbr_cuda_tile.h:63,68; src/mbr_cuda_tile.cu:6851,6926).
+ * fp16/bf16 with in % 16 == 0, out % 8 == 0 and 16-byte aligned pointers run
+ * the tcgen05 GEMM, other shapes and fp32 the CUDA-core GEMM; the call returns
+ * after the stream drains. */
+#define MBR_ACT_NONE 0
+#define MBR_ACT_GELU 1
+#define MBR_ACT_TANH 2
+MBR_API int mbr_op_linear(const void* d_x, const void* d_w, const float* d_bias, void* d_y, int64_t rows, int in,
+                          int out, int act, int dtype, void* stream);
+
 /* Multi-head attention with the head merge: q, k, v [B][heads][N][dim_head]
  * (dtype), out [B][N][heads*dim_head] = softmax(q k^T * scale) v, multiplied
  * by gates [B][N][heads] (fp32, already sigmoid'ed) when d_gates is non-null.

@@ -70,6 +70,13 @@ struct IsBf16<__nv_bfloat16> {
     static constexpr bool value = true;
 };
 
+// One lane of the (converged) warp returns true.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}" : "=r"(pred));
+    return pred != 0;
+}
+
 // Barrier `id` (1..15) over `count` threads (a multiple of 32).
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -161,19 +168,26 @@ __global__ void __launch_bounds__(256, 2)
     constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
     constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
     const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sPa = smem_u32(sm + AttnSmem::P);
+    // descriptor bases; the start-address field (16-byte units) advances by 2
+    // per 32 bytes along K and by 1024 per 16 KB P block
+    const uint64_t dQ = sdesc_sw128(sQ);
+    const uint64_t dK0 = sdesc_sw128(smem_u32(sm + AttnSmem::K0)), dK1 = sdesc_sw128(smem_u32(sm + AttnSmem::K1));
+    const uint64_t dV0 = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V0)),
+                   dV1 = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V1));
+    const uint64_t dP = sdesc_sw128(sPa);
     auto issue_s = [&](int j) {  // S = Q K(j)^T -> tS
-        const uint32_t sK = smem_u32(sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0));
+        const uint64_t dK = (j & 1) ? dK1 : dK0;
 #pragma unroll
-        for (int k = 0; k < DH / 16; ++k) mma_f16(tS, sdesc_sw128(sQ + 32 * k), sdesc_sw128(sK + 32 * k), idS, k > 0);
+        for (int k = 0; k < DH / 16; ++k) mma_f16(tS, dQ + 2 * k, dK + 2 * k, idS, k > 0);
         mma_commit(bar_s);
     };
     auto issue_pv = [&](int j) {  // O (+)= P V(j) -> tO
-        const uint32_t sV = smem_u32(sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0));
+        const uint64_t dV = (j & 1) ? dV1 : dV0;
 #pragma unroll
         for (int k = 0; k < KB / 16; ++k) {
             const uint32_t blk = k >> 2, kk = k & 3;
             // A: P rows (K-major, 64 keys per 16 KB block); B: V keys 16k..16k+15 (MN-major)
-            mma_f16(tO, sdesc_sw128(sPa + blk * 16384 + 32 * kk), sdesc_sw128_mn(sV + 2048 * k), idO, (j | k) != 0);
+            mma_f16(tO, dP + blk * 1024 + 2 * kk, dV + 128 * k, idO, (j | k) != 0);
         }
         mma_commit(bar_o);
     };
@@ -340,21 +354,25 @@ __global__ void __launch_bounds__(256, 2)
         fence_proxy_async_smem();  // P visible to the tensor cores
         tc_fence_before();         // S reads / O stores ordered before the next MMAs
         __syncthreads();
-        if (leader && ok) {
-            // P.V(j), then S(j+1) behind it.  Buffer reuse: V((j+1)&1) held
+        if (warp == 0 && ok) {
+            // P.V(j), then S(j+1) behind it, issued by one elected lane of
+            // warp 0 (warp-uniform operands).  Buffer reuse: V((j+1)&1) held
             // V(j-1), whose P.V finished before S(j) did; K(j&1) held K(j),
             // consumed by S(j).
             tc_fence_after();
-            if (j >= 1 && j + 1 < nkv) load_v(j + 1);
-            ok = mbar_wait(&bar_v[j & 1], (j >> 1) & 1, err);
-            if (ok) issue_pv(j);
-            if (ok && j + 1 < nkv) {
-                ok = mbar_wait(&bar_k[(j + 1) & 1], ((j + 1) >> 1) & 1, err);
-                if (ok) {
+            if (leader && j >= 1 && j + 1 < nkv) load_v(j + 1);
+            bool okw = __all_sync(0xffffffffu, mbar_wait(&bar_v[j & 1], (j >> 1) & 1, err));
+            if (okw && elect_one()) issue_pv(j);
+            __syncwarp();
+            if (okw && j + 1 < nkv) {
+                okw = __all_sync(0xffffffffu, mbar_wait(&bar_k[(j + 1) & 1], ((j + 1) >> 1) & 1, err));
+                if (okw && elect_one()) {
                     issue_s(j + 1);
                     if (j + 2 < nkv) load_k(j + 2);
                 }
+                __syncwarp();
             }
+            ok = okw;
         }
     }
     // S(j+1) is issued after P(j).V(j), so only the last P.V is waited for

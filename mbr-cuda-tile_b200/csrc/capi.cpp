@@ -429,6 +429,14 @@ MBR_API int mbr_op_rope(const void* d_x, const float* d_cos, const float* d_sin,
     });
 }
 
+MBR_API int mbr_op_linear(const void* d_x, const void* d_w, const float* d_bias, void* d_y, int64_t rows, int in,
+                          int out, int act, int dtype, void* stream) {
+    return guard([&] {
+        need(d_x && d_w && d_y && rows >= 0 && in > 0 && out > 0 && act >= 0 && act <= 2, "bad argument");
+        mbr::opsapi::linear(d_x, d_w, d_bias, d_y, rows, in, out, act, dtype, (cudaStream_t)stream);
+    });
+}
+
 MBR_API int mbr_op_attention(const void* d_q, const void* d_k, const void* d_v, int64_t B, int heads, int N,
                              int dim_head, float scale, const float* d_gates, void* d_out, int dtype, void* stream) {
     return guard([&] {

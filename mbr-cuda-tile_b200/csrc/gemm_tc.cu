@@ -526,10 +526,14 @@ bool gemm_supported(int epi) { return epi >= ops::EPI_F32 && epi <= ops::EPI_QKV
 
 void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, GemmLaunch& L, size_t& L_first) {
     MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "tc gemm needs fp16 or bf16 operands");
+    // 16-bit staged stores pair two 32-column chunks per 128-byte box, so a
+    // warp's column half (BN / 2) must hold an even number of chunks: BN 192
+    // would leave a half-filled box spilling into the neighbouring columns.
+    const bool staged16 = p.c_dtype >= 0 && p.c_dtype != DT_F32;
     int bn;
     if (p.epi == ops::EPI_GLU_F32) bn = 128;
     else if (p.maxN % 256 == 0) bn = 256;
-    else if (p.maxN % 192 == 0) bn = 192;
+    else if (p.maxN % 192 == 0 && !staged16) bn = 192;
     else if (p.maxN % 128 == 0 || p.maxN < 256) bn = 128;
     else bn = 256;
     L.bn = bn;

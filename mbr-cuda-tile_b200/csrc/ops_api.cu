@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "ops_api.h"
 #include "attention_tc.h"
+#include "gemm_tc.h"
 #include "ops.h"
 
 namespace mbr {
@@ -368,6 +369,33 @@ float* istft_static_scratch() {
     return ptrs[dev];
 }
 
+namespace {
+// Launch descriptors of the stand-alone GEMM (one group + its tile list),
+// grown on demand per device and reused by every call on that device.
+struct LinearScratch {
+    std::mutex mu;
+    ops::GemmGroup* d_group = nullptr;
+    int4* d_tiles = nullptr;
+    size_t tile_cap = 0;
+};
+LinearScratch& linear_scratch(int dev) {
+    static LinearScratch s[kMaxDevices];
+    return s[dev];
+}
+
+void check_op_error(cudaStream_t st) {
+    MBR_CUDA(cudaStreamSynchronize(st));
+    int* err = op_error_word();
+    int e = 0;
+    MBR_CUDA(cudaMemcpy(&e, err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e != 0) {
+        const int zero = 0;
+        MBR_CUDA(cudaMemcpy(err, &zero, sizeof(int), cudaMemcpyHostToDevice));
+        throw Error(e == 2 ? ERR_CUDA : ERR_TIMEOUT, "tensor-core kernel error " + std::to_string(e));
+    }
+}
+}  // namespace
+
 void attention(const void* q, const void* k, const void* v, int64_t B, int H, int N, int D, float scale,
                const float* gates, void* out, int dtype, cudaStream_t st) {
     MBR_CHECK(B > 0 && H > 0 && N > 0 && (D == 32 || D == 64), "attention: bad shape (head dim 32 or 64)");
@@ -376,17 +404,67 @@ void attention(const void* q, const void* k, const void* v, int64_t B, int H, in
     if (dtype != DT_F32 && tc::attention_supported(D)) {
         int* err = op_error_word();
         tc::attention(q, k, v, B, H, N, D, scale, gates, ops::SEQ_FREQ, N, 1, out, dtype, err, st);
-        MBR_CUDA(cudaStreamSynchronize(st));
-        int e = 0;
-        MBR_CUDA(cudaMemcpy(&e, err, sizeof(int), cudaMemcpyDeviceToHost));
-        if (e != 0) {
-            const int zero = 0;
-            MBR_CUDA(cudaMemcpy(err, &zero, sizeof(int), cudaMemcpyHostToDevice));
-            throw Error(e == 2 ? ERR_CUDA : ERR_TIMEOUT, "attention: tensor-core kernel error " + std::to_string(e));
-        }
+        check_op_error(st);
     } else {
         ops::attention_simt(q, k, v, B, H, N, D, scale, gates, ops::SEQ_FREQ, N, 1, out, dtype, st);
     }
+}
+
+
+void linear(const void* x, const void* w, const float* bias, void* y, int64_t rows, int in, int out, int act,
+            int dtype, cudaStream_t st) {
+    MBR_CHECK(rows >= 0 && rows < (1ll << 31) && in > 0 && out > 0 && act >= 0 && act <= 2, "linear: bad argument");
+    if (rows == 0) return;
+    int dev = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    MBR_CHECK(dev >= 0 && dev < kMaxDevices, "device index out of range");
+    LinearScratch& S = linear_scratch(dev);
+    std::lock_guard<std::mutex> lock(S.mu);
+    if (!S.d_group) MBR_CUDA(cudaMalloc(&S.d_group, sizeof(ops::GemmGroup)));
+    ops::GemmGroup g{};
+    g.A = x;
+    g.B = w;
+    g.C = y;
+    g.bias = bias;
+    g.lda = in;
+    g.ldb = in;
+    g.ldc = out;
+    g.M = (int)rows;
+    g.N = out;
+    g.K = in;
+    const int epi = act == 1 ? ops::EPI_GELU_T : act == 2 ? ops::EPI_TANH_T : ops::EPI_T;
+    MBR_CUDA(cudaMemcpyAsync(S.d_group, &g, sizeof(g), cudaMemcpyHostToDevice, st));
+    auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+    const bool tc_ok = dtype != DT_F32 && in % 16 == 0 && out % 8 == 0 && al16(x) && al16(w) && al16(y);
+    if (tc_ok) {
+        tc::GemmPlanTC p;
+        p.groups = S.d_group;
+        p.h_groups = &g;
+        p.ngroups = 1;
+        p.maxM = g.M;
+        p.maxN = out;
+        p.epi = epi;
+        p.a_base = x, p.a_rows = rows, p.a_cols = in;
+        p.b_base = w, p.b_rows = out, p.b_cols = in;
+        p.c_base = y, p.c_rows = rows, p.c_cols = out, p.c_groups = 1;
+        p.c_row_stride = out, p.c_group_stride = rows * out, p.c_dtype = dtype;
+        std::vector<int4> tiles;
+        tc::GemmLaunch L;
+        size_t first = 0;
+        tc::gemm_prepare(p, dtype, tiles, L, first);
+        if (tiles.size() > S.tile_cap) {
+            if (S.d_tiles) MBR_CUDA(cudaFree(S.d_tiles));
+            S.d_tiles = nullptr;
+            MBR_CUDA(cudaMalloc(&S.d_tiles, tiles.size() * sizeof(int4)));
+            S.tile_cap = tiles.size();
+        }
+        MBR_CUDA(cudaMemcpyAsync(S.d_tiles, tiles.data(), tiles.size() * sizeof(int4), cudaMemcpyHostToDevice, st));
+        L.tiles = S.d_tiles;
+        tc::gemm_launch(L, dtype, op_error_word(), st);
+    } else {
+        ops::gemm_simt(S.d_group, 1, g.M, out, dtype, epi, st);
+    }
+    check_op_error(st);  // the scratch (and the pageable sources above) are reused next call
 }
 
 void add(const void* a, const void* b, void* y, int64_t n, int dtype, cudaStream_t st) {

@@ -32,6 +32,13 @@ void mask_scatter(const float2* spec, const void* masks, int B, int S, int C, in
 // kernel and return after the stream drains (a pipeline timeout throws).
 void attention(const void* q, const void* k, const void* v, int64_t B, int H, int N, int D, float scale,
                const float* gates, void* out, int dtype, cudaStream_t st);
+// y [rows][out] = act(x [rows][in] . w[out][in]^T + bias[out]), act 0 none,
+// 1 exact GELU, 2 tanh; y has the input dtype.  16-bit inputs whose shapes
+// meet the TMA rules (in % 16 == 0, out % 8 == 0, 16-byte aligned rows) run
+// the tcgen05 GEMM, everything else the CUDA-core GEMM; both return after the
+// stream drains (the launch descriptors live in per-device scratch).
+void linear(const void* x, const void* w, const float* bias, void* y, int64_t rows, int in, int out, int act,
+            int dtype, cudaStream_t st);
 // STFT frames of an L-sample signal (center, reflect pad n_fft/2)
 int64_t stft_frames(int64_t L, int hop);
 // sig [n][L] -> out [n][1025][T] complex (n_fft 2048, periodic Hann, onesided)

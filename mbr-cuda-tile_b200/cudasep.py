@@ -29,7 +29,7 @@ EXPORTS = [
     "mbr_forward_chunk", "mbr_forward_tap", "mbr_separate_device", "mbr_separate", "mbr_shard_info",
     "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_backend", "mbr_last_launches",
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
-    "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_op_attention",
+    "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_op_attention", "mbr_op_linear",
     "mbr_rope_tables",
     "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft", "mbr_op_istft_noalloc",
     "mbr_plan_shard", "mbr_wav_info", "mbr_wav_read", "mbr_wav_write",
@@ -82,6 +82,7 @@ def lib():
         L.mbr_op_gelu.argtypes = [fp, fp, i64, c_int, vp]
         L.mbr_op_sigmoid_gate.argtypes = [fp, fp, fp, i64, c_int, c_int, c_int, vp]
         L.mbr_op_rope.argtypes = [fp, fp, fp, fp, i64, c_int, c_int, c_int, vp]
+        L.mbr_op_linear.argtypes = [fp, fp, fp, fp, i64, c_int, c_int, c_int, c_int, vp]
         L.mbr_op_attention.argtypes = [fp, fp, fp, i64, c_int, c_int, c_int, c_float, fp, fp, c_int, vp]
         L.mbr_rope_tables.argtypes = [c_int, c_int, fp, fp]
         L.mbr_op_band_gather.argtypes = [vp, fp, c_int, c_int, fp, c_int, vp]
@@ -176,6 +177,21 @@ def op_rope(x, cos_t, sin_t, y=None, stream=None):
     seqs, L, heads = x.shape[0], x.shape[1], x.shape[2]
     _check(lib().mbr_op_rope(_ptr(x), _ptr(cos_t), _ptr(sin_t), _ptr(y), seqs, L, heads, _dt(x), _stream(stream)))
     return y
+
+
+ACT_NONE, ACT_GELU, ACT_TANH = 0, 1, 2
+
+
+def op_linear(x, w, bias=None, act=ACT_NONE, out=None, stream=None):
+    """x [rows, in] . w[out, in]^T + bias, then act; same dtype as x."""
+    import torch
+
+    rows, fin = x.shape
+    fout = w.shape[0]
+    out = torch.empty((rows, fout), dtype=x.dtype, device=x.device) if out is None else out
+    b = _ptr(bias) if bias is not None else None
+    _check(lib().mbr_op_linear(_ptr(x), _ptr(w), b, _ptr(out), rows, fin, fout, int(act), _dt(x), _stream(stream)))
+    return out
 
 
 def op_attention(q, k, v, scale=0.0, gates=None, out=None, stream=None):

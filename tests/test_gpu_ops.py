@@ -240,3 +240,43 @@ def test_attention_op(torch_cuda, dtype, B, H, N, D, ramp, gated):
         worst = (err / bound).max()
         print(f"attention {dtype} B{B} H{H} N{N} D{D} ramp {ramp}: worst err/bound {worst:.3f}")
         assert worst <= 1.0
+
+
+@pytest.mark.parametrize(
+    "dtype,rows,fin,fout,act",
+    [
+        ("fp16", 48060, 384, 1536, 1),  # FFN1 of the std chunk (GELU)
+        ("bf16", 3001, 1536, 384, 0),  # FFN2 shape, ragged rows
+        ("fp16", 801, 384, 1536, 2),  # mask-estimator hidden layer (tanh)
+        ("bf16", 1000, 384, 1536, 0),
+        ("fp16", 130, 64, 200, 1),  # one K block, ragged N (200 = 192 + 8)
+        ("fp16", 77, 100, 60, 0),  # K not a multiple of 16: CUDA-core path
+        ("fp32", 500, 384, 96, 1),  # fp32: CUDA-core path
+    ],
+)
+def test_linear_op(torch_cuda, dtype, rows, fin, fout, act):
+    """mbr_op_linear (linear / linear_gelu / tanh) against fp64 math on the same
+    rounded operands: one rounding of the output (TOL) plus the fp32
+    accumulation (K * 2^-23 of sum |x w|)."""
+    torch = torch_cuda
+    import cudasep
+
+    g = torch.Generator().manual_seed(rows + fin + fout)
+    x = torch.randn(rows, fin, generator=g).to(_tdt(torch, dtype))
+    w = (torch.randn(fout, fin, generator=g) * (1.0 / np.sqrt(fin))).to(_tdt(torch, dtype))
+    b = torch.randn(fout, generator=g) * 0.1
+    got = cudasep.op_linear(x.cuda(), w.cuda(), b.cuda(), act).double().cpu().numpy()
+    xd, wd = x.double().numpy(), w.double().numpy()
+    pre = xd @ wd.T + b.double().numpy()
+    if act == 1:
+        from scipy.special import erf
+
+        ref = 0.5 * pre * (1 + erf(pre / np.sqrt(2)))
+    elif act == 2:
+        ref = np.tanh(pre)
+    else:
+        ref = pre
+    acc = fin * 2.0 ** -23 * (np.abs(xd) @ np.abs(wd).T)
+    bound = TOL[dtype] * np.maximum(np.abs(ref), 1e-3) * 1.01 + acc + 1e-6
+    err = np.abs(got - ref)
+    assert np.all(err <= bound), f"linear {dtype} {rows}x{fin}x{fout} act {act}: max err/bound {(err / bound).max():.3f}"
