@@ -1,17 +1,17 @@
 // attention_tc.cu — tcgen05 flash attention for the time axis (L = T frames,
-// 128-key blocks) and the band axis (L <= 64 bands, two sequences packed per
-// 128-row tile with a block-diagonal mask), head dim 64, fp16/bf16.
+// 64-key blocks) and the band axis (L <= 64 bands, two sequences packed per
+// 128-row tile, each attending only its own key block), head dim 64,
+// fp16/bf16.
 //
-// One CTA (8 warps, two CTAs per SM) = one 128-query tile of one (sequence,
-// head) [or two packed band sequences]; warps q and q+4 share query rows
-// 32q..32q+31 (TMEM lanes), each taking 64 of the 128 keys of a block and 32
-// of the 64 output columns.  Per 128-key block j:
-//   S = Q K^T          -> TMEM (128 x 128 fp32)
-//   P = exp2(S*c - m)  -> shared memory (16-bit, 128-byte swizzled K-major)
-//   O += P V           -> TMEM (128 x 64 fp32)
-// Thread 0 issues the TMA loads and, after the CTA barrier that publishes
-// P(j), the MMAs P.V(j) and S(j+1); K and V blocks are double buffered.
-// V keeps the [seq][H][L][64] layout of q and k: its 128-key tile is the
+// One CTA (two per SM) = one 128-query tile of one (sequence, head) [or two
+// packed band sequences]: warps 0-3 run the softmax (thread r = query row r =
+// TMEM lane r), warp 4 issues the TMA loads and the MMAs.  Per 64-key block j:
+//   S(j) = Q K(j)^T       -> TMEM buffer j%2 (128 x 64 fp32)
+//   P(j) = exp2(S*c - m)  -> shared buffer j%2 (16-bit, 128-byte swizzled)
+//   O   += P(j) V(j)      -> TMEM (128 x 64 fp32)
+// S(j+2) is computed while the softmax works on S(j+1), so the softmax warps
+// do not wait for the tensor cores; K and V stream through a 4-stage ring.
+// V keeps the [seq][H][L][64] layout of q and k: its 64-key tile is the
 // MN-major B operand of the P.V product.  The epilogue multiplies by the
 // sigmoid gate and writes the merged-head row of each token
 // (apply_gates_and_merge_heads).  All waits are bounded (error word instead of
@@ -34,7 +34,8 @@ namespace {
 
 constexpr int DH = 64;
 constexpr int QT = 128;  // queries per tile
-constexpr int KB = 128;  // keys per block
+constexpr int KB = 64;   // keys per block (one 128-byte swizzle atom of P per row)
+constexpr int NS = 4;    // K / V pipeline stages
 // O and l are rescaled only when a block's row max (log2 units) exceeds the
 // running offset by more than this, bounding the probabilities by 2^8.
 constexpr float kRescaleLog2 = 8.0f;
@@ -42,15 +43,15 @@ constexpr float kRescaleLog2 = 8.0f;
 // Two CTAs share an SM, so the layout carries no alignment slack: the kernel
 // checks that the dynamic window is 1024-byte aligned instead.
 struct AttnSmem {
-    static constexpr int Q = 0;
-    static constexpr int K0 = 16384;  // K and V blocks are double buffered
-    static constexpr int K1 = 32768;
-    static constexpr int V0 = 49152;
-    static constexpr int V1 = 65536;
-    static constexpr int P = 81920;  // two 16 KB K-blocks (keys 0-63, 64-127)
-    static constexpr int BAR = 114688;
-    static constexpr int TOTAL = BAR + 128;
+    static constexpr int Q = 0;                    // 128 x 64 (16 KB)
+    static constexpr int K = 16384;                // NS stages of 64 x 64 (8 KB)
+    static constexpr int V = K + NS * 8192;        // NS stages of 64 x 64
+    static constexpr int P = V + NS * 8192;        // 2 buffers of 128 x 64 (16 KB)
+    static constexpr int BAR = P + 2 * 16384;      // 114688
+    static constexpr int TOTAL = BAR + 256;
 };
+// TMEM columns: S double buffer at 0 and 64, O at 128 (256 allocated).
+constexpr uint32_t kTmemCols = 256;
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
     __half2 h = __floats2half2_rn(a, b);
@@ -77,11 +78,6 @@ __device__ __forceinline__ bool elect_one() {
     return pred != 0;
 }
 
-// Barrier `id` (1..15) over `count` threads (a multiple of 32).
-__device__ __forceinline__ void named_barrier_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -95,7 +91,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 template <typename T, bool PACK>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, float scale_log2,
                    const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
@@ -103,240 +99,248 @@ __global__ void __launch_bounds__(256, 2)
     if (!smem_aligned_or_flag(smem_raw, err)) return;  // uniform over the CTA
     uint8_t* sm = smem_raw;
     uint64_t* bar = (uint64_t*)(sm + AttnSmem::BAR);
-    uint64_t* bar_q = bar + 0;
-    uint64_t* bar_k = bar + 1;  // [2]
-    uint64_t* bar_v = bar + 3;  // [2]
-    uint64_t* bar_s = bar + 5;
-    uint64_t* bar_o = bar + 6;
-    uint32_t* tmem_slot = (uint32_t*)(bar + 7);
+    uint64_t* bar_q = bar;            // Q tile landed
+    uint64_t* bar_k = bar + 1;        // [NS] K stage landed
+    uint64_t* bar_v = bar + 1 + NS;   // [NS] V stage landed
+    uint64_t* bar_s = bar + 1 + 2 * NS;  // [2] S buffer computed
+    uint64_t* bar_p = bar_s + 2;      // [2] softmax done with S buffer, P buffer written (4 warps)
+    uint64_t* bar_o = bar_p + 2;      // [2] P.V from P buffer complete
+    uint32_t* tmem_slot = (uint32_t*)(bar_o + 2);
 
-    const int warp = threadIdx.x >> 5;
-    const bool leader = threadIdx.x == 0;
-    // tile decode
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // tile decode: time axis = one 128-query tile of sequence-head sh0, keys in
+    // 64-key blocks; band axis (PACK) = sequence-heads sh0 (rows 0-63) and sh1
+    // (rows 64-127), key block j = the keys of sh_j
     int sh0, sh1 = 0, q0 = 0, nkv;
     if (PACK) {
         sh0 = blockIdx.x * 2;
         sh1 = min(sh0 + 1, nsh - 1);
-        nkv = 1;
+        nkv = 2;
     } else {
         sh0 = blockIdx.y;
         q0 = blockIdx.x * QT;
         nkv = (L + KB - 1) / KB;
     }
 
-    if (leader) {
+    if (threadIdx.x == 0) {
         mbar_init(bar_q, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NS; ++i) {
             mbar_init(&bar_k[i], 1);
             mbar_init(&bar_v[i], 1);
         }
-        mbar_init(bar_s, 1);
-        mbar_init(bar_o, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bar_s[i], 1);
+            mbar_init(&bar_p[i], 4);
+            mbar_init(&bar_o[i], 1);
+        }
         fence_barrier_init();
     }
-    if (warp == 0) {
-        tmem_alloc(tmem_slot, 256);
+    if (warp == 4) {
+        tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS = tmem, tO = tmem + 128;
+    const uint32_t tO = tmem + 128;
 
-    // ---- leader-thread producer / MMA helpers ----
-    auto load_k = [&](int j) {
-        uint8_t* dst = sm + ((j & 1) ? AttnSmem::K1 : AttnSmem::K0);
-        mbar_arrive_expect_tx(&bar_k[j & 1], 16384);
-        if (PACK) {
-            tma_load_2d(dst, &tmK, 0, sh0 * L, &bar_k[j & 1]);
-            tma_load_2d(dst + 8192, &tmK, 0, sh1 * L, &bar_k[j & 1]);
-        } else {
-            tma_load_2d(dst, &tmK, 0, sh0 * L + j * KB, &bar_k[j & 1]);
-        }
-    };
-    auto load_v = [&](int j) {
-        uint8_t* dst = sm + ((j & 1) ? AttnSmem::V1 : AttnSmem::V0);
-        mbar_arrive_expect_tx(&bar_v[j & 1], 16384);
-        if (PACK) {
-            tma_load_2d(dst, &tmV, 0, sh0 * L, &bar_v[j & 1]);
-            tma_load_2d(dst + 8192, &tmV, 0, sh1 * L, &bar_v[j & 1]);
-        } else {
-            tma_load_2d(dst, &tmV, 0, sh0 * L + j * KB, &bar_v[j & 1]);
-        }
-    };
-    constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
-    constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
-    const uint32_t sQ = smem_u32(sm + AttnSmem::Q), sPa = smem_u32(sm + AttnSmem::P);
-    // descriptor bases; the start-address field (16-byte units) advances by 2
-    // per 32 bytes along K and by 1024 per 16 KB P block
-    const uint64_t dQ = sdesc_sw128(sQ);
-    const uint64_t dK0 = sdesc_sw128(smem_u32(sm + AttnSmem::K0)), dK1 = sdesc_sw128(smem_u32(sm + AttnSmem::K1));
-    const uint64_t dV0 = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V0)),
-                   dV1 = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V1));
-    const uint64_t dP = sdesc_sw128(sPa);
-    auto issue_s = [&](int j) {  // S = Q K(j)^T -> tS
-        const uint64_t dK = (j & 1) ? dK1 : dK0;
+    if (warp == 4) {
+        // ---- producer + MMA warp: one elected lane issues, all lanes wait ----
+        auto wait_all = [&](uint64_t* b, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(b, parity, err));
+        };
+        auto key_row = [&](int j) { return PACK ? (j ? sh1 : sh0) * L : sh0 * L + j * KB; };
+        auto load_k = [&](int j) {
+            const int st = j % NS;
+            mbar_arrive_expect_tx(&bar_k[st], 8192);
+            tma_load_2d(sm + AttnSmem::K + st * 8192, &tmK, 0, key_row(j), &bar_k[st]);
+        };
+        auto load_v = [&](int j) {
+            const int st = j % NS;
+            mbar_arrive_expect_tx(&bar_v[st], 8192);
+            tma_load_2d(sm + AttnSmem::V + st * 8192, &tmV, 0, key_row(j), &bar_v[st]);
+        };
+        constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
+        constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
+        // descriptor bases; the start-address field (16-byte units) advances
+        // by 2 per 32 bytes along K, by 512 per 8 KB stage, 1024 per 16 KB
+        const uint64_t dQ = sdesc_sw128(smem_u32(sm + AttnSmem::Q));
+        const uint64_t dK = sdesc_sw128(smem_u32(sm + AttnSmem::K));
+        const uint64_t dV = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V));
+        const uint64_t dP = sdesc_sw128(smem_u32(sm + AttnSmem::P));
+        auto issue_s = [&](int j) {  // S buffer (j & 1) = Q K(j)^T
+            const uint64_t k0 = dK + (uint64_t)(512 * (j % NS));
+            const uint32_t d = tmem + (uint32_t)(64 * (j & 1));
 #pragma unroll
-        for (int k = 0; k < DH / 16; ++k) mma_f16(tS, dQ + 2 * k, dK + 2 * k, idS, k > 0);
-        mma_commit(bar_s);
-    };
-    auto issue_pv = [&](int j) {  // O (+)= P V(j) -> tO
-        const uint64_t dV = (j & 1) ? dV1 : dV0;
+            for (int k = 0; k < DH / 16; ++k) mma_f16(d, dQ + 2 * k, k0 + 2 * k, idS, k > 0);
+            mma_commit(&bar_s[j & 1]);
+        };
+        auto issue_pv = [&](int j) {  // O (+)= P(j & 1) V(j)
+            const uint64_t a0 = dP + (uint64_t)(1024 * (j & 1));
+            const uint64_t b0 = dV + (uint64_t)(512 * (j % NS));
 #pragma unroll
-        for (int k = 0; k < KB / 16; ++k) {
-            const uint32_t blk = k >> 2, kk = k & 3;
-            // A: P rows (K-major, 64 keys per 16 KB block); B: V keys 16k..16k+15 (MN-major)
-            mma_f16(tO, dP + blk * 1024 + 2 * kk, dV + 128 * k, idO, (j | k) != 0);
-        }
-        mma_commit(bar_o);
-    };
+            for (int k = 0; k < KB / 16; ++k)  // B: V keys 16k..16k+15 (MN-major, 2 KB per 16 keys)
+                mma_f16(tO, a0 + 2 * k, b0 + 128 * k, idO, (j | k) != 0);
+            mma_commit(&bar_o[j & 1]);
+        };
 
-    bool ok = true;  // warp-uniform: TMEM loads and stores are warp-collective
-    if (leader) {
-        prefetch_tensormap(&tmQ);
-        prefetch_tensormap(&tmK);
-        prefetch_tensormap(&tmV);
-        mbar_arrive_expect_tx(bar_q, 16384);
-        if (PACK) {
-            tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L, bar_q);
-            tma_load_2d(sm + AttnSmem::Q + 8192, &tmQ, 0, sh1 * L, bar_q);
-        } else {
-            tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L + q0, bar_q);
-        }
-        load_k(0);
-        load_v(0);
-        if (nkv > 1) {
-            load_k(1);
-            load_v(1);
-        }
-        ok = mbar_wait(bar_q, 0, err) && mbar_wait(&bar_k[0], 0, err);
-        if (ok) issue_s(0);
-    }
-
-    // ---- softmax: warps q and q + 4 share query rows 32q..32q+31 (TMEM lane
-    // r = row r); warp half hf = warp / 4 owns key columns [64 hf, 64 hf + 64)
-    // of S (= P block hf) and O columns [32 hf, 32 hf + 32).
-    // O accumulates in TMEM over the key blocks.  The exponent offset m is the
-    // first block's row max and is raised (O and l rescaled in place) only
-    // when a later block's max exceeds it by more than kRescaleLog2, so
-    // P <= 2^kRescaleLog2 and O / l is the same softmax.
-    const int q4 = warp & 3, hf = warp >> 2;
-    const int r = q4 * 32 + (threadIdx.x & 31);
-    int seg = 0, pos, sh = sh0;
-    bool valid;
-    if (PACK) {
-        seg = r >> 6;
-        pos = r & 63;
-        sh = seg ? sh1 : sh0;
-        valid = pos < L && (seg == 0 || sh0 + 1 < nsh);
-    } else {
-        pos = q0 + r;
-        valid = pos < L;
-    }
-    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    uint8_t* sP = sm + AttnSmem::P;
-    // Row-r exchange slots between the two halves: each half writes into the
-    // other half's P row r, which that half overwrites only after reading it.
-    volatile float* x_mine = (volatile float*)(sP + (hf ^ 1) * 16384 + r * 128);
-    volatile float* x_part = (volatile float*)(sP + hf * 16384 + r * 128);
-    float m = 0.f, lh = 0.f;  // lh: this half's share of the row sum
-    for (int j = 0; j < nkv; ++j) {
-        // every thread reaches every barrier below, also after a timeout
-        ok = __all_sync(0xffffffffu, ok && mbar_wait(bar_s, j & 1, err));
-        tc_fence_after();
-        // valid key columns of this row in block j: [kbeg, kend) (warp-uniform)
-        int kbeg, kend;
-        if (PACK) {
-            kbeg = seg * 64;
-            kend = kbeg + min(L, 64);
-        } else {
-            kbeg = 0;
-            kend = min(KB, L - j * KB);
-        }
-        uint32_t sv[2][32];
-        float mx = -INFINITY;
-        if (ok) {
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                const int c0 = hf * 64 + c * 32;
-                if (c0 + 32 > kbeg && c0 < kend) tmem_ld32(tS + lane_off + c0, sv[c]);
+        if (lane == 0) {
+            prefetch_tensormap(&tmQ);
+            prefetch_tensormap(&tmK);
+            prefetch_tensormap(&tmV);
+            mbar_arrive_expect_tx(bar_q, 16384);
+            if (PACK) {
+                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L, bar_q);
+                tma_load_2d(sm + AttnSmem::Q + 8192, &tmQ, 0, sh1 * L, bar_q);
+            } else {
+                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L + q0, bar_q);
             }
+            for (int i = 0; i < NS && i < nkv; ++i) {
+                load_k(i);
+                load_v(i);
+            }
+        }
+        __syncwarp();
+        // S(0), S(1) go ahead; afterwards S(j+2) is issued once the softmax has
+        // consumed S(j) (its buffer), right behind P(j).V(j).
+        bool ok = wait_all(bar_q, 0);
+        for (int i = 0; i < 2 && i < nkv && ok; ++i) {
+            ok = wait_all(&bar_k[i % NS], (i / NS) & 1);
+            if (ok) {
+                tc_fence_after();
+                if (elect_one()) issue_s(i);
+                __syncwarp();
+            }
+        }
+        for (int j = 0; j < nkv && ok; ++j) {
+            ok = wait_all(&bar_p[j & 1], (j >> 1) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            // stage j % NS of K is free (S(j) was consumed): prefetch K(j + NS)
+            if (lane == 0 && j + NS < nkv) load_k(j + NS);
+            // V(j-1)'s stage is free once P.V(j-1) has completed
+            if (j >= 1) {
+                ok = wait_all(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1);
+                if (!ok) break;
+                if (lane == 0 && j - 1 + NS < nkv) load_v(j - 1 + NS);
+            }
+            ok = wait_all(&bar_v[j % NS], (j / NS) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) issue_pv(j);
+            __syncwarp();
+            if (j + 2 < nkv) {
+                ok = wait_all(&bar_k[(j + 2) % NS], ((j + 2) / NS) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                if (elect_one()) issue_s(j + 2);
+                __syncwarp();
+            }
+        }
+    } else {
+        // ---- softmax warps: thread r owns query row r (TMEM lane r) ----
+        // O accumulates in TMEM over the key blocks.  The exponent offset m is
+        // the first block's row max and is raised (O and l rescaled in place)
+        // only when a later block's max exceeds it by more than kRescaleLog2,
+        // so P <= 2^kRescaleLog2 and O / l is the same softmax.
+        const int r = threadIdx.x;
+        int seg = 0, pos, sh = sh0;
+        bool valid;
+        if (PACK) {
+            seg = r >> 6;
+            pos = r & 63;
+            sh = seg ? sh1 : sh0;
+            valid = pos < L && (seg == 0 || sh0 + 1 < nsh);
+        } else {
+            pos = q0 + r;
+            valid = pos < L;
+        }
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        float m = 0.f, l = 0.f;
+        bool ok = true;  // warp-uniform: TMEM loads and stores are warp-collective
+        for (int j = 0; j < nkv; ++j) {
+            const int b = j & 1;
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_s[b], (j >> 1) & 1, err));
+            if (!ok) break;
+            tc_fence_after();
+            // valid key columns of this row in block j: [0, kend) (warp-uniform)
+            const int kend = PACK ? (j == seg ? min(L, KB) : 0) : min(KB, L - j * KB);
+            uint32_t sv[2][32];
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+                if (c * 32 < kend) tmem_ld32(tmem + lane_off + 64 * b + 32 * c, sv[c]);
             tmem_ld_wait();
             float mxp[8];  // 8 independent partial maxima
 #pragma unroll
             for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const int c0 = hf * 64 + c * 32;
-                if (c0 + 32 <= kbeg || c0 >= kend) continue;
-                if (c0 >= kbeg && c0 + 32 <= kend) {
+                if (c * 32 >= kend) continue;
+                if (c * 32 + 32 <= kend) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (c0 + i >= kbeg && c0 + i < kend) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
+                        if (c * 32 + i < kend) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
                 }
             }
-            mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-        }
-        // P.V(j-1) finished before S(j) did, so the P rows are free for the exchange
-        *x_mine = mx;
-        named_barrier_sync(1 + q4, 64);
-        const float mx_row = fmaxf(mx, *x_part);  // same value in both halves
-        if (ok) {
-            const float m_blk = mx_row * scale_log2;  // the scale is positive
+            const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+            const float m_blk = mx * scale_log2;  // the scale is positive
             if (j == 0) {
                 m = m_blk == -INFINITY ? 0.f : m_blk;
             } else {
-                // O holds P.V of blocks < j
                 const bool need = m_blk > m + kRescaleLog2;
-                if (__any_sync(0xffffffffu, need)) {  // TMEM access is warp-collective
+                if (__any_sync(0xffffffffu, need)) {
+                    // O must hold exactly P.V of blocks < j: wait for P.V(j-1)
+                    ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, err));
+                    if (!ok) break;
+                    tc_fence_after();
                     const float alpha = need ? fast_exp2(m - m_blk) : 1.0f;
                     if (need) {
                         m = m_blk;
-                        lh *= alpha;
+                        l *= alpha;
                     }
 #pragma unroll 1
-                    for (int c = 0; c < 2; ++c) {  // this half's 32 O columns, 16 at a time
+                    for (int c = 0; c < DH / 16; ++c) {  // 16 columns at a time: S is still live
                         uint32_t ov[16];
-                        const uint32_t ta = tO + lane_off + hf * 32 + c * 16;
-                        tmem_ld16(ta, ov);
+                        tmem_ld16(tO + lane_off + c * 16, ov);
                         tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st16(ta, ov);
+                        tmem_st16(tO + lane_off + c * 16, ov);
                     }
                     tmem_st_wait();
                 }
             }
-            // probabilities -> P block hf row r (swizzled K-major); chunks
-            // outside the valid range get zeros
+            // P buffer b is free once P.V(j-2) has completed
+            if (j >= 2) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[b], ((j - 2) >> 1) & 1, err));
+                if (!ok) break;
+            }
+            // probabilities -> P buffer b row r (swizzled K-major); masked keys get zeros
+            uint8_t* prow = sm + AttnSmem::P + b * 16384 + r * 128;
             float rsp[8];  // 8 independent partial sums
 #pragma unroll
             for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
-            uint8_t* prow = sP + hf * 16384 + r * 128;
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const int c0 = hf * 64 + c * 32;
-                if (c0 + 32 <= kbeg || c0 >= kend) {
+                if (c * 32 >= kend) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
                     continue;
                 }
                 float p[32];
-                if (c0 >= kbeg && c0 + 32 <= kend) {
+                if (c * 32 + 32 <= kend) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        p[i] = (c0 + i >= kbeg && c0 + i < kend)
-                                   ? fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m))
-                                   : 0.f;
+                        p[i] = c * 32 + i < kend ? fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m)) : 0.f;
                 }
 #pragma unroll
                 for (int i = 0; i < 32; ++i) rsp[i & 7] += p[i];
@@ -349,69 +353,45 @@ __global__ void __launch_bounds__(256, 2)
                     *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = u;
                 }
             }
-            lh += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-        }
-        fence_proxy_async_smem();  // P visible to the tensor cores
-        tc_fence_before();         // S reads / O stores ordered before the next MMAs
-        __syncthreads();
-        if (warp == 0 && ok) {
-            // P.V(j), then S(j+1) behind it, issued by one elected lane of
-            // warp 0 (warp-uniform operands).  Buffer reuse: V((j+1)&1) held
-            // V(j-1), whose P.V finished before S(j) did; K(j&1) held K(j),
-            // consumed by S(j).
-            tc_fence_after();
-            if (leader && j >= 1 && j + 1 < nkv) load_v(j + 1);
-            bool okw = __all_sync(0xffffffffu, mbar_wait(&bar_v[j & 1], (j >> 1) & 1, err));
-            if (okw && elect_one()) issue_pv(j);
+            l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+            fence_proxy_async_smem();  // P visible to the tensor cores
+            tc_fence_before();         // S reads / O stores ordered before the next MMAs
             __syncwarp();
-            if (okw && j + 1 < nkv) {
-                okw = __all_sync(0xffffffffu, mbar_wait(&bar_k[(j + 1) & 1], ((j + 1) >> 1) & 1, err));
-                if (okw && elect_one()) {
-                    issue_s(j + 1);
-                    if (j + 2 < nkv) load_k(j + 2);
-                }
-                __syncwarp();
-            }
-            ok = okw;
+            if (lane == 0) mbar_arrive(&bar_p[b]);
         }
-    }
-    // S(j+1) is issued after P(j).V(j), so only the last P.V is waited for
-    // here (its phase is the only one that can still be open); after it the
-    // P rows are free again for the row-sum exchange.
-    ok = __all_sync(0xffffffffu, ok && mbar_wait(bar_o, (nkv - 1) & 1, err));
-    *x_mine = lh;
-    named_barrier_sync(1 + q4, 64);
-    const float lo = *x_part;
-    const float l = hf == 0 ? lh + lo : lo + lh;
-    if (ok) {
-        tc_fence_after();
-        uint32_t ov[32];
-        tmem_ld32(tO + lane_off + hf * 32, ov);
-        tmem_ld_wait();
-        if (valid) {
-            const int hd = sh % H;
-            const int64_t s = sh / H;
-            int64_t tok;
-            if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
-            else tok = s * NB + pos;
-            const float g = (gates ? gates[tok * H + hd] : 1.0f) / l;
-            uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH + hf * 32);
+        // the last P.V (earlier phases of its barrier were waited above)
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_o[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, err));
+        if (ok) {
+            tc_fence_after();
+            uint32_t ov[DH / 32][32];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t* o = &ov[q * 8];
-                dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * g, __uint_as_float(o[1]) * g, (T*)nullptr),
-                                    pack2(__uint_as_float(o[2]) * g, __uint_as_float(o[3]) * g, (T*)nullptr),
-                                    pack2(__uint_as_float(o[4]) * g, __uint_as_float(o[5]) * g, (T*)nullptr),
-                                    pack2(__uint_as_float(o[6]) * g, __uint_as_float(o[7]) * g, (T*)nullptr));
+            for (int c = 0; c < DH / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov[c]);
+            tmem_ld_wait();
+            if (valid) {
+                const int hd = sh % H;
+                const int64_t s = sh / H;
+                int64_t tok;
+                if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
+                else tok = s * NB + pos;
+                const float g = (gates ? gates[tok * H + hd] : 1.0f) / l;
+                uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH);
+#pragma unroll
+                for (int q = 0; q < DH / 8; ++q) {
+                    const uint32_t* o = &ov[q >> 2][(q & 3) * 8];
+                    dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * g, __uint_as_float(o[1]) * g, (T*)nullptr),
+                                        pack2(__uint_as_float(o[2]) * g, __uint_as_float(o[3]) * g, (T*)nullptr),
+                                        pack2(__uint_as_float(o[4]) * g, __uint_as_float(o[5]) * g, (T*)nullptr),
+                                        pack2(__uint_as_float(o[6]) * g, __uint_as_float(o[7]) * g, (T*)nullptr));
+                }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == 4) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -459,7 +439,7 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
         attr[dev] = true;
     }
     dim3 grid = PACK ? dim3((unsigned)((nsh + 1) / 2)) : dim3((unsigned)((L + QT - 1) / QT), (unsigned)nsh);
-    kern<<<grid, 256, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
+    kern<<<grid, 160, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
                                               err);
     MBR_CUDA(cudaGetLastError());
 }
@@ -478,8 +458,8 @@ void attention(const void* q, const void* k, const void* v, int64_t nseq, int H,
     CUtensorMap mq, mk, mv;
     const int qrows = pack ? 64 : QT;
     make_map(&mq, q, nsh * L, DH, DH, qrows, dtype);
-    make_map(&mk, k, nsh * L, DH, DH, pack ? 64 : KB, dtype);
-    make_map(&mv, v, nsh * L, DH, DH, pack ? 64 : KB, dtype);
+    make_map(&mk, k, nsh * L, DH, DH, KB, dtype);
+    make_map(&mv, v, nsh * L, DH, DH, KB, dtype);
     const float scale_log2 = scale * 1.4426950408889634f;
     if (dtype == DT_BF16) {
         if (pack) launch<__nv_bfloat16, true>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
