@@ -217,25 +217,27 @@ __global__ void __maxnreg__(168)
             ok = wait_all(&bar_p[j & 1], (j >> 1) & 1);
             if (!ok) break;
             tc_fence_after();
-            // stage j % NS of K is free (S(j) was consumed): prefetch K(j + NS)
-            if (lane == 0 && j + NS < nkv) load_k(j + NS);
-            // V(j-1)'s stage is free once P.V(j-1) has completed
-            if (j >= 1) {
-                ok = wait_all(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1);
-                if (!ok) break;
-                if (lane == 0 && j - 1 + NS < nkv) load_v(j - 1 + NS);
-            }
-            ok = wait_all(&bar_v[j % NS], (j / NS) & 1);
-            if (!ok) break;
-            tc_fence_after();
-            if (elect_one()) issue_pv(j);
-            __syncwarp();
+            // the softmax has consumed S(j): its TMEM buffer takes S(j+2) first
+            // (the softmax's next wait), then P(j).V(j)
             if (j + 2 < nkv) {
                 ok = wait_all(&bar_k[(j + 2) % NS], ((j + 2) / NS) & 1);
                 if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) issue_s(j + 2);
                 __syncwarp();
+            }
+            // K stage j % NS is free too (S(j) was consumed): prefetch K(j + NS)
+            if (lane == 0 && j + NS < nkv) load_k(j + NS);
+            ok = wait_all(&bar_v[j % NS], (j / NS) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) issue_pv(j);
+            __syncwarp();
+            // V(j-1)'s stage is free once P.V(j-1) has completed
+            if (j >= 1 && j - 1 + NS < nkv) {
+                ok = wait_all(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1);
+                if (!ok) break;
+                if (lane == 0) load_v(j - 1 + NS);
             }
         }
     } else {
@@ -271,38 +273,80 @@ __global__ void __maxnreg__(168)
             for (int c = 0; c < 2; ++c)
                 if (c * 32 < kend) tmem_ld32(tmem + lane_off + 64 * b + 32 * c, sv[c]);
             tmem_ld_wait();
-            float mxp[8];  // 8 independent partial maxima
+            // P buffer b is free once P.V(j-2) has completed
+            if (j >= 2) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[b], ((j - 2) >> 1) & 1, err));
+                if (!ok) break;
+            }
+            uint8_t* prow = sm + AttnSmem::P + b * 16384 + r * 128;
+            // exponentials with offset mo -> P row (masked keys get zeros); returns
+            // the largest exponent and accumulates the row sum into rs
+            auto emit = [&](float mo, float& rs) {
+                float xm[8], rsp[8];  // independent partial maxima / sums
 #pragma unroll
-            for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
+                for (int u = 0; u < 8; ++u) xm[u] = -INFINITY, rsp[u] = 0.f;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                if (c * 32 >= kend) continue;
-                if (c * 32 + 32 <= kend) {
+                for (int c = 0; c < 2; ++c) {
+                    if (c * 32 >= kend) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
-                } else {
+                        for (int q = 0; q < 4; ++q)
+                            *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+                        continue;
+                    }
+                    float p[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const bool in = c * 32 + 32 <= kend || c * 32 + i < kend;
+                        const float x = fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo);
+                        xm[i & 7] = in ? fmaxf(xm[i & 7], x) : xm[i & 7];
+                        p[i] = in ? fast_exp2(x) : 0.f;
+                        rsp[i & 7] += p[i];
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 u = make_uint4(pack2(p[8 * q], p[8 * q + 1], (T*)nullptr),
+                                             pack2(p[8 * q + 2], p[8 * q + 3], (T*)nullptr),
+                                             pack2(p[8 * q + 4], p[8 * q + 5], (T*)nullptr),
+                                             pack2(p[8 * q + 6], p[8 * q + 7], (T*)nullptr));
+                        *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = u;
+                    }
+                }
+                rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+                return fmaxf(fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])), fmaxf(fmaxf(xm[4], xm[5]), fmaxf(xm[6], xm[7])));
+            };
+            float rs;
+            if (j == 0) {
+                // first block: the offset is this block's row max
+                float mxp[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    if (c * 32 >= kend) continue;
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (c * 32 + i < kend) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
+                        if (c * 32 + 32 <= kend || c * 32 + i < kend)
+                            mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
                 }
-            }
-            const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-            const float m_blk = mx * scale_log2;  // the scale is positive
-            if (j == 0) {
-                m = m_blk == -INFINITY ? 0.f : m_blk;
+                const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                       fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+                m = mx == -INFINITY ? 0.f : mx * scale_log2;  // the scale is positive
+                emit(m, rs);
             } else {
-                const bool need = m_blk > m + kRescaleLog2;
+                // later blocks reuse the offset; a row whose exponents exceed
+                // kRescaleLog2 raises it (rare): O and l are rescaled and the row
+                // of P is recomputed
+                const float xmax = emit(m, rs);
+                const bool need = xmax > kRescaleLog2;
                 if (__any_sync(0xffffffffu, need)) {
                     // O must hold exactly P.V of blocks < j: wait for P.V(j-1)
                     ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, err));
                     if (!ok) break;
                     tc_fence_after();
-                    const float alpha = need ? fast_exp2(m - m_blk) : 1.0f;
-                    if (need) {
-                        m = m_blk;
-                        l *= alpha;
-                    }
+                    const float m_new = need ? m + xmax : m;
+                    const float alpha = need ? fast_exp2(m - m_new) : 1.0f;
+                    m = m_new;
+                    l *= alpha;
 #pragma unroll 1
                     for (int c = 0; c < DH / 16; ++c) {  // 16 columns at a time: S is still live
                         uint32_t ov[16];
@@ -313,47 +357,10 @@ __global__ void __maxnreg__(168)
                         tmem_st16(tO + lane_off + c * 16, ov);
                     }
                     tmem_st_wait();
+                    emit(m, rs);
                 }
             }
-            // P buffer b is free once P.V(j-2) has completed
-            if (j >= 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[b], ((j - 2) >> 1) & 1, err));
-                if (!ok) break;
-            }
-            // probabilities -> P buffer b row r (swizzled K-major); masked keys get zeros
-            uint8_t* prow = sm + AttnSmem::P + b * 16384 + r * 128;
-            float rsp[8];  // 8 independent partial sums
-#pragma unroll
-            for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                if (c * 32 >= kend) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
-                    continue;
-                }
-                float p[32];
-                if (c * 32 + 32 <= kend) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        p[i] = c * 32 + i < kend ? fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m)) : 0.f;
-                }
-#pragma unroll
-                for (int i = 0; i < 32; ++i) rsp[i & 7] += p[i];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    uint4 u = make_uint4(pack2(p[8 * q], p[8 * q + 1], (T*)nullptr),
-                                         pack2(p[8 * q + 2], p[8 * q + 3], (T*)nullptr),
-                                         pack2(p[8 * q + 4], p[8 * q + 5], (T*)nullptr),
-                                         pack2(p[8 * q + 6], p[8 * q + 7], (T*)nullptr));
-                    *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = u;
-                }
-            }
-            l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+            l += rs;
             fence_proxy_async_smem();  // P visible to the tensor cores
             tc_fence_before();         // S reads / O stores ordered before the next MMAs
             __syncwarp();

@@ -196,7 +196,8 @@ def _attention_ref(q, k, v, scale, gates):
 @pytest.mark.parametrize(
     "dtype,B,H,N,D,ramp,gated",
     [
-        ("fp16", 2, 4, 1301, 64, 12.0, False),  # time path, 11 key blocks, 21-key tail, rescales
+        ("fp16", 2, 4, 1301, 64, 12.0, False),  # time path, 21 key blocks, 21-key tail, rescales
+        ("fp16", 1, 2, 801, 64, 1e3 + 40.0, False),  # score step of ~2^288 mid-sequence (exp overflow, recompute)
         ("bf16", 1, 3, 801, 64, 12.0, True),  # the std chunk length
         ("fp16", 1, 2, 801, 64, -12.0, False),  # max in the first block (no rescale)
         ("fp16", 3, 3, 60, 64, 0.0, True),  # band axis: two sequences per tile, odd count
@@ -221,9 +222,14 @@ def test_attention_op(torch_cuda, dtype, B, H, N, D, ramp, gated):
     g = torch.Generator().manual_seed(N * 7 + H)
     u = torch.randn(D, generator=g)
     u /= u.norm()
-    q = torch.randn(B, H, N, D, generator=g) + abs(ramp) * u
+    q = torch.randn(B, H, N, D, generator=g) + min(abs(ramp), 1e3) * u
     pos = torch.linspace(0.0, 1.0, N)[:, None]
-    k = torch.randn(B, H, N, D, generator=g) + np.sign(ramp) * abs(ramp) * pos * u
+    if abs(ramp) > 1e3:  # step: the second half of the keys jumps by |ramp| - 1000 along u
+        step = abs(ramp) - 1e3
+        q = torch.randn(B, H, N, D, generator=g) + step * u
+        k = torch.randn(B, H, N, D, generator=g) + step * (pos >= 0.5).float() * u
+    else:
+        k = torch.randn(B, H, N, D, generator=g) + np.sign(ramp) * abs(ramp) * pos * u
     v = torch.randn(B, H, N, D, generator=g)
     gates = torch.rand(B, N, H, generator=g) if gated else None
     tq, tk, tv = (t.to(_tdt(torch, dtype)) for t in (q, k, v))
