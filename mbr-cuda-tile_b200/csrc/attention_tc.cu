@@ -7,8 +7,8 @@
 // packed band sequences]: warps 0-3 run the softmax (thread r = query row r =
 // TMEM lane r), warp 4 issues the TMA loads and the MMAs.  Per 64-key block j:
 //   S(j) = Q K(j)^T       -> TMEM buffer j%2 (128 x 64 fp32)
-//   P(j) = exp2(S*c - m)  -> shared buffer j%2 (16-bit, 128-byte swizzled)
-//   O   += P(j) V(j)      -> TMEM (128 x 64 fp32)
+//   P(j) = exp2(S*c - m)  -> TMEM buffer j%2 (16-bit pairs)
+//   O   += P(j) V(j)      -> TMEM (128 x 64 fp32), A operand read from TMEM
 // S(j+2) is computed while the softmax works on S(j+1), so the softmax warps
 // do not wait for the tensor cores; K and V stream through a 4-stage ring.
 // V keeps the [seq][H][L][64] layout of q and k: its 64-key tile is the
@@ -46,12 +46,13 @@ struct AttnSmem {
     static constexpr int Q = 0;                    // 128 x 64 (16 KB)
     static constexpr int K = 16384;                // NS stages of 64 x 64 (8 KB)
     static constexpr int V = K + NS * 8192;        // NS stages of 64 x 64
-    static constexpr int P = V + NS * 8192;        // 2 buffers of 128 x 64 (16 KB)
-    static constexpr int BAR = P + 2 * 16384;      // 114688
+    static constexpr int BAR = V + NS * 8192;
     static constexpr int TOTAL = BAR + 256;
 };
-// TMEM columns: S double buffer at 0 and 64, O at 128 (256 allocated).
+// TMEM columns (256 allocated): S double buffer (fp32) at 0 and 64, O at 128,
+// P double buffer (16-bit pairs, the A operand of P.V) at 192 and 224.
 constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemO = 128, kTmemP = 192;
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
     __half2 h = __floats2half2_rn(a, b);
@@ -78,9 +79,6 @@ __device__ __forceinline__ bool elect_one() {
     return pred != 0;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // 2^x with the hardware approximation (relative error ~2^-22; the
 // probabilities are rounded to 16 bits right after).
@@ -143,7 +141,7 @@ __global__ void __maxnreg__(168)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tO = tmem + 128;
+    const uint32_t tO = tmem + kTmemO;
 
     if (warp == 4) {
         // ---- producer + MMA warp: one elected lane issues, all lanes wait ----
@@ -168,7 +166,6 @@ __global__ void __maxnreg__(168)
         const uint64_t dQ = sdesc_sw128(smem_u32(sm + AttnSmem::Q));
         const uint64_t dK = sdesc_sw128(smem_u32(sm + AttnSmem::K));
         const uint64_t dV = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V));
-        const uint64_t dP = sdesc_sw128(smem_u32(sm + AttnSmem::P));
         auto issue_s = [&](int j) {  // S buffer (j & 1) = Q K(j)^T
             const uint64_t k0 = dK + (uint64_t)(512 * (j % NS));
             const uint32_t d = tmem + (uint32_t)(64 * (j & 1));
@@ -176,12 +173,12 @@ __global__ void __maxnreg__(168)
             for (int k = 0; k < DH / 16; ++k) mma_f16(d, dQ + 2 * k, k0 + 2 * k, idS, k > 0);
             mma_commit(&bar_s[j & 1]);
         };
-        auto issue_pv = [&](int j) {  // O (+)= P(j & 1) V(j)
-            const uint64_t a0 = dP + (uint64_t)(1024 * (j & 1));
+        auto issue_pv = [&](int j) {  // O (+)= P(j & 1) V(j), P read from TMEM
+            const uint32_t a0 = tmem + kTmemP + 32 * (j & 1);
             const uint64_t b0 = dV + (uint64_t)(512 * (j % NS));
 #pragma unroll
-            for (int k = 0; k < KB / 16; ++k)  // B: V keys 16k..16k+15 (MN-major, 2 KB per 16 keys)
-                mma_f16(tO, a0 + 2 * k, b0 + 128 * k, idO, (j | k) != 0);
+            for (int k = 0; k < KB / 16; ++k)  // A: keys 16k.. = 8 packed columns; B: V keys 16k.. (MN-major, 2 KB)
+                mma_f16_ts(tO, a0 + 8 * k, b0 + 128 * k, idO, (j | k) != 0);
             mma_commit(&bar_o[j & 1]);
         };
 
@@ -273,24 +270,24 @@ __global__ void __maxnreg__(168)
             for (int c = 0; c < 2; ++c)
                 if (c * 32 < kend) tmem_ld32(tmem + lane_off + 64 * b + 32 * c, sv[c]);
             tmem_ld_wait();
-            // P buffer b is free once P.V(j-2) has completed
+            // P buffer b (TMEM) is free once P.V(j-2) has completed
             if (j >= 2) {
                 ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[b], ((j - 2) >> 1) & 1, err));
                 if (!ok) break;
             }
-            uint8_t* prow = sm + AttnSmem::P + b * 16384 + r * 128;
-            // exponentials with offset mo -> P row (masked keys get zeros); returns
-            // the largest exponent and accumulates the row sum into rs
+            const uint32_t tP = tmem + lane_off + kTmemP + 32 * b;
+            // exponentials with offset mo -> P buffer b in TMEM as 16-bit pairs
+            // (masked keys get zeros); returns the largest exponent and the row sum
             auto emit = [&](float mo, float& rs) {
                 float xm[8], rsp[8];  // independent partial maxima / sums
 #pragma unroll
                 for (int u = 0; u < 8; ++u) xm[u] = -INFINITY, rsp[u] = 0.f;
+                uint32_t pk[32];
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
                     if (c * 32 >= kend) {
 #pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+                        for (int i = 0; i < 16; ++i) pk[16 * c + i] = 0u;
                         continue;
                     }
                     float p[32];
@@ -303,14 +300,9 @@ __global__ void __maxnreg__(168)
                         rsp[i & 7] += p[i];
                     }
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint4 u = make_uint4(pack2(p[8 * q], p[8 * q + 1], (T*)nullptr),
-                                             pack2(p[8 * q + 2], p[8 * q + 3], (T*)nullptr),
-                                             pack2(p[8 * q + 4], p[8 * q + 5], (T*)nullptr),
-                                             pack2(p[8 * q + 6], p[8 * q + 7], (T*)nullptr));
-                        *reinterpret_cast<uint4*>(prow + (((4 * c + q) ^ (r & 7)) << 4)) = u;
-                    }
+                    for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack2(p[2 * i], p[2 * i + 1], (T*)nullptr);
                 }
+                tmem_st32(tP, pk);
                 rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
                 return fmaxf(fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])), fmaxf(fmaxf(xm[4], xm[5]), fmaxf(xm[6], xm[7])));
             };
@@ -361,8 +353,8 @@ __global__ void __maxnreg__(168)
                 }
             }
             l += rs;
-            fence_proxy_async_smem();  // P visible to the tensor cores
-            tc_fence_before();         // S reads / O stores ordered before the next MMAs
+            tmem_st_wait();    // P stores complete
+            tc_fence_before();  // S reads / P and O stores ordered before the next MMAs
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_p[b]);
         }
