@@ -35,10 +35,12 @@ namespace {
 constexpr int DH = 64;
 constexpr int QT = 128;  // queries per tile
 constexpr int KB = 64;   // keys per block (one 128-byte swizzle atom of P per row)
-constexpr int NS = 4;    // K / V pipeline stages
-// O and l are rescaled only when a block's row max (log2 units) exceeds the
-// running offset by more than this, bounding the probabilities by 2^8.
-constexpr float kRescaleLog2 = 8.0f;
+constexpr int NS = 6;    // K / V pipeline stages
+// The exponent offset of a row is raised (O and l rescaled) only when a
+// block's probabilities computed with the current offset sum to more than
+// this; every probability then stays below 2^14 (fp16 range) and sums of
+// stale-offset probabilities need no separate row max.
+constexpr float kRescaleSum = 16384.0f;
 
 // Two CTAs share an SM, so the layout carries no alignment slack: the kernel
 // checks that the dynamic window is 1024-byte aligned instead.
@@ -214,8 +216,19 @@ __global__ void __maxnreg__(168)
             ok = wait_all(&bar_p[j & 1], (j >> 1) & 1);
             if (!ok) break;
             tc_fence_after();
-            // the softmax has consumed S(j): its TMEM buffer takes S(j+2) first
-            // (the softmax's next wait), then P(j).V(j)
+            // Stages freed by the softmax having consumed S(j): K(j) -> K(j+NS),
+            // and V(j-2), whose P.V completed before S(j) did -> V(j-2+NS).
+            if (lane == 0) {
+                if (j + NS < nkv) load_k(j + NS);
+                if (j >= 2 && j - 2 + NS < nkv) load_v(j - 2 + NS);
+            }
+            ok = wait_all(&bar_v[j % NS], (j / NS) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) issue_pv(j);
+            __syncwarp();
+            // S(j+2) into the buffer S(j) held, behind P.V(j): its completion
+            // (bar_s) also tells the softmax that P buffer j%2 is free again
             if (j + 2 < nkv) {
                 ok = wait_all(&bar_k[(j + 2) % NS], ((j + 2) / NS) & 1);
                 if (!ok) break;
@@ -223,26 +236,13 @@ __global__ void __maxnreg__(168)
                 if (elect_one()) issue_s(j + 2);
                 __syncwarp();
             }
-            // K stage j % NS is free too (S(j) was consumed): prefetch K(j + NS)
-            if (lane == 0 && j + NS < nkv) load_k(j + NS);
-            ok = wait_all(&bar_v[j % NS], (j / NS) & 1);
-            if (!ok) break;
-            tc_fence_after();
-            if (elect_one()) issue_pv(j);
-            __syncwarp();
-            // V(j-1)'s stage is free once P.V(j-1) has completed
-            if (j >= 1 && j - 1 + NS < nkv) {
-                ok = wait_all(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1);
-                if (!ok) break;
-                if (lane == 0) load_v(j - 1 + NS);
-            }
         }
     } else {
         // ---- softmax warps: thread r owns query row r (TMEM lane r) ----
         // O accumulates in TMEM over the key blocks.  The exponent offset m is
         // the first block's row max and is raised (O and l rescaled in place)
-        // only when a later block's max exceeds it by more than kRescaleLog2,
-        // so P <= 2^kRescaleLog2 and O / l is the same softmax.
+        // only when a later block's probabilities sum to more than
+        // kRescaleSum, so P < 2^14 and O / l is the same softmax.
         const int r = threadIdx.x;
         int seg = 0, pos, sh = sh0;
         bool valid;
@@ -270,18 +270,15 @@ __global__ void __maxnreg__(168)
             for (int c = 0; c < 2; ++c)
                 if (c * 32 < kend) tmem_ld32(tmem + lane_off + 64 * b + 32 * c, sv[c]);
             tmem_ld_wait();
-            // P buffer b (TMEM) is free once P.V(j-2) has completed
-            if (j >= 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[b], ((j - 2) >> 1) & 1, err));
-                if (!ok) break;
-            }
+            // P buffer b (TMEM) is free: P.V(j-2) was issued before S(j), whose
+            // completion was just observed
             const uint32_t tP = tmem + lane_off + kTmemP + 32 * b;
             // exponentials with offset mo -> P buffer b in TMEM as 16-bit pairs
-            // (masked keys get zeros); returns the largest exponent and the row sum
-            auto emit = [&](float mo, float& rs) {
-                float xm[8], rsp[8];  // independent partial maxima / sums
+            // (masked keys get zeros); returns the row sum of this block
+            auto emit = [&](float mo) {
+                float rsp[8];  // independent partial sums
 #pragma unroll
-                for (int u = 0; u < 8; ++u) xm[u] = -INFINITY, rsp[u] = 0.f;
+                for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
                 uint32_t pk[32];
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
@@ -294,21 +291,17 @@ __global__ void __maxnreg__(168)
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const bool in = c * 32 + 32 <= kend || c * 32 + i < kend;
-                        const float x = fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo);
-                        xm[i & 7] = in ? fmaxf(xm[i & 7], x) : xm[i & 7];
-                        p[i] = in ? fast_exp2(x) : 0.f;
+                        p[i] = in ? fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo)) : 0.f;
                         rsp[i & 7] += p[i];
                     }
 #pragma unroll
                     for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack2(p[2 * i], p[2 * i + 1], (T*)nullptr);
                 }
                 tmem_st32(tP, pk);
-                rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-                return fmaxf(fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])), fmaxf(fmaxf(xm[4], xm[5]), fmaxf(xm[6], xm[7])));
+                return ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
             };
-            float rs;
-            if (j == 0) {
-                // first block: the offset is this block's row max
+            // row max of the valid scores of this block (log2 units)
+            auto row_max = [&]() {
                 float mxp[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
@@ -322,21 +315,27 @@ __global__ void __maxnreg__(168)
                 }
                 const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                                        fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-                m = mx == -INFINITY ? 0.f : mx * scale_log2;  // the scale is positive
-                emit(m, rs);
+                return mx * scale_log2;  // the scale is positive
+            };
+            float rs;
+            if (j == 0) {
+                // first block: the offset is this block's row max
+                const float mb = row_max();
+                m = mb == -INFINITY ? 0.f : mb;
+                rs = emit(m);
             } else {
-                // later blocks reuse the offset; a row whose exponents exceed
-                // kRescaleLog2 raises it (rare): O and l are rescaled and the row
-                // of P is recomputed
-                const float xmax = emit(m, rs);
-                const bool need = xmax > kRescaleLog2;
+                // later blocks reuse the offset; a row whose probabilities grow
+                // too large raises it to the block max (rare): O and l are
+                // rescaled and the row of P is recomputed
+                rs = emit(m);
+                const bool need = !(rs <= kRescaleSum);  // also catches inf / nan
                 if (__any_sync(0xffffffffu, need)) {
                     // O must hold exactly P.V of blocks < j: wait for P.V(j-1)
                     ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, err));
                     if (!ok) break;
                     tc_fence_after();
-                    const float m_new = need ? m + xmax : m;
-                    const float alpha = need ? fast_exp2(m - m_new) : 1.0f;
+                    const float m_new = need ? fmaxf(m, row_max()) : m;
+                    const float alpha = fast_exp2(m - m_new);
                     m = m_new;
                     l *= alpha;
 #pragma unroll 1
@@ -349,7 +348,7 @@ __global__ void __maxnreg__(168)
                         tmem_st16(tO + lane_off + c * 16, ov);
                     }
                     tmem_st_wait();
-                    emit(m, rs);
+                    rs = emit(m);
                 }
             }
             l += rs;
