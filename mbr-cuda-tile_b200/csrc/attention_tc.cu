@@ -288,11 +288,19 @@ __global__ void __maxnreg__(168)
                         continue;
                     }
                     float p[32];
+                    if (c * 32 + 32 <= kend) {  // whole chunk valid: no per-element masking
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const bool in = c * 32 + 32 <= kend || c * 32 + i < kend;
-                        p[i] = in ? fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo)) : 0.f;
-                        rsp[i & 7] += p[i];
+                        for (int i = 0; i < 32; ++i) {
+                            p[i] = fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo));
+                            rsp[i & 7] += p[i];
+                        }
+                    } else {
+                        const int nv = kend - c * 32;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            p[i] = i < nv ? fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo)) : 0.f;
+                            rsp[i & 7] += p[i];
+                        }
                     }
 #pragma unroll
                     for (int i = 0; i < 16; ++i) pk[16 * c + i] = pack2(p[2 * i], p[2 * i + 1], (T*)nullptr);
@@ -308,10 +316,10 @@ __global__ void __maxnreg__(168)
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
                     if (c * 32 >= kend) continue;
+                    const int nv = kend - c * 32;
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (c * 32 + 32 <= kend || c * 32 + i < kend)
-                            mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
+                        if (nv >= 32 || i < nv) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
                 }
                 const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                                        fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
