@@ -18,6 +18,7 @@
 // a hang).
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "attention_tc.h"
@@ -35,21 +36,27 @@ namespace {
 constexpr int DH = 64;
 constexpr int QT = 128;  // queries per tile
 constexpr int KB = 64;   // keys per block (one 128-byte swizzle atom of P per row)
-constexpr int NS = 6;    // K / V pipeline stages
 // The exponent offset of a row is raised (O and l rescaled) only when a
 // block's probabilities computed with the current offset sum to more than
 // this; every probability then stays below 2^14 (fp16 range) and sums of
 // stale-offset probabilities need no separate row max.
 constexpr float kRescaleSum = 16384.0f;
 
-// Two CTAs share an SM, so the layout carries no alignment slack: the kernel
-// checks that the dynamic window is 1024-byte aligned instead.
-struct AttnSmem {
-    static constexpr int Q = 0;                    // 128 x 64 (16 KB)
-    static constexpr int K = 16384;                // NS stages of 64 x 64 (8 KB)
-    static constexpr int V = K + NS * 8192;        // NS stages of 64 x 64
+// Shared-memory plan: NQ Q tiles in flight (persistent CTAs prefetch the next
+// tiles; band tiles have only two key blocks, so they prefetch further) and an
+// NS-stage K / V ring.  Two CTAs share an SM, so the layout carries no
+// alignment slack: the kernel checks that the dynamic window is 1024-byte
+// aligned instead.
+template <bool PACK>
+struct AttnCfg {
+    static constexpr int NS = PACK ? 4 : 5;  // K / V stages of 64 x 64 (8 KB each)
+    static constexpr int NQ = PACK ? 3 : 2;  // Q tiles of 128 x 64 (16 KB)
+    static constexpr int Q = 0;
+    static constexpr int K = NQ * 16384;
+    static constexpr int V = K + NS * 8192;
     static constexpr int BAR = V + NS * 8192;
     static constexpr int TOTAL = BAR + 256;
+    static_assert(2 * (TOTAL + 1024) <= 233472, "two CTAs per SM");
 };
 // TMEM columns (256 allocated): S double buffer (fp32) at 0 and 64, O at 128,
 // P double buffer (16-bit pairs, the A operand of P.V) at 192 and 224.
@@ -95,35 +102,46 @@ __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, float scale_log2,
                    const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
+    using AttnSmem = AttnCfg<PACK>;
+    constexpr int NS = AttnSmem::NS, NQ = AttnSmem::NQ;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     if (!smem_aligned_or_flag(smem_raw, err)) return;  // uniform over the CTA
     uint8_t* sm = smem_raw;
     uint64_t* bar = (uint64_t*)(sm + AttnSmem::BAR);
-    uint64_t* bar_q = bar;            // Q tile landed
-    uint64_t* bar_k = bar + 1;        // [NS] K stage landed
-    uint64_t* bar_v = bar + 1 + NS;   // [NS] V stage landed
-    uint64_t* bar_s = bar + 1 + 2 * NS;  // [2] S buffer computed
-    uint64_t* bar_p = bar_s + 2;      // [2] softmax done with S buffer, P buffer written (4 warps)
-    uint64_t* bar_o = bar_p + 2;      // [2] P.V from P buffer complete
+    uint64_t* bar_q = bar;               // [NQ] Q tile landed
+    uint64_t* bar_k = bar + NQ;          // [NS] K stage landed
+    uint64_t* bar_v = bar_k + NS;        // [NS] V stage landed
+    uint64_t* bar_s = bar_v + NS;        // [2] S buffer computed
+    uint64_t* bar_p = bar_s + 2;         // [2] softmax done with S buffer, P buffer written (4 warps)
+    uint64_t* bar_o = bar_p + 2;         // [2] P.V from P buffer complete
     uint32_t* tmem_slot = (uint32_t*)(bar_o + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // tile decode: time axis = one 128-query tile of sequence-head sh0, keys in
-    // 64-key blocks; band axis (PACK) = sequence-heads sh0 (rows 0-63) and sh1
-    // (rows 64-127), key block j = the keys of sh_j
-    int sh0, sh1 = 0, q0 = 0, nkv;
-    if (PACK) {
-        sh0 = blockIdx.x * 2;
-        sh1 = min(sh0 + 1, nsh - 1);
-        nkv = 2;
-    } else {
-        sh0 = blockIdx.y;
-        q0 = blockIdx.x * QT;
-        nkv = (L + KB - 1) / KB;
-    }
+    // Persistent CTAs: this CTA takes tiles blockIdx.x, + gridDim.x, ...  Time
+    // axis: tile = one 128-query tile of sequence-head sh0, 64-key blocks;
+    // band axis (PACK): tile = sequence-heads sh0 (rows 0-63) and sh1 (rows
+    // 64-127), key block j = the keys of sh_j.  The blocks of all of this
+    // CTA's tiles form one stream g = local tile * nkv + j for the pipelines.
+    const int qtiles = PACK ? 1 : (L + QT - 1) / QT;
+    const int ntiles = PACK ? (nsh + 1) / 2 : nsh * qtiles;
+    const int nkv = PACK ? 2 : (L + KB - 1) / KB;
+    const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my_tiles * nkv;
+    auto tile_of = [&](int tl, int& sh0, int& sh1, int& q0) {
+        const int t = (int)blockIdx.x + tl * (int)gridDim.x;
+        if (PACK) {
+            sh0 = 2 * t;
+            sh1 = min(sh0 + 1, nsh - 1);
+            q0 = 0;
+        } else {
+            sh0 = t / qtiles;
+            sh1 = sh0;
+            q0 = (t - sh0 * qtiles) * QT;
+        }
+    };
 
     if (threadIdx.x == 0) {
-        mbar_init(bar_q, 1);
+        for (int i = 0; i < NQ; ++i) mbar_init(&bar_q[i], 1);
         for (int i = 0; i < NS; ++i) {
             mbar_init(&bar_k[i], 1);
             mbar_init(&bar_v[i], 1);
@@ -147,19 +165,59 @@ __global__ void __maxnreg__(168)
 
     if (warp == 4) {
         // ---- producer + MMA warp: one elected lane issues, all lanes wait ----
-        auto wait_all = [&](uint64_t* b, uint32_t parity) {
+        auto wait_all = [&](uint64_t* b, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(b, parity, err));
         };
-        auto key_row = [&](int j) { return PACK ? (j ? sh1 : sh0) * L : sh0 * L + j * KB; };
-        auto load_k = [&](int j) {
-            const int st = j % NS;
-            mbar_arrive_expect_tx(&bar_k[st], 8192);
-            tma_load_2d(sm + AttnSmem::K + st * 8192, &tmK, 0, key_row(j), &bar_k[st]);
+        // Position in the block stream without divisions: block g is key
+        // block j of local tile tl; `row` is the first key row of the block.
+        struct Cursor {
+            int g, tl, j, row;
         };
-        auto load_v = [&](int j) {
-            const int st = j % NS;
+        auto first_row = [&](int tl, int j) {
+            int sh0, sh1, q0;
+            tile_of(tl, sh0, sh1, q0);
+            return PACK ? (j ? sh1 : sh0) * L : sh0 * L + j * KB;
+        };
+        auto cursor_at = [&](int g) {  // called a few times before the loop only
+            Cursor c;
+            c.g = g;
+            c.tl = g / nkv;
+            c.j = g - c.tl * nkv;
+            c.row = first_row(c.tl, c.j);
+            return c;
+        };
+        auto advance = [&](Cursor& c) {
+            ++c.g;
+            if (++c.j == nkv) {
+                c.j = 0;
+                ++c.tl;
+                c.row = c.tl < my_tiles ? first_row(c.tl, 0) : 0;
+            } else {
+                c.row = PACK ? first_row(c.tl, c.j) : c.row + KB;
+            }
+        };
+        auto load_q = [&](int tl) {
+            int sh0, sh1, q0;
+            tile_of(tl, sh0, sh1, q0);
+            const int qb = tl % NQ;
+            uint8_t* dst = sm + AttnSmem::Q + qb * 16384;
+            mbar_arrive_expect_tx(&bar_q[qb], 16384);
+            if (PACK) {
+                tma_load_2d(dst, &tmQ, 0, sh0 * L, &bar_q[qb]);
+                tma_load_2d(dst + 8192, &tmQ, 0, sh1 * L, &bar_q[qb]);
+            } else {
+                tma_load_2d(dst, &tmQ, 0, sh0 * L + q0, &bar_q[qb]);
+            }
+        };
+        auto load_k = [&](const Cursor& c) {
+            const int st = c.g % NS;
+            mbar_arrive_expect_tx(&bar_k[st], 8192);
+            tma_load_2d(sm + AttnSmem::K + st * 8192, &tmK, 0, c.row, &bar_k[st]);
+        };
+        auto load_v = [&](const Cursor& c) {
+            const int st = c.g % NS;
             mbar_arrive_expect_tx(&bar_v[st], 8192);
-            tma_load_2d(sm + AttnSmem::V + st * 8192, &tmV, 0, key_row(j), &bar_v[st]);
+            tma_load_2d(sm + AttnSmem::V + st * 8192, &tmV, 0, c.row, &bar_v[st]);
         };
         constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
         constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
@@ -168,82 +226,100 @@ __global__ void __maxnreg__(168)
         const uint64_t dQ = sdesc_sw128(smem_u32(sm + AttnSmem::Q));
         const uint64_t dK = sdesc_sw128(smem_u32(sm + AttnSmem::K));
         const uint64_t dV = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V));
-        auto issue_s = [&](int j) {  // S buffer (j & 1) = Q K(j)^T
-            const uint64_t k0 = dK + (uint64_t)(512 * (j % NS));
-            const uint32_t d = tmem + (uint32_t)(64 * (j & 1));
+        auto issue_s = [&](const Cursor& c) {  // S buffer (g & 1) = Q(tile) K(g)^T
+            const uint64_t q = dQ + (uint64_t)(1024 * (c.tl % NQ));
+            const uint64_t k0 = dK + (uint64_t)(512 * (c.g % NS));
+            const uint32_t d = tmem + (uint32_t)(64 * (c.g & 1));
 #pragma unroll
-            for (int k = 0; k < DH / 16; ++k) mma_f16(d, dQ + 2 * k, k0 + 2 * k, idS, k > 0);
-            mma_commit(&bar_s[j & 1]);
+            for (int k = 0; k < DH / 16; ++k) mma_f16(d, q + 2 * k, k0 + 2 * k, idS, k > 0);
+            mma_commit(&bar_s[c.g & 1]);
         };
-        auto issue_pv = [&](int j) {  // O (+)= P(j & 1) V(j), P read from TMEM
-            const uint32_t a0 = tmem + kTmemP + 32 * (j & 1);
-            const uint64_t b0 = dV + (uint64_t)(512 * (j % NS));
+        auto issue_pv = [&](const Cursor& c) {  // O (+)= P(g & 1) V(g), P read from TMEM; O restarts per tile
+            const uint32_t a0 = tmem + kTmemP + 32 * (c.g & 1);
+            const uint64_t b0 = dV + (uint64_t)(512 * (c.g % NS));
 #pragma unroll
             for (int k = 0; k < KB / 16; ++k)  // A: keys 16k.. = 8 packed columns; B: V keys 16k.. (MN-major, 2 KB)
-                mma_f16_ts(tO, a0 + 8 * k, b0 + 128 * k, idO, (j | k) != 0);
-            mma_commit(&bar_o[j & 1]);
+                mma_f16_ts(tO, a0 + 8 * k, b0 + 128 * k, idO, c.j != 0 || k > 0);
+            mma_commit(&bar_o[c.g & 1]);
+        };
+        // S(g) needs its tile's Q: wait for it at the tile's first block
+        auto s_ready = [&](const Cursor& c) -> bool {
+            if (c.j == 0 && !wait_all(&bar_q[c.tl % NQ], (c.tl / NQ) & 1)) return false;
+            return wait_all(&bar_k[c.g % NS], (c.g / NS) & 1);
         };
 
+        Cursor cs = cursor_at(0);             // next S to issue
+        Cursor cp = cs;                        // next P.V
+        Cursor ck = cursor_at(min(NS, total)); // next K load
+        Cursor cv = ck;                        // next V load
         if (lane == 0) {
             prefetch_tensormap(&tmQ);
             prefetch_tensormap(&tmK);
             prefetch_tensormap(&tmV);
-            mbar_arrive_expect_tx(bar_q, 16384);
-            if (PACK) {
-                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L, bar_q);
-                tma_load_2d(sm + AttnSmem::Q + 8192, &tmQ, 0, sh1 * L, bar_q);
-            } else {
-                tma_load_2d(sm + AttnSmem::Q, &tmQ, 0, sh0 * L + q0, bar_q);
-            }
-            for (int i = 0; i < NS && i < nkv; ++i) {
-                load_k(i);
-                load_v(i);
+            for (int tl = 0; tl < NQ && tl < my_tiles; ++tl) load_q(tl);
+            Cursor c = cs;
+            for (int g = 0; g < NS && g < total; ++g, advance(c)) {
+                load_k(c);
+                load_v(c);
             }
         }
         __syncwarp();
-        // S(0), S(1) go ahead; afterwards S(j+2) is issued once the softmax has
-        // consumed S(j) (its buffer), right behind P(j).V(j).
-        bool ok = wait_all(bar_q, 0);
-        for (int i = 0; i < 2 && i < nkv && ok; ++i) {
-            ok = wait_all(&bar_k[i % NS], (i / NS) & 1);
+        // S(0), S(1) go ahead; afterwards S(g+2) is issued once the softmax has
+        // consumed S(g) (its buffer), right behind P(g).V(g).
+        bool ok = true;
+        for (int g = 0; g < 2 && g < total && ok; ++g, advance(cs)) {
+            ok = s_ready(cs);
             if (ok) {
                 tc_fence_after();
-                if (elect_one()) issue_s(i);
+                if (elect_one()) issue_s(cs);
                 __syncwarp();
             }
         }
-        for (int j = 0; j < nkv && ok; ++j) {
-            ok = wait_all(&bar_p[j & 1], (j >> 1) & 1);
+        for (; cp.g < total && ok; advance(cp)) {
+            const int g = cp.g;
+            ok = wait_all(&bar_p[g & 1], (g >> 1) & 1);
             if (!ok) break;
             tc_fence_after();
-            // Stages freed by the softmax having consumed S(j): K(j) -> K(j+NS),
-            // and V(j-2), whose P.V completed before S(j) did -> V(j-2+NS).
-            if (lane == 0) {
-                if (j + NS < nkv) load_k(j + NS);
-                if (j >= 2 && j - 2 + NS < nkv) load_v(j - 2 + NS);
+            // Freed by the softmax having consumed S(g): K stage g -> K(g+NS);
+            // V(g-2), whose P.V completed before S(g) did -> V(g-2+NS); after
+            // the last block of a tile, that tile's Q buffer -> Q(tile + NQ).
+            if (ck.g < total) {
+                if (lane == 0) load_k(ck);
+                advance(ck);
             }
-            ok = wait_all(&bar_v[j % NS], (j / NS) & 1);
+            if (g >= 2 && cv.g < total) {
+                if (lane == 0) load_v(cv);
+                advance(cv);
+            }
+            if (lane == 0 && cp.j == nkv - 1 && cp.tl + NQ < my_tiles) load_q(cp.tl + NQ);
+            ok = wait_all(&bar_v[g % NS], (g / NS) & 1);
             if (!ok) break;
             tc_fence_after();
-            if (elect_one()) issue_pv(j);
+            if (elect_one()) issue_pv(cp);
             __syncwarp();
-            // S(j+2) into the buffer S(j) held, behind P.V(j): its completion
-            // (bar_s) also tells the softmax that P buffer j%2 is free again
-            if (j + 2 < nkv) {
-                ok = wait_all(&bar_k[(j + 2) % NS], ((j + 2) / NS) & 1);
+            // S(g+2) into the buffer S(g) held, behind P.V(g): its completion
+            // (bar_s) also tells the softmax that P buffer g%2 is free again
+            if (cs.g < total) {
+                ok = s_ready(cs);
                 if (!ok) break;
                 tc_fence_after();
-                if (elect_one()) issue_s(j + 2);
+                if (elect_one()) issue_s(cs);
                 __syncwarp();
+                advance(cs);
             }
         }
     } else {
         // ---- softmax warps: thread r owns query row r (TMEM lane r) ----
-        // O accumulates in TMEM over the key blocks.  The exponent offset m is
-        // the first block's row max and is raised (O and l rescaled in place)
-        // only when a later block's probabilities sum to more than
+        // O accumulates in TMEM over a tile's key blocks.  The exponent offset
+        // m is the first block's row max and is raised (O and l rescaled in
+        // place) only when a later block's probabilities sum to more than
         // kRescaleSum, so P < 2^14 and O / l is the same softmax.
         const int r = threadIdx.x;
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        bool ok = true;  // warp-uniform: TMEM loads and stores are warp-collective
+        for (int tl = 0; tl < my_tiles && ok; ++tl) {
+        int sh0, sh1, q0;
+        tile_of(tl, sh0, sh1, q0);
         int seg = 0, pos, sh = sh0;
         bool valid;
         if (PACK) {
@@ -255,12 +331,11 @@ __global__ void __maxnreg__(168)
             pos = q0 + r;
             valid = pos < L;
         }
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
         float m = 0.f, l = 0.f;
-        bool ok = true;  // warp-uniform: TMEM loads and stores are warp-collective
         for (int j = 0; j < nkv; ++j) {
-            const int b = j & 1;
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_s[b], (j >> 1) & 1, err));
+            const int g = tl * nkv + j;
+            const int b = g & 1;
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_s[b], (g >> 1) & 1, err));
             if (!ok) break;
             tc_fence_after();
             // valid key columns of this row in block j: [0, kend) (warp-uniform)
@@ -270,7 +345,7 @@ __global__ void __maxnreg__(168)
             for (int c = 0; c < 2; ++c)
                 if (c * 32 < kend) tmem_ld32(tmem + lane_off + 64 * b + 32 * c, sv[c]);
             tmem_ld_wait();
-            // P buffer b (TMEM) is free: P.V(j-2) was issued before S(j), whose
+            // P buffer b (TMEM) is free: P.V(g-2) was issued before S(g), whose
             // completion was just observed
             const uint32_t tP = tmem + lane_off + kTmemP + 32 * b;
             // exponentials with offset mo -> P buffer b in TMEM as 16-bit pairs
@@ -338,8 +413,8 @@ __global__ void __maxnreg__(168)
                 rs = emit(m);
                 const bool need = !(rs <= kRescaleSum);  // also catches inf / nan
                 if (__any_sync(0xffffffffu, need)) {
-                    // O must hold exactly P.V of blocks < j: wait for P.V(j-1)
-                    ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, err));
+                    // O must hold exactly P.V of blocks < j: wait for P.V(g-1)
+                    ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[(g - 1) & 1], ((g - 1) >> 1) & 1, err));
                     if (!ok) break;
                     tc_fence_after();
                     const float m_new = need ? fmaxf(m, row_max()) : m;
@@ -365,8 +440,10 @@ __global__ void __maxnreg__(168)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_p[b]);
         }
-        // the last P.V (earlier phases of its barrier were waited above)
-        ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_o[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, err));
+        // the tile's last P.V: it is the latest on its barrier, and the one
+        // before it completed ahead of S(g_last), so the parity wait is exact
+        const int g_last = tl * nkv + nkv - 1;
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_o[g_last & 1], (g_last >> 1) & 1, err));
         if (ok) {
             tc_fence_after();
             uint32_t ov[DH / 32][32];
@@ -379,18 +456,20 @@ __global__ void __maxnreg__(168)
                 int64_t tok;
                 if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
                 else tok = s * NB + pos;
-                const float g = (gates ? gates[tok * H + hd] : 1.0f) / l;
+                const float gs = (gates ? gates[tok * H + hd] : 1.0f) / l;
                 uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH);
 #pragma unroll
                 for (int q = 0; q < DH / 8; ++q) {
                     const uint32_t* o = &ov[q >> 2][(q & 3) * 8];
-                    dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * g, __uint_as_float(o[1]) * g, (T*)nullptr),
-                                        pack2(__uint_as_float(o[2]) * g, __uint_as_float(o[3]) * g, (T*)nullptr),
-                                        pack2(__uint_as_float(o[4]) * g, __uint_as_float(o[5]) * g, (T*)nullptr),
-                                        pack2(__uint_as_float(o[6]) * g, __uint_as_float(o[7]) * g, (T*)nullptr));
+                    dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * gs, __uint_as_float(o[1]) * gs, (T*)nullptr),
+                                        pack2(__uint_as_float(o[2]) * gs, __uint_as_float(o[3]) * gs, (T*)nullptr),
+                                        pack2(__uint_as_float(o[4]) * gs, __uint_as_float(o[5]) * gs, (T*)nullptr),
+                                        pack2(__uint_as_float(o[6]) * gs, __uint_as_float(o[7]) * gs, (T*)nullptr));
                 }
             }
+            tc_fence_before();  // O read before the next tile's first P.V overwrites it
         }
+        }  // tiles
     }
     tc_fence_before();
     __syncthreads();
@@ -436,15 +515,22 @@ template <typename T, bool PACK>
 void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int nsh, int H, int L,
             float scale_log2, const float* gates, int mode, int NB, int Tn, void* merged, int* err, cudaStream_t st) {
     auto kern = attn_tc_kernel<T, PACK>;
+    using AttnSmem = AttnCfg<PACK>;
     static bool attr[64] = {};
+    static int sms[64] = {};
     int dev = 0;
     MBR_CUDA(cudaGetDevice(&dev));
     MBR_CHECK(dev >= 0 && dev < 64, "device index out of range");
     if (!attr[dev]) {
         MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem::TOTAL));
+        MBR_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
         attr[dev] = true;
     }
-    dim3 grid = PACK ? dim3((unsigned)((nsh + 1) / 2)) : dim3((unsigned)((L + QT - 1) / QT), (unsigned)nsh);
+    // persistent: two CTAs per SM walk the tiles
+    const int64_t ntiles = PACK ? ((int64_t)nsh + 1) / 2 : (int64_t)nsh * ((L + QT - 1) / QT);
+    MBR_CHECK(ntiles < (1ll << 30), "tc attention: too many tiles");
+    const int grid = (int)std::min<int64_t>(ntiles, 2 * (int64_t)sms[dev]);
+    if (grid == 0) return;
     kern<<<grid, 160, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
                                               err);
     MBR_CUDA(cudaGetLastError());
