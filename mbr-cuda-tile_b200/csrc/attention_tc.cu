@@ -100,7 +100,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 template <typename T, bool PACK>
 __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, float scale_log2,
+                   const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, int n_lo, float scale_log2,
                    const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
     using AttnSmem = AttnCfg<PACK>;
     constexpr int NS = AttnSmem::NS, NQ = AttnSmem::NQ;
@@ -168,22 +168,32 @@ __global__ void __maxnreg__(168)
         auto wait_all = [&](uint64_t* b, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(b, parity, err));
         };
-        // Position in the block stream without divisions: block g is key
-        // block j of local tile tl; `row` is the first key row of the block.
-        struct Cursor {
-            int g, tl, j, row;
+        // TMA coordinates (d, head, position, sequence % n_lo, sequence / n_lo)
+        // of sequence-head sh
+        auto seq_coords = [&](int sh, int& h, int& slo, int& shi) {
+            const int s = sh / H;
+            h = sh - s * H;
+            shi = s / n_lo;
+            slo = s - shi * n_lo;
         };
-        auto first_row = [&](int tl, int j) {
+        // Position in the block stream without per-block divisions: block g is
+        // key block j of local tile tl, starting at key position p of the
+        // sequence-head with coordinates (h, slo, shi).
+        struct Cursor {
+            int g, tl, j, h, p, slo, shi;
+        };
+        auto set_block = [&](Cursor& c) {
             int sh0, sh1, q0;
-            tile_of(tl, sh0, sh1, q0);
-            return PACK ? (j ? sh1 : sh0) * L : sh0 * L + j * KB;
+            tile_of(c.tl, sh0, sh1, q0);
+            seq_coords(PACK && c.j ? sh1 : sh0, c.h, c.slo, c.shi);
+            c.p = PACK ? 0 : c.j * KB;
         };
         auto cursor_at = [&](int g) {  // called a few times before the loop only
             Cursor c;
             c.g = g;
             c.tl = g / nkv;
             c.j = g - c.tl * nkv;
-            c.row = first_row(c.tl, c.j);
+            if (c.tl < my_tiles) set_block(c);
             return c;
         };
         auto advance = [&](Cursor& c) {
@@ -191,33 +201,35 @@ __global__ void __maxnreg__(168)
             if (++c.j == nkv) {
                 c.j = 0;
                 ++c.tl;
-                c.row = c.tl < my_tiles ? first_row(c.tl, 0) : 0;
+                if (c.tl < my_tiles) set_block(c);
+            } else if (PACK) {
+                set_block(c);
             } else {
-                c.row = PACK ? first_row(c.tl, c.j) : c.row + KB;
+                c.p += KB;
             }
         };
         auto load_q = [&](int tl) {
-            int sh0, sh1, q0;
+            int sh0, sh1, q0, h, slo, shi;
             tile_of(tl, sh0, sh1, q0);
             const int qb = tl % NQ;
             uint8_t* dst = sm + AttnSmem::Q + qb * 16384;
             mbar_arrive_expect_tx(&bar_q[qb], 16384);
+            seq_coords(sh0, h, slo, shi);
+            tma_load_5d(dst, &tmQ, 0, h, q0, slo, shi, &bar_q[qb]);
             if (PACK) {
-                tma_load_2d(dst, &tmQ, 0, sh0 * L, &bar_q[qb]);
-                tma_load_2d(dst + 8192, &tmQ, 0, sh1 * L, &bar_q[qb]);
-            } else {
-                tma_load_2d(dst, &tmQ, 0, sh0 * L + q0, &bar_q[qb]);
+                seq_coords(sh1, h, slo, shi);
+                tma_load_5d(dst + 8192, &tmQ, 0, h, 0, slo, shi, &bar_q[qb]);
             }
         };
         auto load_k = [&](const Cursor& c) {
             const int st = c.g % NS;
             mbar_arrive_expect_tx(&bar_k[st], 8192);
-            tma_load_2d(sm + AttnSmem::K + st * 8192, &tmK, 0, c.row, &bar_k[st]);
+            tma_load_5d(sm + AttnSmem::K + st * 8192, &tmK, 0, c.h, c.p, c.slo, c.shi, &bar_k[st]);
         };
         auto load_v = [&](const Cursor& c) {
             const int st = c.g % NS;
             mbar_arrive_expect_tx(&bar_v[st], 8192);
-            tma_load_2d(sm + AttnSmem::V + st * 8192, &tmV, 0, c.row, &bar_v[st]);
+            tma_load_5d(sm + AttnSmem::V + st * 8192, &tmV, 0, c.h, c.p, c.slo, c.shi, &bar_v[st]);
         };
         constexpr uint32_t idS = idesc_f16(QT, KB, IsBf16<T>::value);
         constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
@@ -498,21 +510,27 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-void make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int box_cols, int box_rows, int dtype) {
-    MBR_CHECK(((uintptr_t)base & 15) == 0 && (cols * 2) % 16 == 0, "attention TMA operand misaligned");
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
+// 5-D view (d, head, position, sequence % n_lo, sequence / n_lo) of q, k or v;
+// the box is one head's 64 columns of `box_pos` consecutive positions.
+void make_map(CUtensorMap* m, const void* base, const AttnLayout& lay, int H, int L, int box_pos, int dtype) {
+    MBR_CHECK(((uintptr_t)base & 15) == 0, "attention TMA operand misaligned");
+    const int64_t es = 2;
+    cuuint64_t dims[5] = {(cuuint64_t)DH, (cuuint64_t)H, (cuuint64_t)L, (cuuint64_t)lay.n_lo, (cuuint64_t)lay.n_hi};
+    cuuint64_t strides[4] = {(cuuint64_t)(lay.head * es), (cuuint64_t)(lay.pos * es), (cuuint64_t)(lay.lo * es),
+                             (cuuint64_t)((lay.n_hi > 1 ? lay.hi : lay.lo * lay.n_lo) * es)};  // unused if n_hi == 1
+    for (int i = 0; i < 4; ++i)
+        MBR_CHECK(strides[i] % 16 == 0 && strides[i] < (1ull << 40), "attention TMA strides must be 16-byte multiples");
+    cuuint32_t box[5] = {(cuuint32_t)DH, 1, (cuuint32_t)box_pos, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     CUresult r = encode_fn()(m, dtype == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                             2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             5, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 
 template <typename T, bool PACK>
-void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int nsh, int H, int L,
+void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int nsh, int H, int L, int n_lo,
             float scale_log2, const float* gates, int mode, int NB, int Tn, void* merged, int* err, cudaStream_t st) {
     auto kern = attn_tc_kernel<T, PACK>;
     using AttnSmem = AttnCfg<PACK>;
@@ -531,8 +549,8 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
     MBR_CHECK(ntiles < (1ll << 30), "tc attention: too many tiles");
     const int grid = (int)std::min<int64_t>(ntiles, 2 * (int64_t)sms[dev]);
     if (grid == 0) return;
-    kern<<<grid, 160, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, scale_log2, gates, mode, NB, Tn, (T*)merged,
-                                              err);
+    kern<<<grid, 160, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, n_lo, scale_log2, gates, mode, NB, Tn,
+                                              (T*)merged, err);
     MBR_CUDA(cudaGetLastError());
 }
 
@@ -540,25 +558,38 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
 
 bool attention_supported(int dim_head) { return dim_head == DH; }
 
-void attention(const void* q, const void* k, const void* v, int64_t nseq, int H, int L, int dh, float scale,
-               const float* gates, int mode, int NB, int T, void* merged, int dtype, int* d_err, cudaStream_t st) {
+AttnLayout head_major_layout(int64_t nseq, int H, int L, int dh) {
+    AttnLayout lay;
+    lay.head = (int64_t)L * dh;
+    lay.pos = dh;
+    lay.lo = (int64_t)H * L * dh;
+    lay.hi = 0;
+    lay.n_lo = (int)nseq;
+    lay.n_hi = 1;
+    return lay;
+}
+
+void attention(const void* q, const void* k, const void* v, const AttnLayout& lay, int64_t nseq, int H, int L,
+               int dh, float scale, const float* gates, int mode, int NB, int T, void* merged, int dtype, int* d_err,
+               cudaStream_t st) {
     MBR_CHECK(dh == DH, "tc attention: dim_head must be 64");
     MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "tc attention: fp16 or bf16 only");
     const int64_t nsh = nseq * H;
-    MBR_CHECK(nsh < (1 << 30) && nsh * L < (1ll << 31), "tc attention: problem too large for 32-bit coordinates");
+    MBR_CHECK(nsh < (1 << 30) && L > 0 && lay.n_lo > 0 && lay.n_hi > 0 && (int64_t)lay.n_lo * lay.n_hi == nseq,
+              "tc attention: bad problem or layout");
     const bool pack = L <= 64;
     CUtensorMap mq, mk, mv;
-    const int qrows = pack ? 64 : QT;
-    make_map(&mq, q, nsh * L, DH, DH, qrows, dtype);
-    make_map(&mk, k, nsh * L, DH, DH, KB, dtype);
-    make_map(&mv, v, nsh * L, DH, DH, KB, dtype);
+    make_map(&mq, q, lay, H, L, pack ? 64 : QT, dtype);
+    make_map(&mk, k, lay, H, L, KB, dtype);
+    make_map(&mv, v, lay, H, L, KB, dtype);
     const float scale_log2 = scale * 1.4426950408889634f;
+    const int n = (int)nsh;
     if (dtype == DT_BF16) {
-        if (pack) launch<__nv_bfloat16, true>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
-        else launch<__nv_bfloat16, false>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        if (pack) launch<__nv_bfloat16, true>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        else launch<__nv_bfloat16, false>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
     } else {
-        if (pack) launch<__half, true>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
-        else launch<__half, false>(mq, mk, mv, (int)nsh, H, L, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        if (pack) launch<__half, true>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        else launch<__half, false>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
     }
 }
 

@@ -134,9 +134,38 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
     }
 }
 
-// QKV epilogue: RoPE on q and k (interleaved pairs, src/mbr_cuda_tile.cu:3928-3943)
-// and scatter of the 32 columns [n0, n0+32) of token `row` into the
-// per-sequence head-major q / k / v tensors [seq][H][L][64].
+// RoPE (interleaved pairs, src/mbr_cuda_tile.cu:3928-3943) of the 32 columns
+// [n0, n0+32) of token `row` of a fused q|k|v projection, in place; v columns
+// (section 2) are left alone.  The position is the token's index in its
+// sequence: the frame along the time axis, the band along the band axis.
+__device__ __forceinline__ void rope_rotate(const EpiQKV& e, int row, int n0, float (&v)[32]) {
+    const int DI = e.H * 64;
+    const int sec = n0 / DI;
+    const int d0 = (n0 - sec * DI) & 63;
+    const int pos = e.mode == ops::SEQ_TIME ? (row / e.NB) % e.T : row % e.NB;
+    if (sec < 2) {
+        // 16 consecutive table entries (64 bytes, 64-byte aligned) per lane as
+        // four 16-byte loads: along the band axis every lane has its own
+        // position, so scalar loads would cost one L1 wavefront per lane each
+        const float4* cs = reinterpret_cast<const float4*>(e.cos_t + pos * 32 + (d0 >> 1));
+        const float4* sn = reinterpret_cast<const float4*>(e.sin_t + pos * 32 + (d0 >> 1));
+#pragma unroll
+        for (int i4 = 0; i4 < 4; ++i4) {
+            const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+            const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = 4 * i4 + u;
+                const float x0 = v[2 * i], x1 = v[2 * i + 1];
+                v[2 * i] = x0 * cc[u] - x1 * ss[u];
+                v[2 * i + 1] = x0 * ss[u] + x1 * cc[u];
+            }
+        }
+    }
+}
+
+// QKV epilogue: RoPE, then scatter of the 32 columns [n0, n0+32) of token
+// `row` into the per-sequence head-major q / k / v tensors [seq][H][L][64].
 template <typename T>
 __device__ __forceinline__ void epilogue_qkv(const EpiQKV& e, int row, int n0, const uint32_t (&r)[32]) {
     const int DI = e.H * 64;
@@ -158,25 +187,7 @@ __device__ __forceinline__ void epilogue_qkv(const EpiQKV& e, int row, int n0, c
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    if (sec < 2) {
-        // 16 consecutive table entries (64 bytes, 64-byte aligned) per lane as
-        // four 16-byte loads: along the band axis every lane has its own
-        // position, so scalar loads would cost one L1 wavefront per lane each
-        const float4* cs = reinterpret_cast<const float4*>(e.cos_t + pos * 32 + (d0 >> 1));
-        const float4* sn = reinterpret_cast<const float4*>(e.sin_t + pos * 32 + (d0 >> 1));
-#pragma unroll
-        for (int i4 = 0; i4 < 4; ++i4) {
-            const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
-            const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int i = 4 * i4 + u;
-                const float x0 = v[2 * i], x1 = v[2 * i + 1];
-                v[2 * i] = x0 * cc[u] - x1 * ss[u];
-                v[2 * i + 1] = x0 * ss[u] + x1 * cc[u];
-            }
-        }
-    }
+    rope_rotate(e, row, n0, v);
     T* base = (T*)(sec == 0 ? e.q : sec == 1 ? e.k : e.v);
     uint4* dst = reinterpret_cast<uint4*>(base + ((s * e.H + h) * L + pos) * 64 + d0);
 #pragma unroll
@@ -344,8 +355,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int row = tl.y + q * 32 + lane;
             const bool rv = row < g.M;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + half * (BN / 2);
-            constexpr bool kStoresViaTma = EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32 ||
-                                           EPI == ops::EPI_T || EPI == ops::EPI_GELU_T || EPI == ops::EPI_TANH_T;
+            constexpr bool kStoresViaTma = EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32 || EPI == ops::EPI_T ||
+                                           EPI == ops::EPI_GELU_T || EPI == ops::EPI_TANH_T ||
+                                           EPI == ops::EPI_ROPE_T;
             if (kStoresViaTma && c_tma) {
                 // stage through this warp's 32-row tile; one TMA store (or
                 // reduce-add into the fp32 residual) per 128-byte row group
@@ -363,6 +375,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
                     apply_epi<EPI>(g, n0, v);
+                    if constexpr (EPI == ops::EPI_ROPE_T) rope_rotate(qkv, tl.y + q * 32 + lane, n0, v);
                     const int h16 = k16 ? (c & 1) : 0;
                     if (h16 == 0) {  // the staging tile is free once the previous store has read it
                         if (lane == 0) bulk_wait_read_all();
@@ -392,8 +405,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tmem_ld32(taddr + c * 32, r);
                     tmem_ld_wait();
                     if (rv) {
-                        if constexpr (EPI == ops::EPI_QKV) epilogue_qkv<T>(qkv, row, n0, r);
-                        else epilogue_chunk<T, EPI>(g, row, n0, r);
+                        if constexpr (EPI == ops::EPI_QKV) {
+                            epilogue_qkv<T>(qkv, row, n0, r);
+                        } else if constexpr (EPI == ops::EPI_ROPE_T) {
+                            float v[32];
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                            apply_epi<EPI>(g, n0, v);
+                            rope_rotate(qkv, row, n0, v);
+                            uint4* c4 = reinterpret_cast<uint4*>((T*)g.C + (int64_t)row * g.ldc + n0);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)  // N is a multiple of 64 (checked on the host)
+                                c4[j] = make_uint4(pack2(v[8 * j], v[8 * j + 1], (T*)nullptr),
+                                                   pack2(v[8 * j + 2], v[8 * j + 3], (T*)nullptr),
+                                                   pack2(v[8 * j + 4], v[8 * j + 5], (T*)nullptr),
+                                                   pack2(v[8 * j + 6], v[8 * j + 7], (T*)nullptr));
+                        }
+                        else {
+                            epilogue_chunk<T, EPI>(g, row, n0, r);
+                        }
                     }
                 }
             }
@@ -509,6 +539,7 @@ void launch_bn(const GemmLaunch& L, int* d_err, cudaStream_t st) {
         case ops::EPI_TANH_T: launch_one<T, BN, ops::EPI_TANH_T>(L, d_err, st); break;
         case ops::EPI_GLU_F32: launch_one<T, BN, ops::EPI_GLU_F32>(L, d_err, st); break;
         case ops::EPI_QKV: launch_one<T, BN, ops::EPI_QKV>(L, d_err, st); break;
+        case ops::EPI_ROPE_T: launch_one<T, BN, ops::EPI_ROPE_T>(L, d_err, st); break;
         default: throw Error(ERR_INVALID, "tc gemm: bad epilogue");
     }
 }
@@ -522,7 +553,7 @@ void launch_t(const GemmLaunch& L, int* d_err, cudaStream_t st) {
 
 }  // namespace
 
-bool gemm_supported(int epi) { return epi >= ops::EPI_F32 && epi <= ops::EPI_QKV; }
+bool gemm_supported(int epi) { return epi >= ops::EPI_F32 && epi <= ops::EPI_ROPE_T; }
 
 void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, GemmLaunch& L, size_t& L_first) {
     MBR_CHECK(dtype == DT_F16 || dtype == DT_BF16, "tc gemm needs fp16 or bf16 operands");
@@ -538,6 +569,9 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
     else bn = 256;
     L.bn = bn;
     L.epi = p.epi;
+    if (p.epi == ops::EPI_ROPE_T)
+        MBR_CHECK(L.qkv.cos_t && L.qkv.sin_t && L.qkv.H > 0 && p.maxN == 3 * L.qkv.H * 64 && p.c_dtype == dtype,
+                  "tc gemm: RoPE epilogue needs head dim 64, the rope tables and a 16-bit output view");
     if (p.epi == ops::EPI_QKV)
         MBR_CHECK(L.qkv.q && L.qkv.k && L.qkv.v && L.qkv.cos_t && L.qkv.H > 0 && p.maxN == 3 * L.qkv.H * 64 &&
                       bn % 64 == 0,
@@ -560,7 +594,7 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
     L.groups = p.groups;
     L.c_tma = 0;
     const bool staged_epi = p.epi == ops::EPI_F32 || p.epi == ops::EPI_ADD_F32 || p.epi == ops::EPI_T ||
-                            p.epi == ops::EPI_GELU_T || p.epi == ops::EPI_TANH_T;
+                            p.epi == ops::EPI_GELU_T || p.epi == ops::EPI_TANH_T || p.epi == ops::EPI_ROPE_T;
     if (p.c_dtype >= 0 && staged_epi) {
         const bool f32 = p.epi == ops::EPI_F32 || p.epi == ops::EPI_ADD_F32;
         MBR_CHECK(f32 ? p.c_dtype == DT_F32 : p.c_dtype == dtype, "tc gemm: output view dtype mismatch");

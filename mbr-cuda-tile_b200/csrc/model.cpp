@@ -459,9 +459,8 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
             tp.c_group_stride = p->c_group_stride;
             tp.c_dtype = p->c_dtype;
             tc::GemmLaunch L;
-            if (p->qkv_mode >= 0 && dh_ == 64) {
-                // fused RoPE + head scatter epilogue (replaces rope_scatter)
-                tp.epi = ops::EPI_QKV;
+            const bool qkv = p->qkv_mode >= 0 && dh_ == 64;
+            if (qkv) {
                 L.qkv.mode = p->qkv_mode;
                 L.qkv.NB = NB_;
                 L.qkv.T = (int)ws->T;
@@ -471,12 +470,28 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
                 L.qkv.q = ws->q;
                 L.qkv.k = ws->k;
                 L.qkv.v = ws->v;
+                // RoPE in the epilogue, q|k|v stored token-major through TMA
+                tp.epi = ops::EPI_ROPE_T;
+                tp.c_base = ws->qkv, tp.c_rows = ws->M, tp.c_cols = 3 * DI_, tp.c_groups = 1;
+                tp.c_row_stride = 3 * DI_, tp.c_group_stride = ws->M * 3 * DI_, tp.c_dtype = dtype_;
             }
             size_t first = 0;
             tc::gemm_prepare(tp, dtype_, tiles, L, first);
             p->launch = (int)ws->launches.size();
             ws->launches.push_back(L);
             firsts.push_back(first);
+            if (qkv) {
+                // RoPE + head-major scatter for the CUDA-core attention
+                tc::GemmPlanTC ts = tp;
+                ts.epi = ops::EPI_QKV;
+                ts.c_dtype = -1;
+                tc::GemmLaunch Ls;
+                Ls.qkv = L.qkv;
+                tc::gemm_prepare(ts, dtype_, tiles, Ls, first);
+                p->launch_scatter = (int)ws->launches.size();
+                ws->launches.push_back(Ls);
+                firsts.push_back(first);
+            }
         }
         MBR_CUDA(cudaMalloc(&ws->d_tiles, sizeof(int4) * std::max<size_t>(1, tiles.size())));
         MBR_CUDA(cudaMemcpy(ws->d_tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice));
@@ -669,14 +684,15 @@ void MelBandRoformer::profile_read(int kind, double* ms, int64_t* count) {
         ++launches_;                                             \
     } while (0)
 
-void MelBandRoformer::run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st) {
-    if (gemm_backend_ != BACKEND_SIMT && dtype_ != DT_F32 && p.launch >= 0) {
-        if (gemm_backend_ == BACKEND_TC_DIRECT && ws.launches[p.launch].c_tma) {
-            tc::GemmLaunch L = ws.launches[p.launch];
+void MelBandRoformer::run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st, int launch) {
+    if (launch < 0) launch = p.launch;
+    if (gemm_backend_ != BACKEND_SIMT && dtype_ != DT_F32 && launch >= 0) {
+        if (gemm_backend_ == BACKEND_TC_DIRECT && ws.launches[launch].c_tma) {
+            tc::GemmLaunch L = ws.launches[launch];
             L.c_tma = 0;  // epilogue stores from registers
             MBR_LAUNCH(kind, tc::gemm_launch(L, dtype_, d_err_, st));
         } else {
-            MBR_LAUNCH(kind, tc::gemm_launch(ws.launches[p.launch], dtype_, d_err_, st));
+            MBR_LAUNCH(kind, tc::gemm_launch(ws.launches[launch], dtype_, d_err_, st));
         }
     } else {
         MBR_LAUNCH(kind, ops::gemm_simt(ws.d_groups + p.first, p.n, p.maxM, p.maxN, dtype_, p.epi, st));
@@ -698,17 +714,43 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
         const Plan* p = plans + 4 * l;
         MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.attn_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, lw.wg,
                                           lw.bg, H_, ws.gates, st));
-        run_gemm(ws, p[0], PK_GEMM_QKV, st);
-        // the tensor-core QKV GEMM applies RoPE and scatters q/k/v in its epilogue
-        const bool fused_qkv = gemm_backend_ != BACKEND_SIMT && p[0].launch >= 0 &&
-                               ws.launches[p[0].launch].epi == ops::EPI_QKV;
-        if (!fused_qkv)
+        const bool tc_gemm = gemm_backend_ != BACKEND_SIMT && dtype_ != DT_F32 && p[0].launch >= 0;
+        const bool tc_attn = attn_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::attention_supported(dh_);
+        // tensor cores end to end: the QKV GEMM applies RoPE and stores q|k|v
+        // token-major; the attention reads them there through strided TMA views
+        const bool in_place = tc_gemm && tc_attn && p[0].launch_scatter >= 0;
+        if (in_place) {
+            run_gemm(ws, p[0], PK_GEMM_QKV, st);
+        } else if (tc_gemm && p[0].launch_scatter >= 0) {
+            run_gemm(ws, p[0], PK_GEMM_QKV, st, p[0].launch_scatter);  // RoPE + head-major scatter
+        } else {
+            run_gemm(ws, p[0], PK_GEMM_QKV, st);
             MBR_LAUNCH(PK_ROPE, ops::rope_scatter(ws.qkv, M, H_, dh_, rc, rs, mode, NB_, (int)ws.T, ws.q, ws.k, ws.v,
                                                   dtype_, st));
-        const bool tc_attn = attn_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::attention_supported(dh_);
-        if (tc_attn) {
-            MBR_LAUNCH(attn_kind, tc::attention(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode, NB_,
-                                                (int)ws.T, ws.merged, dtype_, d_err_, st));
+        }
+        if (in_place) {
+            const int64_t row = 3 * (int64_t)DI_;  // elements per token of q|k|v
+            tc::AttnLayout lay;
+            lay.head = dh_;
+            if (mode == ops::SEQ_TIME) {  // sequence (b, band k), position = frame t
+                lay.pos = (int64_t)NB_ * row;
+                lay.lo = row;
+                lay.n_lo = NB_;
+            } else {  // sequence (b, frame t), position = band k
+                lay.pos = row;
+                lay.lo = (int64_t)NB_ * row;
+                lay.n_lo = (int)ws.T;
+            }
+            lay.hi = ws.T * NB_ * row;
+            lay.n_hi = ws.B;
+            const size_t es = dtype_bytes(dtype_);
+            const uint8_t* q = (const uint8_t*)ws.qkv;
+            MBR_LAUNCH(attn_kind, tc::attention(q, q + es * DI_, q + 2 * es * DI_, lay, nseq, H_, L, dh_, attn_scale,
+                                                ws.gates, mode, NB_, (int)ws.T, ws.merged, dtype_, d_err_, st));
+        } else if (tc_attn) {
+            MBR_LAUNCH(attn_kind, tc::attention(ws.q, ws.k, ws.v, tc::head_major_layout(nseq, H_, L, dh_), nseq, H_, L,
+                                                dh_, attn_scale, ws.gates, mode, NB_, (int)ws.T, ws.merged, dtype_,
+                                                d_err_, st));
         } else {
             MBR_LAUNCH(attn_kind, ops::attention_simt(ws.q, ws.k, ws.v, nseq, H_, L, dh_, attn_scale, ws.gates, mode,
                                                       NB_, (int)ws.T, ws.merged, dtype_, st));

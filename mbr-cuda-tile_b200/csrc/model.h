@@ -135,6 +135,10 @@ private:
         size_t first = 0;  // index into the workspace's group array
         int n = 0, maxM = 0, maxN = 0, maxK = 0, epi = 0;
         int launch = -1;  // index into Workspace::launches (tensor-core path)
+        // QKV projections: the launch above writes RoPE'd q|k|v token-major
+        // (read in place by the tensor-core attention); this one scatters them
+        // head-major for the CUDA-core attention
+        int launch_scatter = -1;
         int qkv_mode = -1;  // QKV projection of a time (0) / band (1) transformer
         // operand tensor shapes for the tensor-core path (rows x cols, elements)
         const void* a_base = nullptr;
@@ -197,7 +201,8 @@ private:
 
     Workspace& workspace(int B, int64_t L);
     void build_plans(Workspace& ws);
-    void run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st);
+    // launch: a prepared tensor-core launch other than p.launch (-1: p.launch)
+    void run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st, int launch = -1);
     void run_transformer(Workspace& ws, const TransW& tw, int mode, const Plan* plans, bool last_of_model,
                          cudaStream_t st);
     void run_forward(Workspace& ws, const float* d_audio, float* d_out, int tap, float* d_tap, int64_t* tap_n,

@@ -65,6 +65,7 @@ enum Epilogue {
     EPI_TANH_T = 4,   // C (dtype) = tanh(acc + bias)
     EPI_GLU_F32 = 5,  // C[m][n/2] (fp32) = (acc_n + b_n) * sigmoid(acc_{n+1} + b_{n+1}), n even
     EPI_QKV = 6,      // RoPE(q, k) + scatter of q, k, v into [seq][H][L][64] (tensor-core path only)
+    EPI_ROPE_T = 7,   // C (dtype) = acc with RoPE on the q and k sections, token-major (tensor-core path only)
 };
 void gemm_simt(const GemmGroup* d_groups, int ngroups, int maxM, int maxN, int dtype, int epi, cudaStream_t st);
 

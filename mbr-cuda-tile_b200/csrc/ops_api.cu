@@ -403,7 +403,8 @@ void attention(const void* q, const void* k, const void* v, int64_t B, int H, in
     // sequence s = b, position = token within it: the band-axis token map with NB = N
     if (dtype != DT_F32 && tc::attention_supported(D)) {
         int* err = op_error_word();
-        tc::attention(q, k, v, B, H, N, D, scale, gates, ops::SEQ_FREQ, N, 1, out, dtype, err, st);
+        tc::attention(q, k, v, tc::head_major_layout(B, H, N, D), B, H, N, D, scale, gates, ops::SEQ_FREQ, N, 1, out,
+                      dtype, err, st);
         check_op_error(st);
     } else {
         ops::attention_simt(q, k, v, B, H, N, D, scale, gates, ops::SEQ_FREQ, N, 1, out, dtype, st);
