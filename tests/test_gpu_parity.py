@@ -213,3 +213,20 @@ def test_tensor_core_attention_matches_cuda_core(torch_cuda, make_csm, preset, d
     s = snr_db(b, a)
     print(f"{preset}/{dtype}/L={L}: tcgen05 vs CUDA-core attention forward SNR {s:.1f} dB")
     assert s >= (FP16_SNR_DB if dtype == "fp16" else BF16_SNR_DB)
+
+
+def test_separate_two_gpus_matches_one(torch_cuda, make_csm):
+    """mbr_separate over two GPUs (chunk-range shards, one boundary added over
+    a peer copy) equals the single-GPU result up to the fp32 rounding of the
+    boundary sums, which are added in a different order."""
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    path = make_csm("tiny2", seed=23)
+    m = _model(path, "fp16")
+    x = _audio(24, 1, 2, 44100 * 9)[0]
+    one = m.separate(x, overlap=2, n_gpus=1)
+    two = m.separate(x, overlap=2, n_gpus=2)
+    err = np.abs(two - one).max() / max(np.abs(one).max(), 1e-12)
+    print(f"two-GPU vs one-GPU separate: max rel err {err:.2e}")
+    assert err <= 1e-5
