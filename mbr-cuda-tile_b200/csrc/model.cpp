@@ -700,7 +700,8 @@ void MelBandRoformer::run_gemm(const Workspace& ws, const Plan& p, int kind, cud
 }
 
 void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode, const Plan* plans,
-                                      bool last_of_model, cudaStream_t st) {
+                                      bool last_of_model, cudaStream_t st, bool first_norm_done,
+                                      const LayerW* next_first) {
     const float scale = std::sqrt((float)D_);
     const float attn_scale = 1.0f / std::sqrt((float)dh_);
     const int64_t M = ws.M;
@@ -712,8 +713,9 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
     for (size_t l = 0; l < tw.layers.size(); ++l) {
         const LayerW& lw = tw.layers[l];
         const Plan* p = plans + 4 * l;
-        MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.attn_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, lw.wg,
-                                          lw.bg, H_, ws.gates, st));
+        if (l > 0 || !first_norm_done)  // else the previous block's final norm produced xn and the gates
+            MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.attn_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr,
+                                              lw.wg, lw.bg, H_, ws.gates, st));
         const bool tc_gemm = gemm_backend_ != BACKEND_SIMT && dtype_ != DT_F32 && p[0].launch >= 0;
         const bool tc_attn = attn_backend_ == BACKEND_TC && dtype_ != DT_F32 && tc::attention_supported(dh_);
         // tensor cores end to end: the QKV GEMM applies RoPE and stores q|k|v
@@ -763,8 +765,16 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
     }
     // final RMSNorm of the transformer; the model's last one also writes the
     // band-major 16-bit copy the mask estimators read
-    MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, tw.final_gamma, scale, last_of_model ? ws.rm : nullptr, dtype_,
-                                      last_of_model ? ws.MT : 0, NB_, ws.R, nullptr, nullptr, 0, nullptr, st));
+    if (next_first) {
+        // fused with the next block's pre-norm: xn and the gates of its first layer
+        MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, tw.final_gamma, scale, ws.xn, dtype_, 0, NB_, ws.R,
+                                          next_first->wg, next_first->bg, H_, ws.gates, st,
+                                          next_first->attn_gamma));
+    } else {
+        MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, tw.final_gamma, scale, last_of_model ? ws.rm : nullptr,
+                                          dtype_, last_of_model ? ws.MT : 0, NB_, ws.R, nullptr, nullptr, 0, nullptr,
+                                          st));
+    }
 }
 
 void MelBandRoformer::run_forward(Workspace& ws, const float* d_audio, float* d_out, int tap, float* d_tap,
@@ -790,13 +800,21 @@ void MelBandRoformer::run_forward(Workspace& ws, const float* d_audio, float* d_
     if (tap == 0) return;
     // 8: depth loop (:740-801)
     size_t pi = 0;
+    // A block's final RMSNorm also computes the next block's first pre-norm
+    // (and gates) when nothing happens to the residual stream in between.
+    bool norm_done = false;
     for (int d = 0; d < c.depth; ++d) {
         if (c.skip_connection)
             for (int j = 0; j < d; ++j) MBR_LAUNCH(PK_NORM, ops::add_inplace_f32(ws.R, ws.skip[j], M * D_, st));
         bool last = d == c.depth - 1;
-        run_transformer(ws, tt_[d], ops::SEQ_TIME, ws.layer_plans.data() + pi, false, st);
+        const LayerW* nf = ft_[d].layers.empty() ? nullptr : &ft_[d].layers[0];
+        run_transformer(ws, tt_[d], ops::SEQ_TIME, ws.layer_plans.data() + pi, false, st, norm_done, nf);
+        norm_done = nf != nullptr;
         pi += 4 * tt_[d].layers.size();
-        run_transformer(ws, ft_[d], ops::SEQ_FREQ, ws.layer_plans.data() + pi, last, st);
+        const LayerW* nt = (!last && !c.skip_connection && !tt_[d + 1].layers.empty()) ? &tt_[d + 1].layers[0]
+                                                                                       : nullptr;
+        run_transformer(ws, ft_[d], ops::SEQ_FREQ, ws.layer_plans.data() + pi, last, st, norm_done, nt);
+        norm_done = nt != nullptr;
         pi += 4 * ft_[d].layers.size();
         if (c.skip_connection) MBR_CUDA(cudaMemcpyAsync(ws.skip[d], ws.R, 4 * M * D_, cudaMemcpyDeviceToDevice, st));
         if (d == 0) {

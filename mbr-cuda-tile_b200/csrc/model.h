@@ -204,7 +204,7 @@ private:
     // launch: a prepared tensor-core launch other than p.launch (-1: p.launch)
     void run_gemm(const Workspace& ws, const Plan& p, int kind, cudaStream_t st, int launch = -1);
     void run_transformer(Workspace& ws, const TransW& tw, int mode, const Plan* plans, bool last_of_model,
-                         cudaStream_t st);
+                         cudaStream_t st, bool first_norm_done = false, const LayerW* next_first = nullptr);
     void run_forward(Workspace& ws, const float* d_audio, float* d_out, int tap, float* d_tap, int64_t* tap_n,
                      cudaStream_t st);
 

@@ -34,9 +34,12 @@ void band_gather_norm(const float2* spec, int64_t MT, int FC, const int* fi, con
 //  xn (dtype) receives y (row map: identity, or band-major k*MT + bt when band_major_mt > 0);
 //  r_out (fp32, may alias R) receives y too when non-null;
 //  gates[m][h] = sigmoid(y . wg[h] + bg[h]) when wg is non-null.
+//  With gamma2, r_out still receives y but xn and the gates are taken from
+//  y2 = RMSNorm(y) * gamma2 * scale (a block's final norm fused with the next
+//  block's pre-norm).
 void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale, void* xn, int dtype,
               int64_t band_major_mt, int NB, float* r_out, const float* wg, const float* bg, int H, float* gates,
-              cudaStream_t st);
+              cudaStream_t st, const float* gamma2 = nullptr);
 
 // q, k (rotated) and, if v is non-null, v -> [nseq][H][L][dh].
 void rope_scatter(const void* qkv, int64_t M, int H, int dh, const float* cos_t, const float* sin_t, int mode,

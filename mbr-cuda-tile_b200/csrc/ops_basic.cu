@@ -132,7 +132,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
                                                        T* __restrict__ xn, int64_t band_major_mt, int NB,
                                                        float* r_out, const float* __restrict__ wg,
                                                        const float* __restrict__ bg, int H,
-                                                       float* __restrict__ gates) {
+                                                       float* __restrict__ gates,
+                                                       const float* __restrict__ gamma2) {
     extern __shared__ float4 swg4[];  // [H][D/4]
     const int D4 = D / 4;
     if (wg) {
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
     }
     const int lane = threadIdx.x & 31;
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    const float4* h4 = reinterpret_cast<const float4*>(gamma2);
     float4 g[MAXC];
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
@@ -167,10 +169,28 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
             const int c = lane + 32 * i;
             v[i] = make_float4(v[i].x * inv * g[i].x, v[i].y * inv * g[i].y, v[i].z * inv * g[i].z,
                                v[i].w * inv * g[i].w);
-            if (c < D4) {
-                if (r_out) reinterpret_cast<float4*>(r_out + m * D)[c] = v[i];
-                if (xn) store4<T>(xn + orow * D + 4 * c, v[i]);
+            if (c < D4 && r_out) reinterpret_cast<float4*>(r_out + m * D)[c] = v[i];
+        }
+        if (gamma2) {
+            // a second RMSNorm of the (stored) first result: the next block's
+            // pre-norm, so the residual stream is read once for both
+            float ss2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < MAXC; ++i) ss2 += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+            ss2 = warp_sum(ss2);
+            const float inv2 = rsqrtf(ss2 + 1e-12f) * scale;
+#pragma unroll
+            for (int i = 0; i < MAXC; ++i) {
+                const int c = lane + 32 * i;
+                const float4 g2 = c < D4 ? __ldg(h4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);  // L1-resident
+                v[i] = make_float4(v[i].x * inv2 * g2.x, v[i].y * inv2 * g2.y, v[i].z * inv2 * g2.z,
+                                   v[i].w * inv2 * g2.w);
             }
+        }
+#pragma unroll
+        for (int i = 0; i < MAXC; ++i) {
+            const int c = lane + 32 * i;
+            if (c < D4 && xn) store4<T>(xn + orow * D + 4 * c, v[i]);
         }
         if (wg) {
             float mine = 0.f;  // lane h ends up holding the dot product of gate h
@@ -502,7 +522,7 @@ void band_gather_norm(const float2* spec, int64_t MT, int FC, const int* fi, con
 
 void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale, void* xn, int dtype,
               int64_t band_major_mt, int NB, float* r_out, const float* wg, const float* bg, int H, float* gates,
-              cudaStream_t st) {
+              cudaStream_t st, const float* gamma2) {
     MBR_CHECK(D % 4 == 0 && D <= 1024, "rms_norm: dim must be a multiple of 4 and <= 1024");
     MBR_CHECK(!wg || H <= 32, "rms_norm: at most 32 gates");
     size_t sm = wg ? sizeof(float) * H * D : 0;
@@ -517,7 +537,8 @@ void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale,
         auto run = [&](auto kern) {
             if (sm > 48 * 1024)
                 MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-            kern<<<grid, 256, sm, st>>>(R, M, D, gamma, scale, (T*)xn, band_major_mt, NB, r_out, wg, bg, H, gates);
+            kern<<<grid, 256, sm, st>>>(R, M, D, gamma, scale, (T*)xn, band_major_mt, NB, r_out, wg, bg, H, gates,
+                                        gamma2);
         };
         if (D <= 128) run(rms_norm_kernel<T, 1>);
         else if (D <= 256) run(rms_norm_kernel<T, 2>);
