@@ -192,7 +192,49 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
             const int c = lane + 32 * i;
             if (c < D4 && xn) store4<T>(xn + orow * D + 4 * c, v[i]);
         }
-        if (wg) {
+        if (wg && H == 8) {
+            // eight dot products at once: per-lane partial sums for all heads,
+            // then a transposing butterfly (each xor step halves the heads a
+            // lane carries) so lane 4h ends with head h: 9 shuffles instead of 40
+            float a[8];
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < MAXC; ++i) {
+                    const int c = lane + 32 * i;
+                    if (c < D4) {
+                        const float4 w = swg4[h * D4 + c];
+                        acc += v[i].x * w.x + v[i].y * w.y + v[i].z * w.z + v[i].w * w.w;
+                    }
+                }
+                a[h] = acc;
+            }
+            const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float send = b4 ? a[k] : a[k + 4];
+                const float keep = b4 ? a[k + 4] : a[k];
+                a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const float send = b3 ? a[k] : a[k + 2];
+                const float keep = b3 ? a[k + 2] : a[k];
+                a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+            {
+                const float send = b2 ? a[0] : a[1];
+                const float keep = b2 ? a[1] : a[0];
+                a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+            a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
+            a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
+            if ((lane & 3) == 0) {
+                const int h = lane >> 2;
+                gates[m * H + h] = 1.0f / (1.0f + expf(-(a[0] + bg[h])));
+            }
+        } else if (wg) {
             float mine = 0.f;  // lane h ends up holding the dot product of gate h
             for (int h = 0; h < H; ++h) {
                 float acc = 0.f;

@@ -43,7 +43,7 @@ def _model(path, dtype):
     return cudasep.Model(path, 0, dtype)
 
 
-@pytest.mark.parametrize("preset", ["tiny", "tiny2"])
+@pytest.mark.parametrize("preset", ["tiny", "tiny2", "mid"])  # mid: 8 heads (butterfly gate reduction)
 def test_forward_fp32_matches_oracle(torch_cuda, make_csm, preset):
     torch = torch_cuda
     path = make_csm(preset, seed=1)
