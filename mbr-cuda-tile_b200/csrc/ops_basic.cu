@@ -127,13 +127,15 @@ __device__ __forceinline__ void store4(T* p, float4 y) {
 // staged in shared memory once per CTA).  Each lane holds up to MAXC float4
 // chunks of the row in registers.  D % 4 == 0, D <= 128 * MAXC, H <= 32.
 template <typename T, int MAXC>
-__global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ R, int64_t M, int D,
-                                                       const float* __restrict__ gamma, float scale,
-                                                       T* __restrict__ xn, int64_t band_major_mt, int NB,
-                                                       float* r_out, const float* __restrict__ wg,
-                                                       const float* __restrict__ bg, int H,
-                                                       float* __restrict__ gates,
-                                                       const float* __restrict__ gamma2) {
+__global__ void __launch_bounds__(256, 3) rms_norm_kernel(const float* __restrict__ R, int64_t M, int D,
+                                                          const float* __restrict__ gamma, float scale,
+                                                          T* __restrict__ xn, int64_t band_major_mt, int NB,
+                                                          float* r_out, const float* __restrict__ wg,
+                                                          const float* __restrict__ bg, int H,
+                                                          float* __restrict__ gates,
+                                                          const float* __restrict__ gamma2) {
+    // One warp normalises two rows at a time (lane c holds columns 4c + 128i):
+    // the gate weights read from shared memory then feed both rows.
     extern __shared__ float4 swg4[];  // [H][D/4]
     const int D4 = D / 4;
     if (wg) {
@@ -144,112 +146,138 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__
     const int lane = threadIdx.x & 31;
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
     const float4* h4 = reinterpret_cast<const float4*>(gamma2);
-    float4 g[MAXC];
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    for (int64_t m0 = 2 * wid; m0 < M; m0 += 2 * warps) {
+        const bool two = m0 + 1 < M;
+        float4 v[2][MAXC];
+        float ss[2] = {0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-        const int c = lane + 32 * i;
-        g[i] = c < D4 ? g4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t m = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += stride) {
-        const float4* x4 = reinterpret_cast<const float4*>(R + m * D);
-        float4 v[MAXC];
-        float ss = 0.f;
+        for (int r = 0; r < 2; ++r) {
+            const float4* x4 = reinterpret_cast<const float4*>(R + (m0 + (r && two ? 1 : 0)) * D);
 #pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const int c = lane + 32 * i;
-            v[i] = c < D4 ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-            ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+            for (int i = 0; i < MAXC; ++i) {
+                const int c = lane + 32 * i;
+                v[r][i] = c < D4 ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+                ss[r] += v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y + v[r][i].z * v[r][i].z +
+                         v[r][i].w * v[r][i].w;
+            }
         }
-        ss = warp_sum(ss);
-        const float inv = rsqrtf(ss + 1e-12f) * scale;
-        const int64_t orow = band_major_mt > 0 ? (m % NB) * band_major_mt + m / NB : m;
+        ss[0] = warp_sum(ss[0]);
+        ss[1] = warp_sum(ss[1]);
 #pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const int c = lane + 32 * i;
-            v[i] = make_float4(v[i].x * inv * g[i].x, v[i].y * inv * g[i].y, v[i].z * inv * g[i].z,
-                               v[i].w * inv * g[i].w);
-            if (c < D4 && r_out) reinterpret_cast<float4*>(r_out + m * D)[c] = v[i];
+        for (int r = 0; r < 2; ++r) {
+            const int64_t m = m0 + r;
+            const float inv = rsqrtf(ss[r] + 1e-12f) * scale;
+#pragma unroll
+            for (int i = 0; i < MAXC; ++i) {
+                const int c = lane + 32 * i;
+                const float4 g = c < D4 ? __ldg(g4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[r][i] = make_float4(v[r][i].x * inv * g.x, v[r][i].y * inv * g.y, v[r][i].z * inv * g.z,
+                                      v[r][i].w * inv * g.w);
+                if (c < D4 && r_out && (r == 0 || two)) reinterpret_cast<float4*>(r_out + m * D)[c] = v[r][i];
+            }
         }
         if (gamma2) {
             // a second RMSNorm of the (stored) first result: the next block's
             // pre-norm, so the residual stream is read once for both
-            float ss2 = 0.f;
+            float s2[2] = {0.f, 0.f};
 #pragma unroll
-            for (int i = 0; i < MAXC; ++i) ss2 += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
-            ss2 = warp_sum(ss2);
-            const float inv2 = rsqrtf(ss2 + 1e-12f) * scale;
+            for (int r = 0; r < 2; ++r)
 #pragma unroll
-            for (int i = 0; i < MAXC; ++i) {
-                const int c = lane + 32 * i;
-                const float4 g2 = c < D4 ? __ldg(h4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);  // L1-resident
-                v[i] = make_float4(v[i].x * inv2 * g2.x, v[i].y * inv2 * g2.y, v[i].z * inv2 * g2.z,
-                                   v[i].w * inv2 * g2.w);
+                for (int i = 0; i < MAXC; ++i)
+                    s2[r] += v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y + v[r][i].z * v[r][i].z +
+                             v[r][i].w * v[r][i].w;
+            s2[0] = warp_sum(s2[0]);
+            s2[1] = warp_sum(s2[1]);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const float inv2 = rsqrtf(s2[r] + 1e-12f) * scale;
+#pragma unroll
+                for (int i = 0; i < MAXC; ++i) {
+                    const int c = lane + 32 * i;
+                    const float4 g2 = c < D4 ? __ldg(h4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    v[r][i] = make_float4(v[r][i].x * inv2 * g2.x, v[r][i].y * inv2 * g2.y,
+                                          v[r][i].z * inv2 * g2.z, v[r][i].w * inv2 * g2.w);
+                }
             }
         }
+        if (xn) {
 #pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const int c = lane + 32 * i;
-            if (c < D4 && xn) store4<T>(xn + orow * D + 4 * c, v[i]);
+            for (int r = 0; r < 2; ++r) {
+                if (r == 1 && !two) break;
+                const int64_t m = m0 + r;
+                const int64_t orow = band_major_mt > 0 ? (m % NB) * band_major_mt + m / NB : m;
+#pragma unroll
+                for (int i = 0; i < MAXC; ++i) {
+                    const int c = lane + 32 * i;
+                    if (c < D4) store4<T>(xn + orow * D + 4 * c, v[r][i]);
+                }
+            }
         }
         if (wg && H == 8) {
-            // eight dot products at once: per-lane partial sums for all heads,
-            // then a transposing butterfly (each xor step halves the heads a
-            // lane carries) so lane 4h ends with head h: 9 shuffles instead of 40
-            float a[8];
+            // eight dot products per row at once: per-lane partial sums for all
+            // heads, then a transposing butterfly (each xor step halves the
+            // heads a lane carries) so lane 4h ends with head h
+            float a[2][8];
 #pragma unroll
             for (int h = 0; h < 8; ++h) {
-                float acc = 0.f;
+                a[0][h] = 0.f;
+                a[1][h] = 0.f;
 #pragma unroll
                 for (int i = 0; i < MAXC; ++i) {
                     const int c = lane + 32 * i;
                     if (c < D4) {
                         const float4 w = swg4[h * D4 + c];
-                        acc += v[i].x * w.x + v[i].y * w.y + v[i].z * w.z + v[i].w * w.w;
+#pragma unroll
+                        for (int r = 0; r < 2; ++r)
+                            a[r][h] += v[r][i].x * w.x + v[r][i].y * w.y + v[r][i].z * w.z + v[r][i].w * w.w;
                     }
                 }
-                a[h] = acc;
             }
             const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float send = b4 ? a[k] : a[k + 4];
-                const float keep = b4 ? a[k + 4] : a[k];
-                a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-            }
+            for (int r = 0; r < 2; ++r) {
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const float send = b3 ? a[k] : a[k + 2];
-                const float keep = b3 ? a[k + 2] : a[k];
-                a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-            }
-            {
-                const float send = b2 ? a[0] : a[1];
-                const float keep = b2 ? a[1] : a[0];
-                a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-            }
-            a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
-            a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
-            if ((lane & 3) == 0) {
-                const int h = lane >> 2;
-                gates[m * H + h] = 1.0f / (1.0f + expf(-(a[0] + bg[h])));
+                for (int k = 0; k < 4; ++k) {
+                    const float send = b4 ? a[r][k] : a[r][k + 4];
+                    const float keep = b4 ? a[r][k + 4] : a[r][k];
+                    a[r][k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const float send = b3 ? a[r][k] : a[r][k + 2];
+                    const float keep = b3 ? a[r][k + 2] : a[r][k];
+                    a[r][k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+                const float send = b2 ? a[r][0] : a[r][1];
+                const float keep = b2 ? a[r][1] : a[r][0];
+                float t = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                t += __shfl_xor_sync(0xffffffffu, t, 2);
+                t += __shfl_xor_sync(0xffffffffu, t, 1);
+                if ((lane & 3) == 0 && (r == 0 || two)) {
+                    const int h = lane >> 2;
+                    gates[(m0 + r) * H + h] = 1.0f / (1.0f + expf(-(t + bg[h])));
+                }
             }
         } else if (wg) {
-            float mine = 0.f;  // lane h ends up holding the dot product of gate h
-            for (int h = 0; h < H; ++h) {
-                float acc = 0.f;
+            for (int r = 0; r < 2; ++r) {
+                float mine = 0.f;  // lane h ends up holding the dot product of gate h
+                for (int h = 0; h < H; ++h) {
+                    float acc = 0.f;
 #pragma unroll
-                for (int i = 0; i < MAXC; ++i) {
-                    const int c = lane + 32 * i;
-                    if (c < D4) {
-                        const float4 w = swg4[h * D4 + c];
-                        acc += v[i].x * w.x + v[i].y * w.y + v[i].z * w.z + v[i].w * w.w;
+                    for (int i = 0; i < MAXC; ++i) {
+                        const int c = lane + 32 * i;
+                        if (c < D4) {
+                            const float4 w = swg4[h * D4 + c];
+                            acc += v[r][i].x * w.x + v[r][i].y * w.y + v[r][i].z * w.z + v[r][i].w * w.w;
+                        }
                     }
+                    acc = warp_sum(acc);
+                    if (lane == h) mine = acc;
                 }
-                acc = warp_sum(acc);
-                if (lane == h) mine = acc;
+                if (lane < H && (r == 0 || two)) gates[(m0 + r) * H + lane] = 1.0f / (1.0f + expf(-(mine + bg[lane])));
             }
-            if (lane < H) gates[m * H + lane] = 1.0f / (1.0f + expf(-(mine + bg[lane])));
         }
     }
 }
@@ -574,7 +602,7 @@ void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale,
         MBR_CUDA(cudaGetDevice(&dev));
         MBR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     }
-    unsigned grid = (unsigned)std::min<int64_t>(ceil_div(M, 8), (int64_t)sms * 8);
+    unsigned grid = (unsigned)std::min<int64_t>(ceil_div(M, 16), (int64_t)sms * 6);  // 2 rows per warp, 3 blocks / SM x 2 waves
     MBR_DISPATCH_DTYPE(dtype, T, {
         auto run = [&](auto kern) {
             if (sm > 48 * 1024)
