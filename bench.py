@@ -285,7 +285,10 @@ def main():
     seconds = wl["seconds"] * world
     track = pink_noise(seconds, 1234)
     N = track.shape[1]
-    stream = torch.cuda.current_stream(dev)
+    # a dedicated stream (the legacy default stream cannot be graph-captured);
+    # made current so that torch's copies and NCCL calls order with our work
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     d_track = torch.from_numpy(track).to(dev)
     d_out = torch.empty((S, C, N), dtype=torch.float32, device=dev)
 

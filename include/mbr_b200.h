@@ -145,6 +145,14 @@ MBR_API int mbr_shard_add_boundary(mbr_handle* h, int64_t N, float overlap, int 
 MBR_API int mbr_shard_finalize(mbr_handle* h, int64_t N, float overlap, int rank, int world, float* d_acc,
                                float* d_wsum, float* d_out, int64_t out_stride, void* stream);
 
+/* CUDA-graph replay of the chunk forward (on by default): the first forward
+ * with a given input shape and input/output buffer pair runs eagerly and is
+ * captured; later ones replay the graph.  Streams that cannot be captured (the
+ * legacy default stream, a stream the caller is capturing) always run eagerly.
+ * This is the "graph capture per (B, T)" step of the chunk-batched pipeline
+ * (src/inference_app.cpp:92-128 runs every chunk op by op). */
+MBR_API int mbr_set_graphs(mbr_handle* h, int enable);
+
 /* Kernel backend selection (MBR_BACKEND_*) for the GEMMs and the attention. */
 MBR_API int mbr_set_backend(mbr_handle* h, int gemm, int attention);
 

@@ -324,6 +324,19 @@ MBR_API int mbr_shard_finalize(mbr_handle* h, int64_t N, float overlap, int rank
     });
 }
 
+MBR_API int mbr_set_graphs(mbr_handle* h, int enable) {
+    return guard([&] {
+        need(h, "null argument");
+        MBR_CUDA(cudaSetDevice(h->device));
+        h->model->set_graphs(enable != 0);
+        for (auto& p : h->peers) {
+            MBR_CUDA(cudaSetDevice(p->device));
+            p->model->set_graphs(enable != 0);
+        }
+        MBR_CUDA(cudaSetDevice(h->device));
+    });
+}
+
 MBR_API int mbr_set_backend(mbr_handle* h, int gemm, int attention) {
     return guard([&] {
         need(h, "null argument");

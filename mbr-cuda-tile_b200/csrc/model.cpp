@@ -338,6 +338,8 @@ MelBandRoformer::~MelBandRoformer() {
     for (auto& kv : ws_) {
         cudaFree(kv.second->base);
         if (kv.second->d_tiles) cudaFree(kv.second->d_tiles);
+        for (Workspace::Graph& g : kv.second->graphs)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
     }
     cudaFree(d_err_);
     cudaFree(wbase_);
@@ -847,7 +849,54 @@ void MelBandRoformer::forward(const float* d_audio, int B, int64_t L, float* d_o
     MBR_CHECK(B >= 1, "batch must be >= 1");
     MBR_CUDA(cudaSetDevice(device_));
     Workspace& ws = workspace(B, L);
+    // The legacy default stream cannot be captured; a stream the caller is
+    // capturing already records our launches into the caller's graph.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const bool capturable = graphs_on_ && !prof_on_ && st != nullptr && st != cudaStreamLegacy &&
+                            st != cudaStreamPerThread && cudaStreamIsCapturing(st, &cs) == cudaSuccess &&
+                            cs == cudaStreamCaptureStatusNone;
+    if (!capturable) {
+        run_forward(ws, d_audio, d_out, -1, nullptr, nullptr, st);
+        return;
+    }
+    for (const Workspace::Graph& g : ws.graphs)
+        if (g.in == d_audio && g.out == d_out) {
+            if (!g.exec) break;
+            MBR_CUDA(cudaGraphLaunch(g.exec, st));
+            launches_ = g.launches;
+            return;
+        }
+    // first use of this buffer pair: run eagerly (sets kernel attributes and
+    // computes the result), then capture the same launch sequence for reuse
     run_forward(ws, d_audio, d_out, -1, nullptr, nullptr, st);
+    bool known = false;
+    for (const Workspace::Graph& g : ws.graphs) known |= g.in == d_audio && g.out == d_out;
+    if (known) return;  // capture failed before: stay eager
+    Workspace::Graph g{d_audio, d_out, nullptr, launches_};
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+        bool ok = true;
+        try {
+            run_forward(ws, d_audio, d_out, -1, nullptr, nullptr, st);
+        } catch (const Error&) {
+            ok = false;
+        }
+        const cudaError_t e = cudaStreamEndCapture(st, &graph);
+        if (ok && e == cudaSuccess && graph &&
+            cudaGraphInstantiateWithFlags(&g.exec, graph, 0) != cudaSuccess)
+            g.exec = nullptr;
+        if (graph) cudaGraphDestroy(graph);
+    }
+    cudaGetLastError();  // a failed capture leaves no sticky error; clear the last one
+    launches_ = g.launches;
+    ws.graphs.push_back(g);
+}
+
+void MelBandRoformer::drop_graphs() {
+    for (auto& kv : ws_)
+        for (Workspace::Graph& g : kv.second->graphs)
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+    for (auto& kv : ws_) kv.second->graphs.clear();
 }
 
 int64_t MelBandRoformer::forward_tap(const float* d_audio, int B, int64_t L, int tap, float* d_tap, cudaStream_t st) {

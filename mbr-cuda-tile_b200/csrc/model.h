@@ -114,7 +114,15 @@ public:
     void set_backend(int gemm, int attention) {
         gemm_backend_ = gemm;
         attn_backend_ = attention;
+        drop_graphs();
     }
+    // Replay the forward from a CUDA graph captured per input shape and buffer
+    // pair (on by default; streams that cannot be captured run eagerly).
+    void set_graphs(bool on) {
+        graphs_on_ = on;
+        if (!on) drop_graphs();
+    }
+    bool graphs() const { return graphs_on_; }
     int gemm_backend() const { return gemm_backend_; }
     int attn_backend() const { return attn_backend_; }
     // Kernel launches issued by the last forward().
@@ -197,6 +205,14 @@ private:
         Plan band_split;
         std::vector<Plan> layer_plans;  // [depth][2][layers][4]: qkv, out, ffn1, ffn2
         std::vector<std::vector<Plan>> mask_plans;  // [stem][linear]
+        // CUDA graphs of the whole forward, one per (input, output) buffer pair
+        struct Graph {
+            const float* in;
+            float* out;
+            cudaGraphExec_t exec;  // null: capture failed, run eagerly
+            int64_t launches;
+        };
+        std::vector<Graph> graphs;
     };
 
     Workspace& workspace(int B, int64_t L);
@@ -214,6 +230,8 @@ private:
     int64_t J_ = 0, KP_ = 0;
     int gemm_backend_ = BACKEND_SIMT, attn_backend_ = BACKEND_SIMT;
     int64_t launches_ = 0;
+    bool graphs_on_ = true;
+    void drop_graphs();
 
     // profiler state
     bool prof_on_ = false;

@@ -27,7 +27,7 @@ INFO = dict(dim=0, depth=1, num_stems=2, channels=3, num_bands=4, sample_rate=5,
 EXPORTS = [
     "mbr_last_error", "mbr_version", "mbr_create", "mbr_destroy", "mbr_get_info", "mbr_output_length",
     "mbr_forward_chunk", "mbr_forward_tap", "mbr_separate_device", "mbr_separate", "mbr_shard_info",
-    "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_backend", "mbr_last_launches",
+    "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_graphs", "mbr_set_backend", "mbr_last_launches",
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
     "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_op_attention", "mbr_op_linear",
     "mbr_rope_tables",
@@ -73,6 +73,7 @@ def lib():
         L.mbr_shard_add_boundary.argtypes = [vp, i64, c_float, c_int, c_int, fp, fp, fp, fp, i64, vp]
         L.mbr_shard_finalize.argtypes = [vp, i64, c_float, c_int, c_int, fp, fp, fp, i64, vp]
         L.mbr_set_backend.argtypes = [vp, c_int, c_int]
+        L.mbr_set_graphs.argtypes = [vp, c_int]
         L.mbr_last_launches.argtypes = [vp, i64p]
         L.mbr_sync_check.argtypes = [vp]
         L.mbr_profile_enable.argtypes = [vp, c_int]
@@ -282,6 +283,10 @@ class Model:
         v = ctypes.c_int64()
         _check(lib().mbr_output_length(self.h, int(L), ctypes.byref(v)))
         return v.value
+
+    def set_graphs(self, enable: bool = True):
+        """CUDA-graph replay of the chunk forward (on by default)."""
+        _check(lib().mbr_set_graphs(self.h, int(bool(enable))))
 
     def set_backend(self, gemm: int = BACKEND_TC, attention: int = BACKEND_TC):
         _check(lib().mbr_set_backend(self.h, int(gemm), int(attention)))
