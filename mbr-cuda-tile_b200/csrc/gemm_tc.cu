@@ -13,6 +13,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -35,11 +36,14 @@ constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 constexpr int kStageRowBytes = 128;                    // one swizzled 128-byte row per lane
 constexpr int kStagingPerWarp = 32 * kStageRowBytes;   // 32 rows x 128 B
 
-template <int BN>
+// CG = 1: one CTA computes a 128 x BN tile.  CG = 2: a CTA pair (cluster of
+// two) computes 256 x BN with cta_group::2 MMAs; each CTA holds its 128 A rows
+// and half of the B rows, so a stage is 16 KB + BN*64 bytes per CTA.
+template <int BN, int CG = 1>
 struct TileCfg {
-    static constexpr int STAGES = BN == 128 ? 6 : 4;
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = (BN / CG) * BK * 2;
+    static constexpr int STAGES = CG == 2 ? (BN == 128 ? 8 : 6) : (BN == 128 ? 6 : 4);
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGING_OFF = STAGES * STAGE_BYTES;  // 1024-aligned
     static constexpr int BAR_OFF = STAGING_OFF + kEpiWarps * kStagingPerWarp;
@@ -247,12 +251,17 @@ __device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float
     }
 }
 
-template <typename T, int BN, int EPI>
+template <typename T, int BN, int EPI, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, int c_tma, const ops::GemmGroup* __restrict__ groups,
                    const int4* __restrict__ tiles, int ntiles, int* err, const EpiQKV qkv) {
-    using Cfg = TileCfg<BN>;
+    using Cfg = TileCfg<BN, CG>;
+    // CTA pair: rank 0 issues the MMAs, counts both CTAs' TMA bytes on its full
+    // barriers and collects both CTAs' epilogue arrivals on its acc_empty
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
+    const bool leader = rank == 0;
+    const int cta_tile0 = (int)blockIdx.x / CG, cta_tile_step = (int)gridDim.x / CG;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
@@ -271,16 +280,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], kEpiWarps);
+            mbar_init(&acc_empty[b], kEpiWarps * CG);
         }
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (CG == 2) {
+            tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // the peer's barriers exist before any remote arrive / TMA count
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -290,7 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             prefetch_tensormap(&tmB);
             uint32_t it = 0;
             bool alive = true;
-            for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x) {
+            for (int t = cta_tile0; t < ntiles && alive; t += cta_tile_step) {
                 const int4 tl = tiles[t];
                 const ops::GemmGroup& g = groups[tl.x];
                 for (int kb = 0; kb < tl.w; ++kb, ++it) {
@@ -300,20 +315,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         alive = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
                     const int kx = g.k_col0 + kb * BK;
-                    tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kx, g.a_row0 + tl.y, &full[s]);
-                    tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kx, g.b_row0 + tl.z, &full[s]);
+                    if constexpr (CG == 2) {
+                        // both CTAs' bytes complete on the leader's full barrier
+                        const uint32_t fb = map_to_cta(smem_u32(&full[s]), 0);
+                        if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                        tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, kx, g.a_row0 + tl.y + (int)rank * BM, fb);
+                        tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, kx, g.b_row0 + tl.z + (int)rank * (BN / 2), fb);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                        tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kx, g.a_row0 + tl.y, &full[s]);
+                        tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kx, g.b_row0 + tl.z, &full[s]);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16(BM, BN, IsBf16<T>::value);
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_f16(BM * CG, BN, IsBf16<T>::value);
             uint32_t it = 0;
             int tcount = 0;
             bool alive = true;
-            for (int t = blockIdx.x; t < ntiles && alive; t += gridDim.x, ++tcount) {
+            for (int t = cta_tile0; t < ntiles && alive; t += cta_tile_step, ++tcount) {
                 const int4 tl = tiles[t];
                 const int K = groups[tl.x].K;
                 const int buf = tcount & 1;
@@ -332,12 +355,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
                     const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
                     const int ksteps = min(BK / 16, (K - kb * BK) / 16);
-                    for (int k = 0; k < ksteps; ++k)
-                        mma_f16(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, (kb | k) != 0);
-                    mma_commit(&empty[s]);
+                    if constexpr (CG == 2) {
+                        for (int k = 0; k < ksteps; ++k)
+                            mma_f16_pair(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc,
+                                         (kb | k) != 0);
+                        mma_commit_pair(&empty[s]);  // frees the stage in both CTAs
+                    } else {
+                        for (int k = 0; k < ksteps; ++k)
+                            mma_f16(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc, (kb | k) != 0);
+                        mma_commit(&empty[s]);
+                    }
                 }
                 if (!alive) break;
-                mma_commit(&acc_full[buf]);
+                if constexpr (CG == 2) mma_commit_pair(&acc_full[buf]);
+                else mma_commit(&acc_full[buf]);
             }
         }
     } else {
@@ -345,8 +376,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int half = (warp - 2) >> 2;
         constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp
         int tcount = 0;
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tcount) {
-            const int4 tl = tiles[t];
+        // this CTA's 128 rows of the tile
+        const uint32_t acc_empty_leader = CG == 2 ? map_to_cta(smem_u32(&acc_empty[0]), 0) : 0;
+        for (int t = cta_tile0; t < ntiles; t += cta_tile_step, ++tcount) {
+            int4 tl = tiles[t];
+            tl.y += (int)rank * BM;
             const ops::GemmGroup g = groups[tl.x];
             const int buf = tcount & 1;
             const uint32_t use = tcount >> 1;
@@ -429,16 +463,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            if (lane == 0) {
+                if constexpr (CG == 2) mbar_arrive_cluster(acc_empty_leader + 8u * buf);  // the leader's barrier
+                else mbar_arrive(&acc_empty[buf]);
+            }
         }
         if (lane == 0) bulk_wait_all();  // outstanding TMA stores complete before exit
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // no CTA leaves while its peer may still touch its memory
+    else __syncthreads();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+        if constexpr (CG == 2) tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+        else tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
 }
 
@@ -503,6 +542,15 @@ void make_out_map(CUtensorMap* m, const GemmPlanTC& p, bool& swapped) {
     if (r != CUDA_SUCCESS) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled (output) failed: " + std::to_string((int)r));
 }
 
+// MBR_GEMM_PAIRS=0 keeps every GEMM on single-CTA tiles (A/B comparisons).
+bool pair_tiles_off() {
+    static const bool off = [] {
+        const char* e = std::getenv("MBR_GEMM_PAIRS");
+        return e && e[0] == '0';
+    }();
+    return off;
+}
+
 int num_sms() {
     int dev = 0, n = 0;
     MBR_CUDA(cudaGetDevice(&dev));
@@ -510,23 +558,41 @@ int num_sms() {
     return n;
 }
 
-template <typename T, int BN, int EPI>
-void launch_one(const GemmLaunch& L, int* d_err, cudaStream_t st) {
-    auto kern = gemm_tc_kernel<T, BN, EPI>;
+template <typename T, int BN, int EPI, int CG>
+void launch_cg(const GemmLaunch& L, int* d_err, cudaStream_t st) {
+    auto kern = gemm_tc_kernel<T, BN, EPI, CG>;
+    using Cfg = TileCfg<BN, CG>;
     static bool attr[64] = {};  // per instantiation and device
     static int sms[64] = {};
     int dev = 0;
     MBR_CUDA(cudaGetDevice(&dev));
     MBR_CHECK(dev >= 0 && dev < 64, "device index out of range");
     if (!attr[dev]) {
-        MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TileCfg<BN>::SMEM));
+        MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
         sms[dev] = num_sms();
         attr[dev] = true;
     }
-    int grid = std::min(L.ntiles, sms[dev]);
-    kern<<<grid, kGemmThreads, TileCfg<BN>::SMEM, st>>>(L.tmA, L.tmB, L.tmC, L.c_tma, L.groups, L.tiles, L.ntiles,
-                                                         d_err, L.qkv);
-    MBR_CUDA(cudaGetLastError());
+    // persistent: one CTA (pair) per SM (pair), at most one per tile
+    const int grid = CG * std::min(L.ntiles, sms[dev] / CG);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = CG;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    MBR_CUDA(cudaLaunchKernelEx(&cfg, kern, L.tmA, L.tmB, L.tmC, L.c_tma, L.groups, L.tiles, L.ntiles, d_err, L.qkv));
+}
+
+template <typename T, int BN, int EPI>
+void launch_one(const GemmLaunch& L, int* d_err, cudaStream_t st) {
+    if (L.cg == 2) launch_cg<T, BN, EPI, 2>(L, d_err, st);
+    else launch_cg<T, BN, EPI, 1>(L, d_err, st);
 }
 
 template <typename T, int BN>
@@ -537,8 +603,8 @@ void launch_bn(const GemmLaunch& L, int* d_err, cudaStream_t st) {
         case ops::EPI_ADD_F32: launch_one<T, BN, ops::EPI_ADD_F32>(L, d_err, st); break;
         case ops::EPI_GELU_T: launch_one<T, BN, ops::EPI_GELU_T>(L, d_err, st); break;
         case ops::EPI_TANH_T: launch_one<T, BN, ops::EPI_TANH_T>(L, d_err, st); break;
-        case ops::EPI_GLU_F32: launch_one<T, BN, ops::EPI_GLU_F32>(L, d_err, st); break;
-        case ops::EPI_QKV: launch_one<T, BN, ops::EPI_QKV>(L, d_err, st); break;
+        case ops::EPI_GLU_F32: launch_cg<T, BN, ops::EPI_GLU_F32, 1>(L, d_err, st); break;
+        case ops::EPI_QKV: launch_cg<T, BN, ops::EPI_QKV, 1>(L, d_err, st); break;
         case ops::EPI_ROPE_T: launch_one<T, BN, ops::EPI_ROPE_T>(L, d_err, st); break;
         default: throw Error(ERR_INVALID, "tc gemm: bad epilogue");
     }
@@ -577,7 +643,11 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
                       bn % 64 == 0,
                   "tc gemm: QKV epilogue needs head dim 64 and its q/k/v/rope buffers");
     make_map(&L.tmA, p.a_base, p.a_rows, p.a_cols, BM, dtype);
-    make_map(&L.tmB, p.b_base, p.b_rows, p.b_cols, bn, dtype);
+    // CTA pairs for the large single-problem GEMMs with staged epilogues (one
+    // 256-row tile then wastes little on the ragged last row block)
+    const bool staged = p.c_dtype >= 0 && p.epi != ops::EPI_QKV && p.epi != ops::EPI_GLU_F32;
+    L.cg = staged && p.maxM >= 4096 && !pair_tiles_off() ? 2 : 1;
+    make_map(&L.tmB, p.b_base, p.b_rows, p.b_cols, bn / L.cg, dtype);
     L_first = tiles.size();
     for (int gi = 0; gi < p.ngroups; ++gi) {
         const ops::GemmGroup& g = p.h_groups[gi];
@@ -587,7 +657,7 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
                   "tc gemm: group outside its operand tensors");
         MBR_CHECK(g.k_col0 % 8 == 0, "tc gemm: K offset must be 16-byte aligned");
         int kb = (int)ceil_div(g.K, BK);
-        for (int m0 = 0; m0 < g.M; m0 += BM)
+        for (int m0 = 0; m0 < g.M; m0 += BM * L.cg)
             for (int n0 = 0; n0 < g.N; n0 += bn) tiles.push_back(make_int4(gi, m0, n0, kb));
     }
     L.ntiles = (int)(tiles.size() - L_first);

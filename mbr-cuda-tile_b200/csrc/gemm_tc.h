@@ -58,6 +58,7 @@ struct GemmLaunch {
     const int4* tiles = nullptr;  // device: (group, m0, n0, k-blocks)
     int ntiles = 0;
     int bn = 128;
+    int cg = 1;  // 2: CTA pairs (cluster of two, cta_group::2 MMAs on 256-row tiles)
     int epi = 0;
     const ops::GemmGroup* groups = nullptr;
     EpiQKV qkv;
