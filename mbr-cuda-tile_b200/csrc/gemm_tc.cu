@@ -643,10 +643,14 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
                       bn % 64 == 0,
                   "tc gemm: QKV epilogue needs head dim 64 and its q/k/v/rope buffers");
     make_map(&L.tmA, p.a_base, p.a_rows, p.a_cols, BM, dtype);
-    // CTA pairs for the large single-problem GEMMs with staged epilogues (one
-    // 256-row tile then wastes little on the ragged last row block)
-    const bool staged = p.c_dtype >= 0 && p.epi != ops::EPI_QKV && p.epi != ops::EPI_GLU_F32;
-    L.cg = staged && p.maxM >= 4096 && !pair_tiles_off() ? 2 : 1;
+    // CTA pairs for the large residual GEMMs with a long K loop (FFN2): the
+    // pair halves each SM's B traffic there.  Where the epilogue is heavy
+    // relative to K (QKV + RoPE, FFN1 + GELU, K = 384) the coupling of the two
+    // CTAs' epilogues costs more than it saves, measured on B200.
+    int maxK = 0;
+    for (int gi = 0; gi < p.ngroups; ++gi) maxK = std::max(maxK, p.h_groups[gi].K);
+    L.cg = p.c_dtype >= 0 && p.epi == ops::EPI_ADD_F32 && p.maxM >= 4096 && maxK >= 1024 && !pair_tiles_off() ? 2
+                                                                                                              : 1;
     make_map(&L.tmB, p.b_base, p.b_rows, p.b_cols, bn / L.cg, dtype);
     L_first = tiles.size();
     for (int gi = 0; gi < p.ngroups; ++gi) {
