@@ -250,6 +250,9 @@ def main():
     ap.add_argument("--workload", default="std", choices=sorted(WORKLOADS))
     ap.add_argument("--cpu-excerpt", type=float, default=1.0, help="seconds of audio in the CPU sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--op-sweep", action="store_true",
+                    help="tensor-op sweep: achieved HBM GB/s of every stand-alone op over [B*801*60, D] activations "
+                         "(one JSON line per case, then a summary line)")
     ap.add_argument("--single-chunk", action="store_true",
                     help="profiling aid: run exactly warmup+steps forwards of one chunk batch and print their time "
                          "(not the benchmark line)")
@@ -259,6 +262,8 @@ def main():
         return run_reference(args, wl)
     if args.single_chunk:
         return run_single_chunk(args, wl)
+    if args.op_sweep:
+        return run_op_sweep(args)
 
     import torch
 
@@ -434,6 +439,99 @@ def main():
         os.rmdir(tmpdir)
     except OSError:
         pass
+    return 0
+
+
+def run_op_sweep(args):
+    """Tensor-op sweep: activations [B*801*60, D] seeded
+    N(0, 1), D in {192, 384, 512}, B in {1, 4, 8}, fp32 / fp16 / bf16.  Each op
+    is timed with CUDA events around one launch after an L2 flush (a 256 MiB
+    write), averaged over `--steps` launches after `--warmup`; GB/s counts the
+    algorithmic bytes (every input read once, every output written once)."""
+    import torch
+
+    import csm_tool
+    import cudasep
+
+    torch.cuda.set_device(0)
+    peak = load_peaks()["hbm_gbs"]
+    T, NB, J2 = 801, 60, 2 * 3958  # frames, bands, band-freq values (7916) of the 60-band split
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    tdt = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
+    reps, warm = max(args.steps, 3), max(args.warmup, 1)
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        tot = 0.0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(reps):
+            flush.zero_()
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / reps / 1e3
+
+    results = []
+
+    def report(op, dtype, D, B, nbytes, sec):
+        gbs = nbytes / sec / 1e9
+        line = {"op": op, "dtype": dtype, "D": D, "B": B, "bytes": int(nbytes), "us": sec * 1e6, "GB/s": gbs,
+                "frac_of_hbm_peak": gbs / peak}
+        results.append(line)
+        print(json.dumps(line), flush=True)
+
+    with tempfile.TemporaryDirectory() as d:
+        csm = os.path.join(d, "m.csm")
+        cfg = csm_tool.base_config(**csm_tool.PRESETS["tiny"])
+        csm_tool.write_csm(csm, cfg, csm_tool.random_weights(cfg, 0))
+        model = cudasep.Model(csm, 0, "fp32")
+        for dtype in ("fp32", "fp16", "bf16"):
+            dt, e = tdt[dtype], torch.tensor([], dtype=tdt[dtype]).element_size()
+            for B in (1, 4, 8):
+                rows = B * T * NB
+                for D in (192, 384, 512):
+                    N = rows * D
+                    x = torch.randn(rows, D, generator=gen, device="cuda").to(dt)
+                    y = torch.empty_like(x)
+                    gamma = torch.ones(D, device="cuda")
+                    report("rms_norm", dtype, D, B, 2 * N * e + D * 4,
+                           timed(lambda: cudasep.op_rms_norm(x, gamma, D ** 0.5, y=y)))
+                    x2 = torch.randn(rows, D, generator=gen, device="cuda").to(dt)
+                    report("add", dtype, D, B, 3 * N * e, timed(lambda: cudasep.op_add(x, x2, y=y)))
+                    del x2
+                    report("gelu", dtype, D, B, 2 * N * e, timed(lambda: cudasep.op_gelu(x, y=y)))
+                    H = D // 64
+                    gate = torch.rand(rows, H, generator=gen, device="cuda").to(dt)
+                    report("sigmoid_gate", dtype, D, B, 2 * N * e + rows * H * e,
+                           timed(lambda: cudasep.op_sigmoid_gate(x, gate, H, y=y)))
+                    c, s_ = cudasep.rope_tables(T, 64)
+                    ct, st = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+                    xr, yr = x.view(B * NB, T, H, 64), y.view(B * NB, T, H, 64)
+                    report("rope", dtype, D, B, 2 * N * e + 2 * c.nbytes,
+                           timed(lambda: cudasep.op_rope(xr, ct, st, y=yr)))
+                    del x, y, gate
+                # band ops (independent of D)
+                spec = torch.randn(B, 2, 1025, T, 2, generator=gen, device="cuda")
+                xb = torch.empty(B, T, J2, dtype=dt, device="cuda")
+                report("band_gather", dtype, 0, B, spec.numel() * 4 + xb.numel() * e,
+                       timed(lambda: model.op_band_gather(spec, out_dtype=dt)))
+                masks = torch.randn(1, B * T, J2, generator=gen, device="cuda").to(dt)
+                report("mask_scatter", dtype, 0, B,
+                       masks.numel() * e + spec.numel() * 4 + 1025 * 4 + B * 2 * 1025 * T * 2 * 4,
+                       timed(lambda: model.op_mask_scatter(spec, masks)))
+                del spec, xb, masks
+        model.close()
+    by_op = {}
+    for r in results:
+        by_op.setdefault(r["op"], []).append(r["frac_of_hbm_peak"])
+    print(json.dumps({"metric": "tensor-op HBM GB/s vs peak", "peak_gbs": peak,
+                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth)",
+                      "median_frac_by_op": {k: sorted(v)[len(v) // 2] for k, v in by_op.items()},
+                      "min_frac_by_op": {k: min(v) for k, v in by_op.items()}, "cases": len(results)}), flush=True)
     return 0
 
 

@@ -477,7 +477,7 @@ MBR_API int mbr_op_band_gather(mbr_handle* h, const float* d_spec, int B, int T,
         need(h && d_spec && d_x && B > 0 && T > 0, "bad argument");
         MBR_CUDA(cudaSetDevice(h->device));
         mbr::opsapi::band_gather((const float2*)d_spec, B, h->model->channels(), 1025, T, h->model->d_freq_indices(),
-                                 h->model->band_freqs(), d_x, dtype, (cudaStream_t)stream);
+                                 h->model->band_freqs(), h->model->band_tiles(), d_x, dtype, (cudaStream_t)stream);
     });
 }
 
@@ -487,8 +487,8 @@ MBR_API int mbr_op_mask_scatter(mbr_handle* h, const float* d_spec, const void* 
         need(h && d_spec && d_masks && d_out && B > 0 && S > 0 && T > 0, "bad argument");
         MBR_CUDA(cudaSetDevice(h->device));
         mbr::opsapi::mask_scatter((const float2*)d_spec, d_masks, B, S, h->model->channels(), 1025, T,
-                                  h->model->d_rev_off(), h->model->d_rev_idx(), h->model->d_bands_per_freq(),
-                                  h->model->band_freqs(), (float2*)d_out, dtype, (cudaStream_t)stream);
+                                  h->model->d_bands_per_freq(), h->model->band_freqs(), h->model->band_tiles(),
+                                  (float2*)d_out, dtype, (cudaStream_t)stream);
     });
 }
 

@@ -4,6 +4,9 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cstdint>
+#include <type_traits>
+
 #include "common.h"
 
 namespace mbr {
@@ -28,6 +31,47 @@ template <>
 __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 template <>
 __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// complex value (two floats) <-> a pair of elements of T stored together
+// (one 8-byte word for float, one 4-byte word for the 16-bit types)
+template <typename T>
+struct PairOf {
+    using type = uint32_t;
+};
+template <>
+struct PairOf<float> {
+    using type = float2;
+};
+template <typename T>
+__device__ __forceinline__ float2 pair_to_f32(typename PairOf<T>::type p) {
+    if constexpr (std::is_same_v<T, float>) {
+        return p;
+    } else if constexpr (std::is_same_v<T, __half>) {
+        return __half22float2(*reinterpret_cast<const __half2*>(&p));
+    } else {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&p));
+    }
+}
+template <typename T>
+__device__ __forceinline__ void store_pair(T* dst, float2 v) {
+    if constexpr (std::is_same_v<T, float>) {
+        *reinterpret_cast<float2*>(dst) = v;
+    } else if constexpr (std::is_same_v<T, __half>) {
+        *reinterpret_cast<__half2*>(dst) = __float22half2_rn(v);
+    } else {
+        *reinterpret_cast<__nv_bfloat162*>(dst) = __float22bfloat162_rn(v);
+    }
+}
+
+// asynchronous global -> shared copy of N (4, 8 or 16) bytes, both addresses
+// N-byte aligned; cp_async_wait_all() waits for all of this thread's copies
+template <int N>
+__device__ __forceinline__ void cp_async(void* smem, const void* gmem) {
+    static_assert(N == 4 || N == 8 || N == 16, "cp.async copies 4, 8 or 16 bytes");
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(s), "l"(gmem), "n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "common.h"
+#include "ops_api.h"
 #include "gemm_tc.h"
 #include "ops.h"
 #include "weights.h"
@@ -99,6 +100,8 @@ public:
     const int* d_rev_off() const { return d_rev_off_; }
     const int* d_rev_idx() const { return d_rev_idx_; }
     const float* d_bands_per_freq() const { return d_nbpf_; }
+    // Frequency-range tiles of the band map for the stand-alone band ops.
+    const opsapi::BandTiles& band_tiles() const { return band_tiles_; }
     int64_t frames(int64_t L) const;      // STFT frames T of an L-sample input
     int64_t out_length(int64_t L) const;  // output samples of an L-sample input
 
@@ -252,6 +255,8 @@ private:
     void* wbase_ = nullptr;  // single device allocation holding every weight
     int* d_err_ = nullptr;   // error word of the tensor-core kernels
     int *d_fi_, *d_band_jofs_, *d_band_kofs_, *d_rev_off_, *d_rev_idx_;
+    opsapi::BandTiles band_tiles_;
+    void* d_band_tiles_ = nullptr;
     float *d_nbpf_, *d_window_, *d_bs_gamma_, *d_bs_bias_;
     float2* d_twiddle_;
     void* d_wbs_;

@@ -82,7 +82,7 @@ __global__ void gelu_kernel(const T* __restrict__ a, T* __restrict__ y, int64_t 
         Vec8<T> x;
         x.load(a + 8 * i);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x.v[k] = gelu_erf(x.v[k]);
+        for (int k = 0; k < 8; ++k) x.v[k] = gelu_as(x.v[k]);  // exact-erf GELU, A&S 7.1.26 (|err| <= 2e-7)
         x.store(y + 8 * i);
     }
 }
@@ -91,12 +91,13 @@ __global__ void gelu_kernel(const T* __restrict__ a, T* __restrict__ y, int64_t 
 template <typename T>
 __global__ void gate_kernel(const T* __restrict__ x, const T* __restrict__ g, T* __restrict__ y, int64_t rows, int H,
                             int dh) {
-    const int per_row = H * dh / 8;
+    const unsigned per_row = (unsigned)(H * dh / 8), dh8 = (unsigned)(dh / 8);
     const int64_t n8 = rows * per_row;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / per_row;
-        const int h = (int)(i % per_row) * 8 / dh;
-        const float gv = to_f32(g[r * H + h]);
+        // 32-bit index arithmetic (n8 < 2^32 checked on the host)
+        const unsigned r = (unsigned)i / per_row;
+        const int h = (int)(((unsigned)i - r * per_row) / dh8);
+        const float gv = to_f32(g[(int64_t)r * H + h]);
         Vec8<T> a;
         a.load(x + 8 * i);
 #pragma unroll
@@ -105,40 +106,48 @@ __global__ void gate_kernel(const T* __restrict__ x, const T* __restrict__ g, T*
     }
 }
 
-// RMSNorm with gamma, dtype in / dtype out; one warp per row, D % 8 == 0, D <= 1024.
+// RMSNorm with gamma, dtype in / dtype out; D % 8 == 0, D <= 1024.  A warp
+// normalises two rows at a time (both rows' loads in flight together).
 template <typename T, int MAXC>
 __global__ void __launch_bounds__(256) rms_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
                                                   T* __restrict__ y, int64_t rows, int D, float scale) {
     const int lane = threadIdx.x & 31, D8 = D / 8;
-    float g[MAXC][8];
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r0 = 2 * ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)); r0 < rows;
+         r0 += 2 * warps) {
+        const bool two = r0 + 1 < rows;
+        Vec8<T> v[2][MAXC];
+        float ss[2] = {0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-        const int c = lane + 32 * i;
+        for (int q = 0; q < 2; ++q) {
+            const int64_t r = two ? r0 + q : r0;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) g[i][k] = c < D8 ? gamma[8 * c + k] : 0.f;
-    }
-    const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += stride) {
-        Vec8<T> v[MAXC];
-        float ss = 0.f;
+            for (int i = 0; i < MAXC; ++i) {
+                const int c = lane + 32 * i;
+                if (c < D8) {
+                    v[q][i].load(x + r * D + 8 * c);
 #pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const int c = lane + 32 * i;
-            if (c < D8) {
-                v[i].load(x + r * D + 8 * c);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) ss += v[i].v[k] * v[i].v[k];
+                    for (int k = 0; k < 8; ++k) ss[q] += v[q][i].v[k] * v[q][i].v[k];
+                }
             }
         }
-        ss = warp_sum(ss);
-        const float inv = rsqrtf(ss + 1e-12f) * scale;
+        ss[0] = warp_sum(ss[0]);
+        ss[1] = warp_sum(ss[1]);
 #pragma unroll
-        for (int i = 0; i < MAXC; ++i) {
-            const int c = lane + 32 * i;
-            if (c < D8) {
+        for (int q = 0; q < 2; ++q) {
+            if (q == 1 && !two) break;
+            const float inv = rsqrtf(ss[q] + 1e-12f) * scale;
 #pragma unroll
-                for (int k = 0; k < 8; ++k) v[i].v[k] *= inv * g[i][k];
-                v[i].store(y + r * D + 8 * c);
+            for (int i = 0; i < MAXC; ++i) {
+                const int c = lane + 32 * i;
+                if (c < D8) {
+                    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * c);
+                    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * c + 1);
+                    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) v[q][i].v[k] *= inv * g[k];
+                    v[q][i].store(y + (r0 + q) * D + 8 * c);
+                }
             }
         }
     }
@@ -150,18 +159,21 @@ template <typename T>
 __global__ void rope_kernel(const T* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
                             T* __restrict__ y, int64_t seqs, int L, int H) {
     const int64_t n8 = seqs * L * H * 8;  // 8 chunks of 8 per 64-wide head
+    const unsigned hh = (unsigned)(8 * H), ll = (unsigned)L;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
         const int chunk = (int)(i & 7);
-        const int p = (int)((i / (8 * H)) % L);
+        const int p = (int)(((unsigned)i / hh) % ll);  // 32-bit (n8 < 2^32 checked on the host)
         Vec8<T> a;
         a.load(x + 8 * i);
+        // pairs 4*chunk .. 4*chunk+3 of position p: one 16-byte load of each table
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + p * 32) + chunk);
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + p * 32) + chunk);
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int pi = chunk * 4 + k;
-            const float c = cs[p * 32 + pi], s = sn[p * 32 + pi];
             const float x0 = a.v[2 * k], x1 = a.v[2 * k + 1];
-            a.v[2 * k] = x0 * c - x1 * s;
-            a.v[2 * k + 1] = x0 * s + x1 * c;
+            a.v[2 * k] = x0 * cc[k] - x1 * ss[k];
+            a.v[2 * k + 1] = x0 * ss[k] + x1 * cc[k];
         }
         a.store(y + 8 * i);
     }
@@ -169,61 +181,152 @@ __global__ void rope_kernel(const T* __restrict__ x, const float* __restrict__ c
 
 // Band gather (gather_freqs_fold_complex with the stereo merge folded in):
 // spec [B][C][F][T] complex -> x[b][t][2j + r] = spec[b][fi_j % C][fi_j / C][t][r].
-// One CTA per (b, 4-frame tile): the tile's frames of every bin pass through
-// shared memory so each strided spectrum read is a full 32-byte sector.
-constexpr int kGT = 4;  // frames per gather CTA
+// One CTA per (frequency-range tile, 32 frames, b): the tile's spectrum rows
+// come in as 256-byte runs of frames, and the tile's band-freq entries go out
+// as runs of consecutive j per frame, so both sides are coalesced and every
+// element moves once.  Each lane owns entries lane + 32 i of the tile (their
+// j and tile row held in registers) and each warp writes whole frames, so the
+// output loop is a shared-memory read and a store per element.  The tile's
+// tables sit at fixed per-tile offsets, so every global load of the prologue
+// is independent of the others.
+constexpr int kTT = 32;      // frames per band-op CTA
+constexpr int kBandEnt = 4;  // tile entries held per lane per pass (128 per warp)
+constexpr int kBandWarps = 8;
+constexpr int kBandRows = 2 * kBandTileBins / kBandWarps;  // tile rows per warp
+constexpr int kBandFrames = kTT / kBandWarps;              // frames per warp
 
 template <typename T>
-__global__ void __launch_bounds__(256) gather_kernel(const float2* __restrict__ spec, int C, int F, int Tn,
-                                                     const int* __restrict__ fi, int64_t J, T* __restrict__ x) {
-    extern __shared__ float2 tile[];  // [C*F][kGT]
-    const int b = blockIdx.y, t0 = blockIdx.x * kGT;
-    const int nt = min(kGT, Tn - t0);
-    const int FC = F * C;
-    for (int i = threadIdx.x; i < FC * kGT; i += blockDim.x) {
-        const int row = i / kGT, tt = i % kGT;  // row = c * F + f
-        tile[i] = tt < nt ? spec[(((int64_t)b * FC + row) * Tn) + t0 + tt] : make_float2(0.f, 0.f);
+__global__ void __launch_bounds__(kBandWarps * 32) gather_tiled_kernel(
+    const float2* __restrict__ spec, int C, int F, int Tn, const int* __restrict__ jl, const int* __restrict__ jr,
+    int stride, int64_t J, T* __restrict__ x) {
+    __shared__ __align__(16) float2 tile[2 * kBandTileBins][kTT + 1];  // [c * nf + f - f0][tt], C <= 2
+    const int f0 = blockIdx.x * kBandTileBins, nf = min(kBandTileBins, F - f0);
+    const int b = blockIdx.z, t0 = blockIdx.y * kTT, nt = min(kTT, Tn - t0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int* jlt = jl + (int64_t)blockIdx.x * stride;
+    const int* jrt = jr + (int64_t)blockIdx.x * stride;
+    const float2* sp = spec + ((int64_t)b * C * F + f0) * Tn + t0 + lane;  // row (c, f0) of this lane's frame
+#pragma unroll
+    for (int i = 0; i < kBandRows; ++i) {
+        const int row = warp + kBandWarps * i, c = row >= nf;  // C <= 2
+        if (row < C * nf && lane < nt) cp_async<8>(&tile[row][lane], sp + (c * (F - nf) + row) * Tn);
     }
-    __syncthreads();
-    for (int tt = 0; tt < nt; ++tt) {
-        T* dst = x + ((int64_t)b * Tn + t0 + tt) * 2 * J;
-        for (int64_t j = threadIdx.x; j < J; j += blockDim.x) {
-            const int fs = fi[j];
-            const float2 v = tile[((fs % C) * F + fs / C) * kGT + tt];
-            dst[2 * j] = from_f32<T>(v.x);
-            dst[2 * j + 1] = from_f32<T>(v.y);
+    const float2* tflat = &tile[0][0];
+    for (int base = 0; base < stride; base += 32 * kBandEnt) {
+        int jj[kBandEnt], rr[kBandEnt];
+#pragma unroll
+        for (int i = 0; i < kBandEnt; ++i) {
+            const int k = base + lane + 32 * i;
+            jj[i] = k < stride ? jlt[k] : -1;
+            rr[i] = k < stride ? jrt[k] * (kTT + 1) : 0;  // flat offset of the entry's tile row
+        }
+        if (base == 0) {
+            cp_async_wait_all();
+            __syncthreads();
+        }
+#pragma unroll
+        for (int u = 0; u < kBandFrames; ++u) {
+            const int tt = warp + kBandWarps * u;
+            if (tt >= nt) break;
+            T* dst = x + ((int64_t)b * Tn + t0 + tt) * 2 * J;
+#pragma unroll
+            for (int i = 0; i < kBandEnt; ++i)
+                if (jj[i] >= 0) store_pair(dst + 2 * jj[i], tflat[rr[i] + tt]);
         }
     }
 }
 
-// Mask scatter-average (apply_mask_and_scatter, gather form over the reverse
-// band map): out[b][s][c][f][t] = sum_{j: fi_j = f*C+c} spec[b][c][f][t] * mask[s][b*T+t][j] / nbpf[f*C+c].
+// Mask scatter-average (apply_mask_and_scatter, gather form):
+// out[b][s][c][f][t] = sum_{j: fi_j = f*C+c} spec[b][c][f][t] * mask[s][b*T+t][j] / nbpf[f*C+c]
+// (each term divided, as the reference does before its atomic add).
+// One CTA per (frequency-range tile, 32 frames, b, s).  Everything the CTA
+// reads is copied into shared memory with asynchronous copies issued up front
+// (the tile's spectrum rows, bin weights and entry tables, then the masks of
+// the tile's entries as runs of consecutive j per frame), so a CTA waits for
+// memory about twice; then each warp produces its (channel, bin) rows of the
+// tile as 32-frame runs.
 template <typename T>
-__global__ void scatter_kernel(const float2* __restrict__ spec, const T* __restrict__ masks, int B, int S, int C,
-                               int F, int Tn, const int* __restrict__ rev_off, const int* __restrict__ rev_idx,
-                               const float* __restrict__ nbpf, int64_t J, float2* __restrict__ out) {
-    const int64_t total = (int64_t)B * S * C * F * Tn;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i % Tn);
-        int64_t r = i / Tn;
-        const int f = (int)(r % F);
-        r /= F;
-        const int c = (int)(r % C);
-        r /= C;
-        const int s = (int)(r % S);
-        const int b = (int)(r / S);
-        const int fs = f * C + c;
-        const float2 x = spec[(((int64_t)b * C + c) * F + f) * Tn + t];
-        const float den = fmaxf(nbpf[fs], 1e-8f);
-        const T* mk = masks + ((int64_t)s * B * Tn + (int64_t)b * Tn + t) * 2 * J;
-        float2 acc = make_float2(0.f, 0.f);
-        for (int q = rev_off[fs]; q < rev_off[fs + 1]; ++q) {
-            const int j = rev_idx[q];
-            const float mr = to_f32(mk[2 * j]), mi = to_f32(mk[2 * j + 1]);
-            acc.x += (x.x * mr - x.y * mi) / den;
-            acc.y += (x.x * mi + x.y * mr) / den;
+__global__ void __launch_bounds__(kBandWarps * 32) scatter_tiled_kernel(
+    const float2* __restrict__ spec, const T* __restrict__ masks, int B, int S, int C, int F, int Tn,
+    const int* __restrict__ jl, const int* __restrict__ bk, const int* __restrict__ bo, int stride,
+    const float* __restrict__ nbpf, int64_t J, float2* __restrict__ out) {
+    using P = typename PairOf<T>::type;
+    extern __shared__ __align__(16) uint8_t band_smem[];
+    // [2 * kBandTileBins][kTT + 1] spectrum tile, [kTT][stride + 1] masks (odd pitch: conflict-free
+    // frame-strided reads), row offsets, grouped entries, per-row bin weights
+    auto xs = reinterpret_cast<float2 (*)[kTT + 1]>(band_smem);
+    P* mk = reinterpret_cast<P*>(band_smem + sizeof(float2) * 2 * kBandTileBins * (kTT + 1));
+    const int ld = stride + 1;
+    int* bos = reinterpret_cast<int*>(mk + kTT * ld);  // [kBandRowOffs]
+    int* bks = bos + kBandRowOffs;                     // [stride]
+    float* nbs = reinterpret_cast<float*>(bks + stride);  // [2 * kBandTileBins]
+    const int f0 = blockIdx.x * kBandTileBins, nf = min(kBandTileBins, F - f0);
+    const int t0 = blockIdx.y * kTT, nt = min(kTT, Tn - t0);
+    const int b = blockIdx.z % B, s = blockIdx.z / B;
+    const int rows = C * nf;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float2* sp = spec + ((int64_t)b * C * F + f0) * Tn + t0 + lane;  // row (c, f0) of this lane's frame
+#pragma unroll
+    for (int i = 0; i < kBandRows; ++i) {
+        const int row = warp + kBandWarps * i, c = row >= nf;  // C <= 2
+        if (row < rows && lane < nt) cp_async<8>(&xs[row][lane], sp + (c * (F - nf) + row) * Tn);
+    }
+    for (int k = threadIdx.x; k < kBandRowOffs; k += blockDim.x)
+        cp_async<4>(&bos[k], &bo[(int64_t)blockIdx.x * kBandRowOffs + k]);
+    for (int k = threadIdx.x; k < stride; k += blockDim.x) cp_async<4>(&bks[k], &bk[(int64_t)blockIdx.x * stride + k]);
+    for (int k = threadIdx.x; k < rows; k += blockDim.x) {
+        const int c = k >= nf;
+        cp_async<4>(&nbs[k], &nbpf[(f0 + k - c * nf) * C + c]);
+    }
+    const int* jlt = jl + (int64_t)blockIdx.x * stride;
+    const T* mrow = masks + ((int64_t)s * B * Tn + (int64_t)b * Tn + t0) * 2 * J;
+    const int jstride = (int)(2 * J);
+    for (int base = 0; base < stride; base += 32 * kBandEnt) {
+        int jj[kBandEnt];
+#pragma unroll
+        for (int i = 0; i < kBandEnt; ++i) {
+            const int k = base + lane + 32 * i;
+            jj[i] = k < stride ? jlt[k] : -1;
         }
-        out[i] = acc;
+#pragma unroll
+        for (int u = 0; u < kBandFrames; ++u) {
+            const int tt = warp + kBandWarps * u;
+            if (tt >= nt) break;
+#pragma unroll
+            for (int i = 0; i < kBandEnt; ++i)
+                if (jj[i] >= 0)
+                    cp_async<sizeof(P)>(&mk[tt * ld + base + lane + 32 * i], mrow + tt * jstride + 2 * jj[i]);
+        }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (lane >= nt) return;
+    float2* op = out + (((int64_t)b * S + s) * C * F + f0) * Tn + t0 + lane;
+    const P* mkl = mk + lane * ld;
+#pragma unroll
+    for (int i = 0; i < kBandRows; ++i) {
+        const int row = warp + kBandWarps * i, c = row >= nf;
+        if (row >= rows) break;
+        const float2 xv = xs[row][lane];
+        const float den = fmaxf(nbs[row], 1e-8f);
+        float2 acc = make_float2(0.f, 0.f);
+        const int q0 = bos[row], q1 = bos[row + 1];
+        if ((__float_as_uint(den) & 0x7fffffu) == 0u) {
+            // power-of-two weight: the product with its exact reciprocal is the correctly rounded quotient
+            const float inv = 1.f / den;
+            for (int q = q0; q < q1; ++q) {
+                const float2 mm = pair_to_f32<T>(mkl[bks[q]]);
+                acc.x += (xv.x * mm.x - xv.y * mm.y) * inv;
+                acc.y += (xv.x * mm.y + xv.y * mm.x) * inv;
+            }
+        } else {
+            for (int q = q0; q < q1; ++q) {
+                const float2 mm = pair_to_f32<T>(mkl[bks[q]]);
+                acc.x += (xv.x * mm.x - xv.y * mm.y) / den;
+                acc.y += (xv.x * mm.y + xv.y * mm.x) / den;
+            }
+        }
+        op[(c * (F - nf) + row) * Tn] = acc;
     }
 }
 
@@ -484,6 +587,7 @@ void gelu(const void* a, void* y, int64_t n, int dtype, cudaStream_t st) {
 
 void sigmoid_gate(const void* x, const void* g, void* y, int64_t rows, int H, int dh, int dtype, cudaStream_t st) {
     MBR_CHECK(dh % 8 == 0, "gate: head dim must be a multiple of 8");
+    MBR_CHECK(rows * H * dh / 8 < (1ll << 32), "gate: tensor too large");
     MBR_DISPATCH_DTYPE(dtype, T, {
         gate_kernel<T><<<grid_for(rows * H * dh / 8, 256), 256, 0, st>>>((const T*)x, (const T*)g, (T*)y, rows, H,
                                                                          dh);
@@ -494,7 +598,8 @@ void sigmoid_gate(const void* x, const void* g, void* y, int64_t rows, int H, in
 void rms_norm(const void* x, const float* gamma, void* y, int64_t rows, int D, float scale, int dtype,
               cudaStream_t st) {
     MBR_CHECK(D % 8 == 0 && D <= 1024, "rms_norm: dim must be a multiple of 8 and <= 1024");
-    unsigned grid = (unsigned)std::min<int64_t>(ceil_div(rows, 8), (int64_t)sm_count() * 8);
+    MBR_CHECK(((uintptr_t)gamma & 15) == 0, "rms_norm: gamma must be 16-byte aligned");
+    unsigned grid = (unsigned)std::min<int64_t>(ceil_div(rows, 16), (int64_t)sm_count() * 8);
     MBR_DISPATCH_DTYPE(dtype, T, {
         if (D <= 256) rms_kernel<T, 1><<<grid, 256, 0, st>>>((const T*)x, gamma, (T*)y, rows, D, scale);
         else if (D <= 512) rms_kernel<T, 2><<<grid, 256, 0, st>>>((const T*)x, gamma, (T*)y, rows, D, scale);
@@ -505,30 +610,80 @@ void rms_norm(const void* x, const float* gamma, void* y, int64_t rows, int D, f
 
 void rope(const void* x, const float* cs, const float* sn, void* y, int64_t seqs, int L, int H, int dtype,
           cudaStream_t st) {
+    MBR_CHECK(seqs * L * H * 8 < (1ll << 32), "rope: tensor too large");
+    MBR_CHECK(((uintptr_t)cs & 15) == 0 && ((uintptr_t)sn & 15) == 0, "rope: tables must be 16-byte aligned");
     MBR_DISPATCH_DTYPE(dtype, T, {
         rope_kernel<T><<<grid_for(seqs * L * H * 8, 256), 256, 0, st>>>((const T*)x, cs, sn, (T*)y, seqs, L, H);
     });
     MBR_CUDA(cudaGetLastError());
 }
 
-void band_gather(const float2* spec, int B, int C, int F, int T, const int* fi, int64_t J, void* x, int dtype,
-                 cudaStream_t st) {
-    size_t sm = sizeof(float2) * (size_t)C * F * kGT;
-    dim3 grid((unsigned)ceil_div(T, kGT), (unsigned)B);
+BandTilesHost make_band_tiles(const std::vector<int>& fi, int C, int F) {
+    BandTilesHost h;
+    std::vector<std::vector<int>> ent;  // per tile: its j, ascending
+    for (int f0 = 0; f0 < F; f0 += kBandTileBins) {
+        std::vector<int> e;
+        for (int j = 0; j < (int)fi.size(); ++j)
+            if (fi[j] / C >= f0 && fi[j] / C < f0 + kBandTileBins) e.push_back(j);
+        h.max_n = std::max(h.max_n, (int)e.size());
+        ent.push_back(std::move(e));
+    }
+    h.stride = std::max(32, (h.max_n + 31) / 32 * 32);
+    for (size_t t = 0; t < ent.size(); ++t) {
+        const int f0 = (int)t * kBandTileBins, nf = std::min(kBandTileBins, F - f0), n = (int)ent[t].size();
+        h.tiles.push_back(make_int4(f0, nf, 0, n));
+        std::vector<int> row(n);
+        for (int k = 0; k < n; ++k) row[k] = (fi[ent[t][k]] % C) * nf + fi[ent[t][k]] / C - f0;
+        for (int k = 0; k < h.stride; ++k) {
+            h.jl.push_back(k < n ? ent[t][k] : -1);
+            h.jr.push_back(k < n ? row[k] : 0);
+        }
+        // entries grouped by row (counting sort), with the rows' start offsets
+        std::vector<int> cnt(kBandRowOffs, 0);
+        for (int k = 0; k < n; ++k) ++cnt[row[k] + 1];
+        for (int r = 1; r < kBandRowOffs; ++r) cnt[r] += cnt[r - 1];
+        h.bo.insert(h.bo.end(), cnt.begin(), cnt.end());
+        std::vector<int> bk(h.stride, 0), cur(cnt.begin(), cnt.end() - 1);
+        for (int k = 0; k < n; ++k) bk[cur[row[k]]++] = k;
+        h.bk.insert(h.bk.end(), bk.begin(), bk.end());
+    }
+    return h;
+}
+
+void band_gather(const float2* spec, int B, int C, int F, int T, const int* fi, int64_t J, const BandTiles& bt,
+                 void* x, int dtype, cudaStream_t st) {
+    (void)fi;  // the tile tables carry the band map
+    MBR_CHECK(C >= 1 && C <= 2 && bt.count == ceil_div(F, kBandTileBins) && bt.stride % 32 == 0,
+              "band gather: one or two channels and a tile map of the spectrum");
+    MBR_CHECK(((uintptr_t)spec & 7) == 0 && ((uintptr_t)x & 3) == 0, "band gather: misaligned buffers");
+    MBR_CHECK((int64_t)C * F * T < (1ll << 31), "band gather: one batch entry of the spectrum exceeds 32-bit offsets");
+    dim3 grid((unsigned)bt.count, (unsigned)ceil_div(T, kTT), (unsigned)B);
     MBR_DISPATCH_DTYPE(dtype, E, {
-        if (sm > 48 * 1024)
-            MBR_CUDA(cudaFuncSetAttribute(gather_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        gather_kernel<E><<<grid, 256, sm, st>>>(spec, C, F, T, fi, J, (E*)x);
+        gather_tiled_kernel<E><<<grid, kBandWarps * 32, 0, st>>>(spec, C, F, T, bt.jl, bt.jr, bt.stride, J, (E*)x);
     });
     MBR_CUDA(cudaGetLastError());
 }
 
-void mask_scatter(const float2* spec, const void* masks, int B, int S, int C, int F, int T, const int* rev_off,
-                  const int* rev_idx, const float* nbpf, int64_t J, float2* out, int dtype, cudaStream_t st) {
-    const int64_t total = (int64_t)B * S * C * F * T;
+void mask_scatter(const float2* spec, const void* masks, int B, int S, int C, int F, int T, const float* nbpf,
+                  int64_t J, const BandTiles& bt, float2* out, int dtype, cudaStream_t st) {
+    MBR_CHECK(C >= 1 && C <= 2 && bt.count == ceil_div(F, kBandTileBins) && bt.stride % 32 == 0,
+              "mask scatter: one or two channels and a tile map of the spectrum");
+    MBR_CHECK(((uintptr_t)spec & 7) == 0 && ((uintptr_t)out & 7) == 0 &&
+                  ((uintptr_t)masks & (dtype == DT_F32 ? 7 : 3)) == 0,
+              "mask scatter: misaligned buffers");
+    MBR_CHECK((int64_t)C * F * T < (1ll << 31) && 2 * J * (int64_t)kTT < (1ll << 31),
+              "mask scatter: one batch entry of the spectrum or a frame block of masks exceeds 32-bit offsets");
+    dim3 grid((unsigned)bt.count, (unsigned)ceil_div(T, kTT), (unsigned)(B * S));
     MBR_DISPATCH_DTYPE(dtype, E, {
-        scatter_kernel<E><<<grid_for(total, 256), 256, 0, st>>>(spec, (const E*)masks, B, S, C, F, T, rev_off,
-                                                                 rev_idx, nbpf, J, out);
+        const size_t sm = sizeof(float2) * 2 * kBandTileBins * (kTT + 1) +
+                          sizeof(typename PairOf<E>::type) * kTT * (size_t)(bt.stride + 1) +
+                          sizeof(int) * (size_t)(kBandRowOffs + bt.stride) + sizeof(float) * 2 * kBandTileBins;
+        MBR_CHECK(sm <= 200 * 1024, "mask scatter: band tile too wide");
+        if (sm > 48 * 1024)
+            MBR_CUDA(cudaFuncSetAttribute(scatter_tiled_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)sm));
+        scatter_tiled_kernel<E><<<grid, kBandWarps * 32, sm, st>>>(spec, (const E*)masks, B, S, C, F, T, bt.jl,
+                                                                    bt.bk, bt.bo, bt.stride, nbpf, J, out);
     });
     MBR_CUDA(cudaGetLastError());
 }

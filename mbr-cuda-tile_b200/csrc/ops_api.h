@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 namespace mbr {
 namespace opsapi {
 
@@ -20,12 +22,36 @@ void rms_norm(const void* x, const float* gamma, void* y, int64_t rows, int D, f
 // x [seqs][L][H][64] rotated by cos/sin [L][32] (interleaved pairs)
 void rope(const void* x, const float* cs, const float* sn, void* y, int64_t seqs, int L, int H, int dtype,
           cudaStream_t st);
+// Frequency-range tiles of a band map for the transposing band ops: tile i
+// covers bins [f0, f0 + nf) (kBandTileBins at most) of all channels and the
+// band-freq entries j whose bin lies there (jl[off .. off + n), ascending);
+// bin_off / bin_k list, for each (channel, bin) row of the tile, the tile-local
+// positions of its entries.
+constexpr int kBandTileBins = 32;
+constexpr int kBandRowOffs = 2 * kBandTileBins + 1;  // row offsets per tile (two channels)
+struct BandTiles {
+    const int4* tiles = nullptr;  // {f0, nf, unused, n}
+    // per tile, padded to `stride` entries (pads: j = -1, row 0, k 0)
+    const int* jl = nullptr;  // band-freq indices j of the tile's entries, ascending
+    const int* jr = nullptr;  // tile row of each entry (channel * nf + bin - f0)
+    const int* bk = nullptr;  // entries grouped by tile row: tile-local entry positions
+    const int* bo = nullptr;  // [kBandRowOffs] per tile: start of each row's group in bk (last = n)
+    int count = 0, max_n = 0, stride = 0;
+};
+// Host construction from the band map (fi: bin*C + channel per entry j).
+struct BandTilesHost {
+    std::vector<int4> tiles;
+    std::vector<int> jl, jr, bk, bo;
+    int max_n = 0, stride = 0;
+};
+BandTilesHost make_band_tiles(const std::vector<int>& fi, int C, int F);
+
 // spec [B][C][F][T] complex -> x [B][T][2J]
-void band_gather(const float2* spec, int B, int C, int F, int T, const int* fi, int64_t J, void* x, int dtype,
-                 cudaStream_t st);
+void band_gather(const float2* spec, int B, int C, int F, int T, const int* fi, int64_t J, const BandTiles& bt,
+                 void* x, int dtype, cudaStream_t st);
 // masks [S][B*T][2J] (dtype), spec [B][C][F][T] complex -> out [B][S][C][F][T] complex
-void mask_scatter(const float2* spec, const void* masks, int B, int S, int C, int F, int T, const int* rev_off,
-                  const int* rev_idx, const float* nbpf, int64_t J, float2* out, int dtype, cudaStream_t st);
+void mask_scatter(const float2* spec, const void* masks, int B, int S, int C, int F, int T, const float* nbpf,
+                  int64_t J, const BandTiles& bt, float2* out, int dtype, cudaStream_t st);
 // q, k, v [B][H][N][D] -> out [B][N][H*D] = softmax(q k^T * scale) v, times
 // gates [B][N][H] when non-null (scaled_dot_product_attention followed by
 // apply_gates_and_merge_heads).  16-bit dtypes with D = 64 run the tcgen05
