@@ -446,7 +446,8 @@ def run_op_sweep(args):
     """Tensor-op sweep: activations [B*801*60, D] seeded
     N(0, 1), D in {192, 384, 512}, B in {1, 4, 8}, fp32 / fp16 / bf16.  Each op
     is timed with CUDA events around one launch after an L2 flush (a 256 MiB
-    write), averaged over `--steps` launches after `--warmup`; GB/s counts the
+    write followed by a 256 MiB read, so the launch meets a cold L2 and none of
+    the flush's dirty lines), averaged over `--steps` launches after `--warmup`; GB/s counts the
     algorithmic bytes (every input read once, every output written once)."""
     import torch
 
@@ -456,7 +457,11 @@ def run_op_sweep(args):
     torch.cuda.set_device(0)
     peak = load_peaks()["hbm_gbs"]
     T, NB, J2 = 801, 60, 2 * 3958  # frames, bands, band-freq values (7916) of the 60-band split
+    # L2 flush between launches: write a 256 MiB buffer, then read another one, so that the timed launch
+    # starts with a cold L2 holding clean lines (the flush's own dirty lines are written back before it)
     flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    flush_rd = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    flush_sum = torch.empty((), dtype=torch.float32, device="cuda")
     gen = torch.Generator(device="cuda").manual_seed(0)
     tdt = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
     reps, warm = max(args.steps, 3), max(args.warmup, 1)
@@ -468,6 +473,7 @@ def run_op_sweep(args):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         for _ in range(reps):
             flush.zero_()
+            torch.sum(flush_rd, 0, out=flush_sum)
             e0.record()
             fn()
             e1.record()

@@ -39,14 +39,22 @@ constexpr int kStagingPerWarp = 32 * kStageRowBytes;   // 32 rows x 128 B
 // CG = 1: one CTA computes a 128 x BN tile.  CG = 2: a CTA pair (cluster of
 // two) computes 256 x BN with cta_group::2 MMAs; each CTA holds its 128 A rows
 // and half of the B rows, so a stage is 16 KB + BN*64 bytes per CTA.
+// Each epilogue warp owns NSTG staging tiles, so a TMA store can still be
+// reading one while the warp fills the other; the operand ring gets what is
+// left of the 227 KB (at most 8 stages).  The 128 x 256 single-CTA tile keeps
+// one staging tile to keep 4 operand stages.
 template <int BN, int CG = 1>
 struct TileCfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = (BN / CG) * BK * 2;
-    static constexpr int STAGES = CG == 2 ? (BN == 128 ? 8 : 6) : (BN == 128 ? 6 : 4);
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int NSTG = (CG == 1 && BN == 256) ? 1 : 2;
+    static constexpr int kSmemMax = 232448 - 256 - 1024;  // opt-in maximum less barriers and alignment slack
+    static constexpr int STAGES_FIT = (kSmemMax - NSTG * kEpiWarps * kStagingPerWarp) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT < 8 ? STAGES_FIT : 8;
+    static_assert(STAGES >= 3, "operand ring too shallow");
     static constexpr int STAGING_OFF = STAGES * STAGE_BYTES;  // 1024-aligned
-    static constexpr int BAR_OFF = STAGING_OFF + kEpiWarps * kStagingPerWarp;
+    static constexpr int BAR_OFF = STAGING_OFF + NSTG * kEpiWarps * kStagingPerWarp;
     static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
     static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
@@ -305,9 +313,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             prefetch_tensormap(&tmB);
             uint32_t it = 0;
             bool alive = true;
+            int4 tl = make_int4(0, 0, 0, 0), ta = tl;
+            if (cta_tile0 < ntiles) tl = tiles[2 * cta_tile0], ta = tiles[2 * cta_tile0 + 1];
             for (int t = cta_tile0; t < ntiles && alive; t += cta_tile_step) {
-                const int4 tl = tiles[t];
-                const ops::GemmGroup& g = groups[tl.x];
+                // the next tile's descriptor is in flight while this tile's loads are issued
+                int4 tl_n = make_int4(0, 0, 0, 0), ta_n = tl_n;
+                if (t + cta_tile_step < ntiles)
+                    tl_n = tiles[2 * (t + cta_tile_step)], ta_n = tiles[2 * (t + cta_tile_step) + 1];
                 for (int kb = 0; kb < tl.w; ++kb, ++it) {
                     const int s = it % Cfg::STAGES;
                     const uint32_t r = it / Cfg::STAGES;
@@ -315,19 +327,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         alive = false;
                         break;
                     }
-                    const int kx = g.k_col0 + kb * BK;
+                    const int kx = ta.z + kb * BK;
                     if constexpr (CG == 2) {
                         // both CTAs' bytes complete on the leader's full barrier
                         const uint32_t fb = map_to_cta(smem_u32(&full[s]), 0);
                         if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
-                        tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, kx, g.a_row0 + tl.y + (int)rank * BM, fb);
-                        tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, kx, g.b_row0 + tl.z + (int)rank * (BN / 2), fb);
+                        tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, kx, ta.x + (int)rank * BM, fb);
+                        tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, kx, ta.y + (int)rank * (BN / 2), fb);
                     } else {
                         mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-                        tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kx, g.a_row0 + tl.y, &full[s]);
-                        tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kx, g.b_row0 + tl.z, &full[s]);
+                        tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kx, ta.x, &full[s]);
+                        tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kx, ta.y, &full[s]);
                     }
                 }
+                tl = tl_n;
+                ta = ta_n;
             }
         }
     } else if (warp == 1) {
@@ -336,15 +350,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t it = 0;
             int tcount = 0;
             bool alive = true;
+            int nkb = 0, klast = 0;  // k-blocks of the tile, k-steps of its last k-block
+            if (cta_tile0 < ntiles) nkb = tiles[2 * cta_tile0].w, klast = tiles[2 * cta_tile0 + 1].w;
             for (int t = cta_tile0; t < ntiles && alive; t += cta_tile_step, ++tcount) {
-                const int4 tl = tiles[t];
-                const int K = groups[tl.x].K;
+                int nkb_n = 0, klast_n = 0;  // the next tile's, in flight during this one
+                if (t + cta_tile_step < ntiles)
+                    nkb_n = tiles[2 * (t + cta_tile_step)].w, klast_n = tiles[2 * (t + cta_tile_step) + 1].w;
                 const int buf = tcount & 1;
                 const uint32_t use = tcount >> 1;
                 if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + buf * BN;
-                for (int kb = 0; kb < tl.w; ++kb, ++it) {
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % Cfg::STAGES;
                     const uint32_t r = it / Cfg::STAGES;
                     if (!mbar_wait(&full[s], r & 1, err)) {
@@ -354,7 +371,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
                     const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
-                    const int ksteps = min(BK / 16, (K - kb * BK) / 16);
+                    const int ksteps = kb + 1 == nkb ? klast : BK / 16;
                     if constexpr (CG == 2) {
                         for (int k = 0; k < ksteps; ++k)
                             mma_f16_pair(d, sdesc_sw128(a0 + 32 * k), sdesc_sw128(b0 + 32 * k), idesc,
@@ -369,6 +386,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (!alive) break;
                 if constexpr (CG == 2) mma_commit_pair(&acc_full[buf]);
                 else mma_commit(&acc_full[buf]);
+                nkb = nkb_n;
+                klast = klast_n;
             }
         }
     } else {
@@ -376,12 +395,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int half = (warp - 2) >> 2;
         constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp
         int tcount = 0;
+        uint32_t boxes = 0;  // staged boxes this warp has issued (selects its staging tile)
         // this CTA's 128 rows of the tile
         const uint32_t acc_empty_leader = CG == 2 ? map_to_cta(smem_u32(&acc_empty[0]), 0) : 0;
+        int4 tl_c = make_int4(0, 0, 0, 0);
+        ops::GemmGroup g = {};
+        if (cta_tile0 < ntiles) {
+            tl_c = tiles[2 * cta_tile0];
+            g = groups[tl_c.x];
+        }
         for (int t = cta_tile0; t < ntiles; t += cta_tile_step, ++tcount) {
-            int4 tl = tiles[t];
+            int4 tl = tl_c;
             tl.y += (int)rank * BM;
-            const ops::GemmGroup g = groups[tl.x];
+            if (t + cta_tile_step < ntiles) tl_c = tiles[2 * (t + cta_tile_step)];  // the next tile's, in flight
             const int buf = tcount & 1;
             const uint32_t use = tcount >> 1;
             if (!mbar_wait(&acc_full[buf], use & 1, err)) break;
@@ -393,26 +419,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                            EPI == ops::EPI_GELU_T || EPI == ops::EPI_TANH_T ||
                                            EPI == ops::EPI_ROPE_T;
             if (kStoresViaTma && c_tma) {
-                // stage through this warp's 32-row tile; one TMA store (or
-                // reduce-add into the fp32 residual) per 128-byte row group
+                // stage through this warp's 32-row tiles (NSTG of them, used in
+                // turn); one TMA store (or reduce-add into the fp32 residual)
+                // per 128-byte row group.  The TMEM load of the next 32 columns
+                // is in flight while the current ones are processed.
                 constexpr bool k16 = !(EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32);
-                uint8_t* stg = smem + Cfg::STAGING_OFF + (warp - 2) * kStagingPerWarp;
+                uint8_t* stg_base = smem + Cfg::STAGING_OFF + (warp - 2) * Cfg::NSTG * kStagingPerWarp;
                 const int yrow = tl.y + q * 32;
+                const int ncol = g.N - (tl.z + half * (BN / 2));
+                const int nch = ncol <= 0 ? 0 : (ncol >= 32 * kChunks ? kChunks : (ncol + 31) / 32);
+                uint32_t r[32];
+                if (nch > 0) tmem_ld32(taddr, r);
 #pragma unroll 1
-                for (int c = 0; c < kChunks; ++c) {
+                for (int c = 0; c < nch; ++c) {
                     const int n0 = tl.z + half * (BN / 2) + c * 32;
-                    if (n0 >= g.N) break;
-                    uint32_t r[32];
-                    tmem_ld32(taddr + c * 32, r);
-                    tmem_ld_wait();
+                    tmem_ld_wait(r);
                     float v[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                    if (c + 1 < nch) tmem_ld32(taddr + (c + 1) * 32, r);
                     apply_epi<EPI>(g, n0, v);
                     if constexpr (EPI == ops::EPI_ROPE_T) rope_rotate(qkv, tl.y + q * 32 + lane, n0, v);
                     const int h16 = k16 ? (c & 1) : 0;
-                    if (h16 == 0) {  // the staging tile is free once the previous store has read it
-                        if (lane == 0) bulk_wait_read_all();
+                    uint8_t* stg = stg_base + (Cfg::NSTG == 2 ? (boxes & 1) : 0) * kStagingPerWarp;
+                    if (h16 == 0) {  // a staging tile is free once the store issued from it has read it
+                        if (lane == 0) {
+                            if constexpr (Cfg::NSTG == 2) bulk_wait_read_1();
+                            else bulk_wait_read_all();
+                        }
                         __syncwarp();
                     }
                     stage_chunk<T, EPI>(stg, lane, h16, v);
@@ -428,6 +462,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             else tma_store_3d(&tmC, stg, x, y, z);
                             bulk_commit();
                         }
+                        if (yrow < g.M) ++boxes;  // a skipped box leaves its staging tile free for the next one
                     }
                 }
             } else {
@@ -467,6 +502,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if constexpr (CG == 2) mbar_arrive_cluster(acc_empty_leader + 8u * buf);  // the leader's barrier
                 else mbar_arrive(&acc_empty[buf]);
             }
+            if (t + cta_tile_step < ntiles) g = groups[tl_c.x];  // loads in flight until the next tile's wait
         }
         if (lane == 0) bulk_wait_all();  // outstanding TMA stores complete before exit
     }
@@ -643,14 +679,11 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
                       bn % 64 == 0,
                   "tc gemm: QKV epilogue needs head dim 64 and its q/k/v/rope buffers");
     make_map(&L.tmA, p.a_base, p.a_rows, p.a_cols, BM, dtype);
-    // CTA pairs for the large residual GEMMs with a long K loop (FFN2): the
-    // pair halves each SM's B traffic there.  Where the epilogue is heavy
-    // relative to K (QKV + RoPE, FFN1 + GELU, K = 384) the coupling of the two
-    // CTAs' epilogues costs more than it saves, measured on B200.
-    int maxK = 0;
-    for (int gi = 0; gi < p.ngroups; ++gi) maxK = std::max(maxK, p.h_groups[gi].K);
-    L.cg = p.c_dtype >= 0 && p.epi == ops::EPI_ADD_F32 && p.maxM >= 4096 && maxK >= 1024 && !pair_tiles_off() ? 2
-                                                                                                              : 1;
+    // CTA pairs (256-row tiles, cta_group::2) for the large residual GEMMs
+    // (out-projection, FFN2): each CTA loads half of the B tile.  For the
+    // 16-bit-output GEMMs with K = 384 (QKV, FFN1) the pair's coupled
+    // epilogues cost more than the halved B traffic saves, measured on B200.
+    L.cg = p.c_dtype >= 0 && p.epi == ops::EPI_ADD_F32 && p.maxM >= 4096 && !pair_tiles_off() ? 2 : 1;
     make_map(&L.tmB, p.b_base, p.b_rows, p.b_cols, bn / L.cg, dtype);
     L_first = tiles.size();
     for (int gi = 0; gi < p.ngroups; ++gi) {
@@ -660,11 +693,17 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
                       (int64_t)g.k_col0 + g.K <= p.a_cols && (int64_t)g.k_col0 + g.K <= p.b_cols,
                   "tc gemm: group outside its operand tensors");
         MBR_CHECK(g.k_col0 % 8 == 0, "tc gemm: K offset must be 16-byte aligned");
-        int kb = (int)ceil_div(g.K, BK);
+        const int kb = (int)ceil_div(g.K, BK);
+        const int klast = (g.K - (kb - 1) * BK) / 16;  // k-steps of the last k-block
+        // two int4 per tile: {group, m0, n0, k-blocks} and the operand coordinates
+        // {A row, B row, first K column, k-steps of the last k-block}
         for (int m0 = 0; m0 < g.M; m0 += BM * L.cg)
-            for (int n0 = 0; n0 < g.N; n0 += bn) tiles.push_back(make_int4(gi, m0, n0, kb));
+            for (int n0 = 0; n0 < g.N; n0 += bn) {
+                tiles.push_back(make_int4(gi, m0, n0, kb));
+                tiles.push_back(make_int4(g.a_row0 + m0, g.b_row0 + n0, g.k_col0, klast));
+            }
     }
-    L.ntiles = (int)(tiles.size() - L_first);
+    L.ntiles = (int)((tiles.size() - L_first) / 2);
     L.groups = p.groups;
     L.c_tma = 0;
     const bool staged_epi = p.epi == ops::EPI_F32 || p.epi == ops::EPI_ADD_F32 || p.epi == ops::EPI_T ||

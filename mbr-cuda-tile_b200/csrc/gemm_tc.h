@@ -55,7 +55,7 @@ struct EpiQKV {
 struct GemmLaunch {
     CUtensorMap tmA, tmB, tmC;
     int c_tma = 0;  // epilogue writes C through tmC
-    const int4* tiles = nullptr;  // device: (group, m0, n0, k-blocks)
+    const int4* tiles = nullptr;  // device, two int4 per tile: (group, m0, n0, k-blocks), (A row, B row, K column, last k-steps)
     int ntiles = 0;
     int bn = 128;
     int cg = 1;  // 2: CTA pairs (cluster of two, cta_group::2 MMAs on 256-row tiles)

@@ -34,20 +34,39 @@ int sm_count() {
     return n;
 }
 
+// 8 elements of T in their storage form: one 16-byte word (16-bit T) or two
+// (fp32), so a load in flight holds 4 or 8 registers until it is unpacked.
+template <typename T>
+struct Raw8 {
+    static constexpr int N = sizeof(T) / 2;
+    uint4 w[N];
+    __device__ __forceinline__ void load(const T* p) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) w[i] = reinterpret_cast<const uint4*>(p)[i];
+    }
+};
+
 // 8 elements of T as floats through one 16-byte (16-bit T) or two (fp32) accesses.
 template <typename T>
 struct Vec8 {
     float v[8];
-    __device__ __forceinline__ void load(const T* p) {
+    __device__ __forceinline__ void set(const Raw8<T>& r) {
         if constexpr (sizeof(T) == 4) {
-            const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+            const float4 a = *reinterpret_cast<const float4*>(&r.w[0]), b = *reinterpret_cast<const float4*>(&r.w[1]);
             v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
         } else {
-            uint4 u = *reinterpret_cast<const uint4*>(p);
-            const T* e = reinterpret_cast<const T*>(&u);
+            const uint32_t u[4] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = to_f32(e[i]);
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = pair_to_f32<T>(u[i]);
+                v[2 * i] = f.x, v[2 * i + 1] = f.y;
+            }
         }
+    }
+    __device__ __forceinline__ void load(const T* p) {
+        Raw8<T> r;
+        r.load(p);
+        set(r);
     }
     __device__ __forceinline__ void store(T* p) const {
         if constexpr (sizeof(T) == 4) {
@@ -63,46 +82,158 @@ struct Vec8 {
     }
 };
 
-// ---- residual add / GELU (n % 8 == 0, grid-stride) ----
+// ---- residual add / GELU / gate (n % 8 == 0, grid-stride) ----
+// Each thread keeps kEwU 8-element vectors in flight (64 bytes of loads per
+// input), the vectors of one step spaced a whole grid apart so every warp
+// access stays a contiguous 512-byte (16-bit) or 1024-byte (fp32) run.
 template <typename T>
-__global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y, int64_t n8) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-        Vec8<T> x, z;
-        x.load(a + 8 * i);
-        z.load(b + 8 * i);
+constexpr int ew_unroll() {
+    return sizeof(T) == 4 ? 2 : 4;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y,
+                                                  int64_t n8) {
+    constexpr int U = ew_unroll<T>();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n8; i0 += U * stride) {
+        Raw8<T> ra[U], rb[U];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x.v[k] += z.v[k];
-        x.store(y + 8 * i);
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * stride < n8) {
+                ra[u].load(a + 8 * (i0 + u * stride));
+                rb[u].load(b + 8 * (i0 + u * stride));
+            }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * stride < n8) {
+                Vec8<T> x, z;
+                x.set(ra[u]);
+                z.set(rb[u]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) x.v[k] += z.v[k];
+                x.store(y + 8 * (i0 + u * stride));
+            }
     }
 }
 
 template <typename T>
-__global__ void gelu_kernel(const T* __restrict__ a, T* __restrict__ y, int64_t n8) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-        Vec8<T> x;
-        x.load(a + 8 * i);
+__global__ void __launch_bounds__(256) gelu_kernel(const T* __restrict__ a, T* __restrict__ y, int64_t n8) {
+    constexpr int U = ew_unroll<T>();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n8; i0 += U * stride) {
+        Raw8<T> ra[U];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x.v[k] = gelu_as(x.v[k]);  // exact-erf GELU, A&S 7.1.26 (|err| <= 2e-7)
-        x.store(y + 8 * i);
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * stride < n8) ra[u].load(a + 8 * (i0 + u * stride));
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * stride < n8) {
+                Vec8<T> x;
+                x.set(ra[u]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) x.v[k] = gelu_as(x.v[k]);  // exact-erf GELU, A&S 7.1.26
+                x.store(y + 8 * (i0 + u * stride));
+            }
     }
 }
 
 // y[r][h*dh + d] = x[r][h*dh + d] * g[r][h]   (dh % 8 == 0)
 template <typename T>
-__global__ void gate_kernel(const T* __restrict__ x, const T* __restrict__ g, T* __restrict__ y, int64_t rows, int H,
-                            int dh) {
+__global__ void __launch_bounds__(256) gate_kernel(const T* __restrict__ x, const T* __restrict__ g,
+                                                   T* __restrict__ y, int64_t rows, int H, int dh) {
+    constexpr int U = ew_unroll<T>();
     const unsigned per_row = (unsigned)(H * dh / 8), dh8 = (unsigned)(dh / 8);
     const int64_t n8 = rows * per_row;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-        // 32-bit index arithmetic (n8 < 2^32 checked on the host)
-        const unsigned r = (unsigned)i / per_row;
-        const int h = (int)(((unsigned)i - r * per_row) / dh8);
-        const float gv = to_f32(g[(int64_t)r * H + h]);
-        Vec8<T> a;
-        a.load(x + 8 * i);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n8; i0 += U * stride) {
+        Raw8<T> ra[U];
+        float gv[U];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) a.v[k] *= gv;
-        a.store(y + 8 * i);
+        for (int u = 0; u < U; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i < n8) {
+                // 32-bit index arithmetic (n8 < 2^32 checked on the host)
+                const unsigned r = (unsigned)i / per_row;
+                const int h = (int)(((unsigned)i - r * per_row) / dh8);
+                gv[u] = to_f32(g[(int64_t)r * H + h]);
+                ra[u].load(x + 8 * i);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (i0 + u * stride < n8) {
+                Vec8<T> a;
+                a.set(ra[u]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) a.v[k] *= gv[u];
+                a.store(y + 8 * (i0 + u * stride));
+            }
+    }
+}
+
+// RMSNorm over groups of R consecutive rows read as one flat run of R*D/8
+// 8-element chunks (R*D/8 = 32*NC): lane l owns chunks l + 32 i (i < NC) of
+// every group, so all 32 lanes carry data for any D the grouping fits, the
+// lane's gamma chunks are the same for every group (loaded once), and a warp
+// has NC 16-byte (16-bit) or 32-byte (fp32) loads in flight per group.
+template <typename T, int R, int NC>
+__global__ void __launch_bounds__(256) rms_group_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
+                                                        T* __restrict__ y, int64_t rows, int D, float scale) {
+    __shared__ __align__(16) float gs[1024];
+    const int lane = threadIdx.x & 31, D8 = D / 8;
+    for (int k = threadIdx.x; k < D; k += blockDim.x) gs[k] = gamma[k];
+    __syncthreads();
+    int rq[NC], gc[NC];  // row within the group and gamma offset of the lane's chunks
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+        const int c = lane + 32 * i;
+        rq[i] = c / D8;
+        gc[i] = 8 * (c - rq[i] * D8);
+    }
+    const int64_t groups = (rows + R - 1) / R;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t grp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); grp < groups; grp += warps) {
+        const int64_t r0 = grp * R;
+        const int nrows = rows - r0 < R ? (int)(rows - r0) : R;
+        const T* xg = x + r0 * D;
+        Raw8<T> raw[NC];
+#pragma unroll
+        for (int i = 0; i < NC; ++i)
+            if (rq[i] < nrows) raw[i].load(xg + 8 * (lane + 32 * i));
+        float ss[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) ss[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < NC; ++i) {
+            float p = 0.f;
+            if (rq[i] < nrows) {
+                Vec8<T> v;
+                v.set(raw[i]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) p += v.v[k] * v.v[k];
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) ss[r] += rq[i] == r ? p : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) ss[r] = rsqrtf(warp_sum(ss[r]) + 1e-12f) * scale;
+        T* yg = y + r0 * D;
+#pragma unroll
+        for (int i = 0; i < NC; ++i)
+            if (rq[i] < nrows) {
+                float inv = ss[0];
+#pragma unroll
+                for (int r = 1; r < R; ++r) inv = rq[i] == r ? ss[r] : inv;
+                Vec8<T> v;
+                v.set(raw[i]);
+                const float4 g0 = *reinterpret_cast<const float4*>(gs + gc[i]);
+                const float4 g1 = *reinterpret_cast<const float4*>(gs + gc[i] + 4);
+                const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v.v[k] *= inv * g[k];
+                v.store(yg + 8 * (lane + 32 * i));
+            }
     }
 }
 
@@ -156,26 +287,42 @@ __global__ void __launch_bounds__(256) rms_kernel(const T* __restrict__ x, const
 // RoPE over positions: x [seqs][L][H][64]; pair (2i, 2i+1) of every head at
 // position p rotated by (cos, sin)[p][i].
 template <typename T>
-__global__ void rope_kernel(const T* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
-                            T* __restrict__ y, int64_t seqs, int L, int H) {
+__global__ void __launch_bounds__(256) rope_kernel(const T* __restrict__ x, const float* __restrict__ cs,
+                                                   const float* __restrict__ sn, T* __restrict__ y, int64_t seqs,
+                                                   int L, int H) {
+    constexpr int U = ew_unroll<T>();
     const int64_t n8 = seqs * L * H * 8;  // 8 chunks of 8 per 64-wide head
     const unsigned hh = (unsigned)(8 * H), ll = (unsigned)L;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-        const int chunk = (int)(i & 7);
-        const int p = (int)(((unsigned)i / hh) % ll);  // 32-bit (n8 < 2^32 checked on the host)
-        Vec8<T> a;
-        a.load(x + 8 * i);
-        // pairs 4*chunk .. 4*chunk+3 of position p: one 16-byte load of each table
-        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + p * 32) + chunk);
-        const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + p * 32) + chunk);
-        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n8; i0 += U * stride) {
+        Raw8<T> ra[U];
+        float4 c4[U], s4[U];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float x0 = a.v[2 * k], x1 = a.v[2 * k + 1];
-            a.v[2 * k] = x0 * cc[k] - x1 * ss[k];
-            a.v[2 * k + 1] = x0 * ss[k] + x1 * cc[k];
+        for (int u = 0; u < U; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i < n8) {
+                const int chunk = (int)(i & 7);
+                const int p = (int)(((unsigned)i / hh) % ll);  // 32-bit (n8 < 2^32 checked on the host)
+                ra[u].load(x + 8 * i);
+                // pairs 4*chunk .. 4*chunk+3 of position p: one 16-byte load of each table
+                c4[u] = __ldg(reinterpret_cast<const float4*>(cs + p * 32) + chunk);
+                s4[u] = __ldg(reinterpret_cast<const float4*>(sn + p * 32) + chunk);
+            }
         }
-        a.store(y + 8 * i);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (i0 + u * stride >= n8) continue;
+            const float cc[4] = {c4[u].x, c4[u].y, c4[u].z, c4[u].w}, ss[4] = {s4[u].x, s4[u].y, s4[u].z, s4[u].w};
+            Vec8<T> a;
+            a.set(ra[u]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float x0 = a.v[2 * k], x1 = a.v[2 * k + 1];
+                a.v[2 * k] = x0 * cc[k] - x1 * ss[k];
+                a.v[2 * k + 1] = x0 * ss[k] + x1 * cc[k];
+            }
+            a.store(y + 8 * (i0 + u * stride));
+        }
     }
 }
 
@@ -595,10 +742,36 @@ void sigmoid_gate(const void* x, const void* g, void* y, int64_t rows, int H, in
     MBR_CUDA(cudaGetLastError());
 }
 
+template <typename T>
+bool launch_rms_group(int R, int NC, unsigned g, const void* x, const float* gamma, void* y, int64_t rows, int D,
+                      float scale, cudaStream_t st) {
+#define MBR_RMS_GROUP(r_, nc_)                                                                      \
+    if (R == r_ && NC == nc_) {                                                                     \
+        rms_group_kernel<T, r_, nc_><<<g, 256, 0, st>>>((const T*)x, gamma, (T*)y, rows, D, scale); \
+        MBR_CUDA(cudaGetLastError());                                                               \
+        return true;                                                                                \
+    }
+    MBR_RMS_GROUP(1, 3) MBR_RMS_GROUP(1, 4) MBR_RMS_GROUP(2, 3) MBR_RMS_GROUP(2, 4) MBR_RMS_GROUP(3, 3)
+    MBR_RMS_GROUP(4, 3) MBR_RMS_GROUP(4, 4) MBR_RMS_GROUP(6, 3) MBR_RMS_GROUP(8, 3) MBR_RMS_GROUP(8, 4)
+#undef MBR_RMS_GROUP
+    return false;
+}
+
 void rms_norm(const void* x, const float* gamma, void* y, int64_t rows, int D, float scale, int dtype,
               cudaStream_t st) {
     MBR_CHECK(D % 8 == 0 && D <= 1024, "rms_norm: dim must be a multiple of 8 and <= 1024");
     MBR_CHECK(((uintptr_t)gamma & 15) == 0, "rms_norm: gamma must be 16-byte aligned");
+    // row groups with every lane busy: (R rows, NC chunks per lane) with R * D / 8 == 32 * NC
+    const int D8 = D / 8;
+    int R = 0, NC = 0;
+    for (int r = 1; r <= 8 && !R; ++r)
+        if ((r * D8) % 32 == 0 && (r * D8) / 32 >= 3 && (r * D8) / 32 <= 4) R = r, NC = r * D8 / 32;
+    if (R) {
+        const unsigned g = (unsigned)std::min<int64_t>(ceil_div(ceil_div(rows, R), 8), (int64_t)sm_count() * 8);
+        bool done = false;
+        MBR_DISPATCH_DTYPE(dtype, T, { done = launch_rms_group<T>(R, NC, g, x, gamma, y, rows, D, scale, st); });
+        if (done) return;
+    }
     unsigned grid = (unsigned)std::min<int64_t>(ceil_div(rows, 16), (int64_t)sm_count() * 8);
     MBR_DISPATCH_DTYPE(dtype, T, {
         if (D <= 256) rms_kernel<T, 1><<<grid, 256, 0, st>>>((const T*)x, gamma, (T*)y, rows, D, scale);

@@ -66,6 +66,26 @@ def test_rms_norm_add_gelu(torch_cuda, dtype, D):
 
 
 @pytest.mark.parametrize("dtype", ["fp32", "fp16", "bf16"])
+@pytest.mark.parametrize("rows,D", [(1001, 64), (1003, 128), (999, 192), (1001, 200), (7, 384), (5, 1024), (1, 512)])
+def test_ragged_rows(torch_cuda, dtype, rows, D):
+    """Row counts that leave a partial row group (RMSNorm) and element counts
+    that leave a partial unrolled step (add, GELU)."""
+    torch = torch_cuda
+    import cudasep
+
+    x, y = _inputs(torch, rows, D, dtype, seed=rows + D, n=2)
+    gamma = torch.linspace(0.25, 2.0, D)
+    xd, yd, gd = x.cuda(), y.cuda(), gamma.cuda()
+    xr = x.double().numpy()
+    ref = xr / np.sqrt((xr ** 2).sum(-1, keepdims=True) + 1e-12) * gamma.double().numpy() * 3.0
+    _close(cudasep.op_rms_norm(xd, gd, 3.0), ref, dtype, "rms_norm")
+    _close(cudasep.op_add(xd, yd), xr + y.double().numpy(), dtype, "add")
+    from scipy.special import erf
+
+    _close(cudasep.op_gelu(xd), 0.5 * xr * (1 + erf(xr / np.sqrt(2))), dtype, "gelu")
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "fp16", "bf16"])
 def test_sigmoid_gate_and_rope(torch_cuda, dtype):
     torch = torch_cuda
     import cudasep
