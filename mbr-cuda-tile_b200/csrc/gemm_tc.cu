@@ -125,7 +125,7 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
     } else {
         if constexpr (EPI == ops::EPI_GELU_T) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_as(v[j]);
+            for (int j = 0; j < 16; ++j) gelu2(v[2 * j], v[2 * j + 1]);
         } else if constexpr (EPI == ops::EPI_TANH_T) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
@@ -172,6 +172,30 @@ __device__ __forceinline__ void rope_rotate(const EpiQKV& e, int row, int n0, fl
                 v[2 * i] = x0 * cc[u] - x1 * ss[u];
                 v[2 * i + 1] = x0 * ss[u] + x1 * cc[u];
             }
+        }
+    }
+}
+
+// The 16 (cos, sin) pairs [p0, p0 + 16) of one table row (64-byte aligned).
+__device__ __forceinline__ void load_rope16(const float* cs, const float* sn, int p0, float4 (&c)[4],
+                                            float4 (&s)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        c[i] = __ldg(reinterpret_cast<const float4*>(cs + p0) + i);
+        s[i] = __ldg(reinterpret_cast<const float4*>(sn + p0) + i);
+    }
+}
+// Rotates the 16 pairs (v[2i], v[2i+1]) by the angles whose cos / sin are given.
+__device__ __forceinline__ void rope_apply16(const float4 (&c)[4], const float4 (&s)[4], float (&v)[32]) {
+#pragma unroll
+    for (int i4 = 0; i4 < 4; ++i4) {
+        const float cc[4] = {c[i4].x, c[i4].y, c[i4].z, c[i4].w}, ss[4] = {s[i4].x, s[i4].y, s[i4].z, s[i4].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = 4 * i4 + u;
+            const float x0 = v[2 * i], x1 = v[2 * i + 1];
+            v[2 * i] = x0 * cc[u] - x1 * ss[u];
+            v[2 * i + 1] = x0 * ss[u] + x1 * cc[u];
         }
     }
 }
@@ -252,7 +276,7 @@ __device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float
     }
     if constexpr (EPI == ops::EPI_GELU_T) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_as(v[j]);
+        for (int j = 0; j < 16; ++j) gelu2(v[2 * j], v[2 * j + 1]);
     } else if constexpr (EPI == ops::EPI_TANH_T) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
@@ -428,18 +452,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int yrow = tl.y + q * 32;
                 const int ncol = g.N - (tl.z + half * (BN / 2));
                 const int nch = ncol <= 0 ? 0 : (ncol >= 32 * kChunks ? kChunks : (ncol + 31) / 32);
+                // RoPE: the lane's position and the section (q, k or v) of this
+                // warp's 128-column half are fixed for the tile; the 16 table
+                // pairs of a chunk are loaded one chunk ahead
+                bool rope = false;
+                const float* rcos = nullptr;
+                const float* rsin = nullptr;
+                float4 tc[4], ts[4];
+                if constexpr (EPI == ops::EPI_ROPE_T) {
+                    const int rrow = tl.y + q * 32 + lane;
+                    const int rpos = qkv.mode == ops::SEQ_TIME ? (rrow / qkv.NB) % qkv.T : rrow % qkv.NB;
+                    rope = (tl.z + half * (BN / 2)) / (qkv.H * 64) < 2;
+                    rcos = qkv.cos_t + rpos * 32;
+                    rsin = qkv.sin_t + rpos * 32;
+                    if (rope && nch > 0) load_rope16(rcos, rsin, 0, tc, ts);
+                }
+                // the next chunk's TMEM load is issued before this chunk's math
+                // (not for RoPE, whose table prefetch needs those registers)
+                constexpr bool kPipeTmem = EPI != ops::EPI_ROPE_T;
                 uint32_t r[32];
-                if (nch > 0) tmem_ld32(taddr, r);
+                if (kPipeTmem && nch > 0) tmem_ld32(taddr, r);
 #pragma unroll 1
                 for (int c = 0; c < nch; ++c) {
                     const int n0 = tl.z + half * (BN / 2) + c * 32;
+                    if (!kPipeTmem) tmem_ld32(taddr + c * 32, r);
                     tmem_ld_wait(r);
                     float v[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                    if (c + 1 < nch) tmem_ld32(taddr + (c + 1) * 32, r);
+                    if (kPipeTmem && c + 1 < nch) tmem_ld32(taddr + (c + 1) * 32, r);
                     apply_epi<EPI>(g, n0, v);
-                    if constexpr (EPI == ops::EPI_ROPE_T) rope_rotate(qkv, tl.y + q * 32 + lane, n0, v);
+                    if constexpr (EPI == ops::EPI_ROPE_T) {
+                        if (rope) {
+                            float4 nc[4], ns[4];
+                            if (c + 1 < nch) load_rope16(rcos, rsin, ((c + 1) & 1) * 16, nc, ns);
+                            rope_apply16(tc, ts, v);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) tc[i] = nc[i], ts[i] = ns[i];
+                        }
+                    }
                     const int h16 = k16 ? (c & 1) : 0;
                     uint8_t* stg = stg_base + (Cfg::NSTG == 2 ? (boxes & 1) : 0) * kStagingPerWarp;
                     if (h16 == 0) {  // a staging tile is free once the store issued from it has read it
@@ -669,6 +720,9 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
     else if (p.maxN % 192 == 0 && !staged16) bn = 192;
     else if (p.maxN % 128 == 0 || p.maxN < 256) bn = 128;
     else bn = 256;
+    // the RoPE epilogue treats each warp's column half (bn / 2) as lying in one
+    // of the q / k / v sections
+    if (p.epi == ops::EPI_ROPE_T && L.qkv.H > 0 && (L.qkv.H * 64) % (bn / 2) != 0) bn = 128;
     L.bn = bn;
     L.epi = p.epi;
     if (p.epi == ops::EPI_ROPE_T)

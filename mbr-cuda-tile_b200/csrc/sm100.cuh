@@ -131,8 +131,13 @@ __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Arrive once on an mbarrier given by its cluster address (possibly the peer's).
+// Arrive on an mbarrier of either CTA of the pair (cluster address), with the
+// default CTA-scope release: a cluster-scope release would also wait for this
+// thread's earlier bulk stores to become visible cluster-wide (thousands of
+// cycles after an epilogue's TMA stores), and the consumer of this arrive only
+// needs the thread's completed TMEM loads ordered before it.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // 2-D tiled TMA load into this CTA's shared memory whose completion is counted
 // on an mbarrier of either CTA of the pair (cluster address).
