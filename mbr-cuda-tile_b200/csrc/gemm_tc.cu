@@ -256,6 +256,19 @@ __device__ __forceinline__ void stage_chunk(uint8_t* stg, int lane, int half16, 
     }
 }
 
+// Stages 32 accumulator columns of this lane's row as one 64-byte row of a
+// 32 x 32 box (16-bit outputs, 64-byte swizzle: 16-byte unit u of row r sits at
+// unit u ^ ((r >> 1) & 3)).
+template <typename T>
+__device__ __forceinline__ void stage_chunk64(uint8_t* stg, int lane, const float (&v)[32]) {
+    uint8_t* row = stg + lane * 64;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(row + ((c ^ ((lane >> 1) & 3)) << 4)) =
+            make_uint4(pack2(v[8 * c], v[8 * c + 1], (T*)nullptr), pack2(v[8 * c + 2], v[8 * c + 3], (T*)nullptr),
+                       pack2(v[8 * c + 4], v[8 * c + 5], (T*)nullptr), pack2(v[8 * c + 6], v[8 * c + 7], (T*)nullptr));
+}
+
 // acc + bias and the activation of the epilogue, in place.
 template <int EPI>
 __device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float (&v)[32]) {
@@ -440,9 +453,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const bool rv = row < g.M;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + half * (BN / 2);
             constexpr bool kStoresViaTma = EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32 || EPI == ops::EPI_T ||
-                                           EPI == ops::EPI_GELU_T || EPI == ops::EPI_TANH_T ||
-                                           EPI == ops::EPI_ROPE_T;
-            if (kStoresViaTma && c_tma) {
+                                           EPI == ops::EPI_GELU_T || EPI == ops::EPI_TANH_T;
+            if (EPI == ops::EPI_ROPE_T && c_tma) {
+                // RoPE output: warp half `half` takes pair half `half` of every
+                // head in the tile (columns 64 h + 32 half .. + 32), so one row
+                // of 16 (cos, sin) pairs, loaded once, serves all its chunks.
+                // Each 32-column chunk is one 32 x 32 box (64-byte rows, 64-byte
+                // swizzle); a warp's staging space holds 2 NSTG boxes in turn.
+                constexpr int kHeads = BN / 64;
+                constexpr int kSlots = 2 * Cfg::NSTG;
+                const int rrow = tl.y + q * 32 + lane;
+                const int rpos = qkv.mode == ops::SEQ_TIME ? (rrow / qkv.NB) % qkv.T : rrow % qkv.NB;
+                float4 tc[4], ts[4];
+                load_rope16(qkv.cos_t + rpos * 32, qkv.sin_t + rpos * 32, half * 16, tc, ts);
+                const int DI = qkv.H * 64;
+                const int yrow = tl.y + q * 32;
+                uint8_t* stg_base = smem + Cfg::STAGING_OFF + (warp - 2) * Cfg::NSTG * kStagingPerWarp;
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + half * 32;
+#pragma unroll 1
+                for (int h = 0; h < kHeads; ++h) {
+                    const int n0 = tl.z + h * 64 + half * 32;
+                    if (n0 >= g.N) break;
+                    uint32_t r[32];
+                    tmem_ld32(tbase + h * 64, r);
+                    tmem_ld_wait(r);
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                    apply_epi<EPI>(g, n0, v);
+                    if (n0 / DI < 2) rope_apply16(tc, ts, v);  // q and k sections
+                    uint8_t* stg = stg_base + (boxes % kSlots) * (kStagingPerWarp / 2);
+                    if (lane == 0) bulk_wait_read_n<kSlots - 1>();  // the store issued from this slot has read it
+                    __syncwarp();
+                    stage_chunk64<T>(stg, lane, v);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (yrow < g.M) {
+                        if (lane == 0) {
+                            tma_store_3d(&tmC, stg, n0, c_tma == 2 ? g.c_group : yrow, c_tma == 2 ? yrow : g.c_group);
+                            bulk_commit();
+                        }
+                        ++boxes;
+                    }
+                }
+            } else if (kStoresViaTma && c_tma) {
                 // stage through this warp's 32-row tiles (NSTG of them, used in
                 // turn); one TMA store (or reduce-add into the fp32 residual)
                 // per 128-byte row group.  The TMEM load of the next 32 columns
@@ -452,45 +506,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int yrow = tl.y + q * 32;
                 const int ncol = g.N - (tl.z + half * (BN / 2));
                 const int nch = ncol <= 0 ? 0 : (ncol >= 32 * kChunks ? kChunks : (ncol + 31) / 32);
-                // RoPE: the lane's position and the section (q, k or v) of this
-                // warp's 128-column half are fixed for the tile; the 16 table
-                // pairs of a chunk are loaded one chunk ahead
-                bool rope = false;
-                const float* rcos = nullptr;
-                const float* rsin = nullptr;
-                float4 tc[4], ts[4];
-                if constexpr (EPI == ops::EPI_ROPE_T) {
-                    const int rrow = tl.y + q * 32 + lane;
-                    const int rpos = qkv.mode == ops::SEQ_TIME ? (rrow / qkv.NB) % qkv.T : rrow % qkv.NB;
-                    rope = (tl.z + half * (BN / 2)) / (qkv.H * 64) < 2;
-                    rcos = qkv.cos_t + rpos * 32;
-                    rsin = qkv.sin_t + rpos * 32;
-                    if (rope && nch > 0) load_rope16(rcos, rsin, 0, tc, ts);
-                }
                 // the next chunk's TMEM load is issued before this chunk's math
-                // (not for RoPE, whose table prefetch needs those registers)
-                constexpr bool kPipeTmem = EPI != ops::EPI_ROPE_T;
                 uint32_t r[32];
-                if (kPipeTmem && nch > 0) tmem_ld32(taddr, r);
+                if (nch > 0) tmem_ld32(taddr, r);
 #pragma unroll 1
                 for (int c = 0; c < nch; ++c) {
                     const int n0 = tl.z + half * (BN / 2) + c * 32;
-                    if (!kPipeTmem) tmem_ld32(taddr + c * 32, r);
                     tmem_ld_wait(r);
                     float v[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-                    if (kPipeTmem && c + 1 < nch) tmem_ld32(taddr + (c + 1) * 32, r);
+                    if (c + 1 < nch) tmem_ld32(taddr + (c + 1) * 32, r);
                     apply_epi<EPI>(g, n0, v);
-                    if constexpr (EPI == ops::EPI_ROPE_T) {
-                        if (rope) {
-                            float4 nc[4], ns[4];
-                            if (c + 1 < nch) load_rope16(rcos, rsin, ((c + 1) & 1) * 16, nc, ns);
-                            rope_apply16(tc, ts, v);
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) tc[i] = nc[i], ts[i] = ns[i];
-                        }
-                    }
                     const int h16 = k16 ? (c & 1) : 0;
                     uint8_t* stg = stg_base + (Cfg::NSTG == 2 ? (boxes & 1) : 0) * kStagingPerWarp;
                     if (h16 == 0) {  // a staging tile is free once the store issued from it has read it
@@ -605,7 +632,9 @@ void make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int 
 // 32 rows x 128 bytes, 128-byte swizzle (the layout stage_chunk writes).
 // The two outer dimensions are ordered by increasing stride; `swapped` tells
 // the kernel that the group dimension comes before the row dimension.
-void make_out_map(CUtensorMap* m, const GemmPlanTC& p, bool& swapped) {
+// box_bytes: the inner extent of one store box, 128 (128-byte swizzle,
+// 32 rows) or 64 (64-byte swizzle, 32 rows, the RoPE epilogue).
+void make_out_map(CUtensorMap* m, const GemmPlanTC& p, bool& swapped, int box_bytes) {
     const int64_t es = p.c_dtype == DT_F32 ? 4 : 2;
     MBR_CHECK(((uintptr_t)p.c_base & 15) == 0, "TMA output base must be 16-byte aligned");
     MBR_CHECK((p.c_row_stride * es) % 16 == 0 && (p.c_group_stride * es) % 16 == 0,
@@ -613,7 +642,7 @@ void make_out_map(CUtensorMap* m, const GemmPlanTC& p, bool& swapped) {
     swapped = p.c_groups > 1 && p.c_group_stride < p.c_row_stride;
     cuuint64_t dims[3] = {(cuuint64_t)p.c_cols, (cuuint64_t)p.c_rows, (cuuint64_t)p.c_groups};
     cuuint64_t strides[2] = {(cuuint64_t)(p.c_row_stride * es), (cuuint64_t)(p.c_group_stride * es)};
-    cuuint32_t box[3] = {(cuuint32_t)(kStageRowBytes / es), 32, 1};
+    cuuint32_t box[3] = {(cuuint32_t)(box_bytes / es), 32, 1};
     if (swapped) {
         std::swap(dims[1], dims[2]);
         std::swap(strides[0], strides[1]);
@@ -624,7 +653,8 @@ void make_out_map(CUtensorMap* m, const GemmPlanTC& p, bool& swapped) {
                             : p.c_dtype == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUresult r = encode_fn()(m, t, 3, const_cast<void*>(p.c_base), dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw Error(ERR_CUDA, "cuTensorMapEncodeTiled (output) failed: " + std::to_string((int)r));
 }
@@ -720,9 +750,6 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
     else if (p.maxN % 192 == 0 && !staged16) bn = 192;
     else if (p.maxN % 128 == 0 || p.maxN < 256) bn = 128;
     else bn = 256;
-    // the RoPE epilogue treats each warp's column half (bn / 2) as lying in one
-    // of the q / k / v sections
-    if (p.epi == ops::EPI_ROPE_T && L.qkv.H > 0 && (L.qkv.H * 64) % (bn / 2) != 0) bn = 128;
     L.bn = bn;
     L.epi = p.epi;
     if (p.epi == ops::EPI_ROPE_T)
@@ -777,7 +804,7 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
                       "tc gemm: group does not match the output view");
         }
         bool swapped = false;
-        make_out_map(&L.tmC, p, swapped);
+        make_out_map(&L.tmC, p, swapped, p.epi == ops::EPI_ROPE_T ? 64 : kStageRowBytes);
         L.c_tma = swapped ? 2 : 1;
     }
     L.ok = true;
