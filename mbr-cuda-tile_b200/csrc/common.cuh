@@ -115,43 +115,36 @@ __device__ __forceinline__ float gelu_as(float x) {
     return x >= 0.0f ? x - q : q;
 }
 
-// Two floats in one 64-bit register pair for the packed f32x2 arithmetic of
-// sm_100 (one instruction works on both halves, round to nearest even).
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-
-// GELU (exact-erf form) of two values with one exponential each:
+// GELU (exact-erf form) of N values (N even) with one exponential each:
 // gelu(x) = x - x Q(x) for x >= 0 and x Q(-x) for x < 0, where the normal tail
-// Q(t) = erfc(t / sqrt 2) / 2 is evaluated as 2^P(t).  P is a degree-9
+// Q(t) = erfc(t / sqrt 2) / 2 is evaluated as 2^P(t).  P is a degree-7
 // least-squares Chebyshev fit of log2 Q(t) on [0, 5.5] (computed from the
 // log of the normal CDF in double precision, converted to monomial form and
 // rounded to fp32); t is clamped to 5.5, where Q < 2e-8.  Evaluated in fp32
-// (packed Horner steps) the GELU error stays below 1.3e-7 absolute over the
-// whole real line, well under a 16-bit output's rounding.
-__device__ __forceinline__ void gelu2(float& x0, float& x1) {
-    constexpr float kC[10] = {-9.999970794e-01f, -1.151165724e+00f, -4.589049518e-01f, -5.313431099e-02f,
-                              7.750511635e-03f,  -5.450547324e-04f, -5.283674182e-05f, 1.788428017e-05f,
-                              -1.828373570e-06f, 7.057403195e-08f};
-    const uint64_t t = f2_pack(fminf(fabsf(x0), 5.5f), fminf(fabsf(x1), 5.5f));
-    uint64_t p = f2_pack(kC[9], kC[9]);
+// the GELU error stays below 5e-7 absolute (Q within 1.1e-5 relative), under
+// a 16-bit output's rounding.  The Horner steps run on packed f32x2 pairs,
+// all N/2 chains advanced together so consecutive instructions are independent.
+template <int N>
+__device__ __forceinline__ void gelu_tail(float (&v)[N]) {
+    constexpr float kC[8] = {-9.999850392e-01f, -1.151344657e+00f, -4.582461119e-01f, -5.417189747e-02f,
+                             8.609841578e-03f,  -9.561956394e-04f, 6.483463949e-05f,  -1.995924322e-06f};
+    float2 t[N / 2], p[N / 2];
 #pragma unroll
-    for (int i = 8; i >= 0; --i) p = f2_fma(p, t, f2_pack(kC[i], kC[i]));
-    float p0, p1;
-    f2_unpack(p, p0, p1);
-    const float r0 = x0 * ex2_approx(p0), r1 = x1 * ex2_approx(p1);
-    x0 = x0 >= 0.0f ? x0 - r0 : r0;
-    x1 = x1 >= 0.0f ? x1 - r1 : r1;
+    for (int j = 0; j < N / 2; ++j) {
+        t[j] = make_float2(fminf(fabsf(v[2 * j]), 5.5f), fminf(fabsf(v[2 * j + 1]), 5.5f));
+        p[j] = make_float2(kC[7], kC[7]);
+    }
+#pragma unroll
+    for (int i = 6; i >= 0; --i)
+#pragma unroll
+        for (int j = 0; j < N / 2; ++j) p[j] = __ffma2_rn(p[j], t[j], make_float2(kC[i], kC[i]));
+#pragma unroll
+    for (int j = 0; j < N / 2; ++j) {
+        const float x0 = v[2 * j], x1 = v[2 * j + 1];
+        const float r0 = x0 * ex2_approx(p[j].x), r1 = x1 * ex2_approx(p[j].y);
+        v[2 * j] = x0 >= 0.0f ? x0 - r0 : r0;
+        v[2 * j + 1] = x1 >= 0.0f ? x1 - r1 : r1;
+    }
 }
 
 // tanh(x) = sign(x) (1 - 2 / (e^{2|x|} + 1)); absolute error ~1e-7.

@@ -124,8 +124,7 @@ __device__ __forceinline__ void epilogue_chunk(const ops::GemmGroup& g, int row,
         }
     } else {
         if constexpr (EPI == ops::EPI_GELU_T) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) gelu2(v[2 * j], v[2 * j + 1]);
+            gelu_tail(v);
         } else if constexpr (EPI == ops::EPI_TANH_T) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
@@ -279,7 +278,9 @@ __device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const float4 b4 = __ldg(reinterpret_cast<const float4*>(b) + j);
-                v[4 * j] += b4.x, v[4 * j + 1] += b4.y, v[4 * j + 2] += b4.z, v[4 * j + 3] += b4.w;
+                const float2 s0 = __fadd2_rn(make_float2(v[4 * j], v[4 * j + 1]), make_float2(b4.x, b4.y));
+                const float2 s1 = __fadd2_rn(make_float2(v[4 * j + 2], v[4 * j + 3]), make_float2(b4.z, b4.w));
+                v[4 * j] = s0.x, v[4 * j + 1] = s0.y, v[4 * j + 2] = s1.x, v[4 * j + 3] = s1.y;
             }
         } else {
 #pragma unroll
@@ -288,8 +289,7 @@ __device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float
         }
     }
     if constexpr (EPI == ops::EPI_GELU_T) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) gelu2(v[2 * j], v[2 * j + 1]);
+        gelu_tail(v);
     } else if constexpr (EPI == ops::EPI_TANH_T) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
