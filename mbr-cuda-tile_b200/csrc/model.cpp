@@ -161,7 +161,6 @@ MelBandRoformer::MelBandRoformer(const ModelWeights& w, int device, int dtype) :
         // tiles of the band map for the stand-alone band ops (one allocation)
         opsapi::BandTilesHost bh = opsapi::make_band_tiles(fi, C_, F_);
         Packer tp;
-        size_t o_t = tp.add(bh.tiles.data(), bh.tiles.size() * sizeof(int4));
         size_t o_j = tp.add(bh.jl.data(), bh.jl.size() * 4);
         size_t o_jr = tp.add(bh.jr.data(), bh.jr.size() * 4);
         size_t o_k = tp.add(bh.bk.data(), bh.bk.size() * 4);
@@ -169,12 +168,11 @@ MelBandRoformer::MelBandRoformer(const ModelWeights& w, int device, int dtype) :
         MBR_CUDA(cudaMalloc(&d_band_tiles_, tp.buf.size()));
         MBR_CUDA(cudaMemcpy(d_band_tiles_, tp.buf.data(), tp.buf.size(), cudaMemcpyHostToDevice));
         uint8_t* base = (uint8_t*)d_band_tiles_;
-        band_tiles_.tiles = (const int4*)(base + o_t);
         band_tiles_.jl = (const int*)(base + o_j);
         band_tiles_.jr = (const int*)(base + o_jr);
         band_tiles_.bk = (const int*)(base + o_k);
         band_tiles_.bo = (const int*)(base + o_o);
-        band_tiles_.count = (int)bh.tiles.size();
+        band_tiles_.count = bh.count;
         band_tiles_.stride = bh.stride;
         band_tiles_.max_n = bh.max_n;
     }

@@ -802,9 +802,9 @@ BandTilesHost make_band_tiles(const std::vector<int>& fi, int C, int F) {
         ent.push_back(std::move(e));
     }
     h.stride = std::max(32, (h.max_n + 31) / 32 * 32);
+    h.count = (int)ent.size();
     for (size_t t = 0; t < ent.size(); ++t) {
         const int f0 = (int)t * kBandTileBins, nf = std::min(kBandTileBins, F - f0), n = (int)ent[t].size();
-        h.tiles.push_back(make_int4(f0, nf, 0, n));
         std::vector<int> row(n);
         for (int k = 0; k < n; ++k) row[k] = (fi[ent[t][k]] % C) * nf + fi[ent[t][k]] / C - f0;
         for (int k = 0; k < h.stride; ++k) {

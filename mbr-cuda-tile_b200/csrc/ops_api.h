@@ -23,14 +23,13 @@ void rms_norm(const void* x, const float* gamma, void* y, int64_t rows, int D, f
 void rope(const void* x, const float* cs, const float* sn, void* y, int64_t seqs, int L, int H, int dtype,
           cudaStream_t st);
 // Frequency-range tiles of a band map for the transposing band ops: tile i
-// covers bins [f0, f0 + nf) (kBandTileBins at most) of all channels and the
-// band-freq entries j whose bin lies there (jl[off .. off + n), ascending);
-// bin_off / bin_k list, for each (channel, bin) row of the tile, the tile-local
-// positions of its entries.
+// covers bins [32 i, 32 i + 32) of all channels and the band-freq entries j
+// whose bin lies there.  The per-tile tables sit at fixed offsets (tile i at
+// i * stride, i * kBandRowOffs) so a kernel reads them without first reading
+// where they are.
 constexpr int kBandTileBins = 32;
 constexpr int kBandRowOffs = 2 * kBandTileBins + 1;  // row offsets per tile (two channels)
 struct BandTiles {
-    const int4* tiles = nullptr;  // {f0, nf, unused, n}
     // per tile, padded to `stride` entries (pads: j = -1, row 0, k 0)
     const int* jl = nullptr;  // band-freq indices j of the tile's entries, ascending
     const int* jr = nullptr;  // tile row of each entry (channel * nf + bin - f0)
@@ -40,9 +39,8 @@ struct BandTiles {
 };
 // Host construction from the band map (fi: bin*C + channel per entry j).
 struct BandTilesHost {
-    std::vector<int4> tiles;
+    int count = 0, max_n = 0, stride = 0;
     std::vector<int> jl, jr, bk, bo;
-    int max_n = 0, stride = 0;
 };
 BandTilesHost make_band_tiles(const std::vector<int>& fi, int C, int F);
 
