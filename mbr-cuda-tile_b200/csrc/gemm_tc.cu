@@ -42,13 +42,14 @@ constexpr int kStagingPerWarp = 32 * kStageRowBytes;   // 32 rows x 128 B
 // Each epilogue warp owns NSTG staging tiles, so a TMA store can still be
 // reading one while the warp fills the other; the operand ring gets what is
 // left of the 227 KB (at most 8 stages).  The 128 x 256 single-CTA tile keeps
-// one staging tile to keep 4 operand stages.
-template <int BN, int CG = 1>
+// one staging tile to keep 4 operand stages, and so do the residual GEMMs
+// (long K, a light reduce-add epilogue): their operand ring is the deeper one.
+template <int BN, int CG, int EPI>
 struct TileCfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = (BN / CG) * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int NSTG = (CG == 1 && BN == 256) ? 1 : 2;
+    static constexpr int NSTG = ((CG == 1 && BN == 256) || EPI == ops::EPI_ADD_F32) ? 1 : 2;
     static constexpr int kSmemMax = 232448 - 256 - 1024;  // opt-in maximum less barriers and alignment slack
     static constexpr int STAGES_FIT = (kSmemMax - NSTG * kEpiWarps * kStagingPerWarp) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT < 8 ? STAGES_FIT : 8;
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, int c_tma, const ops::GemmGroup* __restrict__ groups,
                    const int4* __restrict__ tiles, int ntiles, int* err, const EpiQKV qkv) {
-    using Cfg = TileCfg<BN, CG>;
+    using Cfg = TileCfg<BN, CG, EPI>;
     // CTA pair: rank 0 issues the MMAs, counts both CTAs' TMA bytes on its full
     // barriers and collects both CTAs' epilogue arrivals on its acc_empty
     const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
@@ -678,7 +679,7 @@ int num_sms() {
 template <typename T, int BN, int EPI, int CG>
 void launch_cg(const GemmLaunch& L, int* d_err, cudaStream_t st) {
     auto kern = gemm_tc_kernel<T, BN, EPI, CG>;
-    using Cfg = TileCfg<BN, CG>;
+    using Cfg = TileCfg<BN, CG, EPI>;
     static bool attr[64] = {};  // per instantiation and device
     static int sms[64] = {};
     int dev = 0;
