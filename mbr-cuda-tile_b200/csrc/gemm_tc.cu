@@ -29,12 +29,14 @@ namespace {
 
 constexpr int BM = 128, BK = 64;
 
-// Epilogue warps: warps 2..9; warp w drains TMEM lane quarter (w % 4) for the
-// column half (w - 2) / 4 of the tile.
-constexpr int kEpiWarps = 8;
-constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+// Epilogue warps: warps 2 .. 2 + EW - 1; warp w drains TMEM lane quarter
+// (w % 4), and (w - 2) / 4 numbers it among the EW / 4 warps of its quarter.
+// The GELU epilogue, whose math costs more than the tile's MMAs, gets 12
+// warps (three per quarter); the others 8.
 constexpr int kStageRowBytes = 128;                    // one swizzled 128-byte row per lane
 constexpr int kStagingPerWarp = 32 * kStageRowBytes;   // 32 rows x 128 B
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == ops::EPI_GELU_T ? 12 : 8; }
+__host__ __device__ constexpr int gemm_threads(int epi) { return 64 + 32 * epi_warps(epi); }
 
 // CG = 1: one CTA computes a 128 x BN tile.  CG = 2: a CTA pair (cluster of
 // two) computes 256 x BN with cta_group::2 MMAs; each CTA holds its 128 A rows
@@ -44,18 +46,21 @@ constexpr int kStagingPerWarp = 32 * kStageRowBytes;   // 32 rows x 128 B
 // left of the 227 KB (at most 8 stages).  The 128 x 256 single-CTA tile keeps
 // one staging tile to keep 4 operand stages, and so do the residual GEMMs
 // (long K, a light reduce-add epilogue): their operand ring is the deeper one.
+// The GELU epilogue's 12 warps each stage one 32 x 32 box (2 KB) at a time.
 template <int BN, int CG, int EPI>
 struct TileCfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = (BN / CG) * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int EW = epi_warps(EPI);
     static constexpr int NSTG = ((CG == 1 && BN == 256) || EPI == ops::EPI_ADD_F32) ? 1 : 2;
+    static constexpr int STG_WARP = EPI == ops::EPI_GELU_T ? kStagingPerWarp / 2 : NSTG * kStagingPerWarp;
     static constexpr int kSmemMax = 232448 - 256 - 1024;  // opt-in maximum less barriers and alignment slack
-    static constexpr int STAGES_FIT = (kSmemMax - NSTG * kEpiWarps * kStagingPerWarp) / STAGE_BYTES;
+    static constexpr int STAGES_FIT = (kSmemMax - EW * STG_WARP) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT < 8 ? STAGES_FIT : 8;
     static_assert(STAGES >= 3, "operand ring too shallow");
     static constexpr int STAGING_OFF = STAGES * STAGE_BYTES;  // 1024-aligned
-    static constexpr int BAR_OFF = STAGING_OFF + NSTG * kEpiWarps * kStagingPerWarp;
+    static constexpr int BAR_OFF = STAGING_OFF + EW * STG_WARP;
     static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
     static constexpr int SMEM = BAR_OFF + 256 + 1024;
 };
@@ -298,7 +303,7 @@ __device__ __forceinline__ void apply_epi(const ops::GemmGroup& g, int n0, float
 }
 
 template <typename T, int BN, int EPI, int CG>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, int c_tma, const ops::GemmGroup* __restrict__ groups,
                    const int4* __restrict__ tiles, int ntiles, int* err, const EpiQKV qkv) {
@@ -326,7 +331,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], kEpiWarps * CG);
+            mbar_init(&acc_empty[b], Cfg::EW * CG);
         }
         fence_barrier_init();
     }
@@ -430,8 +435,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else {
         const int q = warp & 3;  // TMEM lane quarter this warp may access
-        const int half = (warp - 2) >> 2;
-        constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp
+        const int half = (warp - 2) >> 2;  // this warp's number within its quarter
+        constexpr int kParts = Cfg::EW / 4;
+        constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp (8 warps)
         int tcount = 0;
         uint32_t boxes = 0;  // staged boxes this warp has issued (selects its staging tile)
         // this CTA's 128 rows of the tile
@@ -469,7 +475,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 load_rope16(qkv.cos_t + rpos * 32, qkv.sin_t + rpos * 32, half * 16, tc, ts);
                 const int DI = qkv.H * 64;
                 const int yrow = tl.y + q * 32;
-                uint8_t* stg_base = smem + Cfg::STAGING_OFF + (warp - 2) * Cfg::NSTG * kStagingPerWarp;
+                uint8_t* stg_base = smem + Cfg::STAGING_OFF + (warp - 2) * Cfg::STG_WARP;
                 const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN + half * 32;
 #pragma unroll 1
                 for (int h = 0; h < kHeads; ++h) {
@@ -497,13 +503,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         ++boxes;
                     }
                 }
+            } else if (EPI == ops::EPI_GELU_T && c_tma) {
+                // GELU output, 12 warps: the three warps of a lane quarter take
+                // the tile's 32-column chunks in turn (chunk c to warp c % 3);
+                // each chunk is one 32 x 32 box (64-byte rows, 64-byte swizzle)
+                // staged in the warp's 2 KB and stored by TMA.
+                uint8_t* stg = smem + Cfg::STAGING_OFF + (warp - 2) * Cfg::STG_WARP;
+                const int yrow = tl.y + q * 32;
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+                for (int c = half; c < BN / 32; c += kParts) {
+                    const int n0 = tl.z + c * 32;
+                    if (n0 >= g.N) break;
+                    uint32_t r[32];
+                    tmem_ld32(tbase + c * 32, r);
+                    tmem_ld_wait(r);
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                    apply_epi<EPI>(g, n0, v);
+                    if (lane == 0) bulk_wait_read_all();  // the previous box's store has read the staging
+                    __syncwarp();
+                    stage_chunk64<T>(stg, lane, v);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && yrow < g.M) {
+                        tma_store_3d(&tmC, stg, n0, c_tma == 2 ? g.c_group : yrow, c_tma == 2 ? yrow : g.c_group);
+                        bulk_commit();
+                    }
+                }
             } else if (kStoresViaTma && c_tma) {
                 // stage through this warp's 32-row tiles (NSTG of them, used in
                 // turn); one TMA store (or reduce-add into the fp32 residual)
                 // per 128-byte row group.  The TMEM load of the next 32 columns
                 // is in flight while the current ones are processed.
                 constexpr bool k16 = !(EPI == ops::EPI_F32 || EPI == ops::EPI_ADD_F32);
-                uint8_t* stg_base = smem + Cfg::STAGING_OFF + (warp - 2) * Cfg::NSTG * kStagingPerWarp;
+                uint8_t* stg_base = smem + Cfg::STAGING_OFF + (warp - 2) * Cfg::STG_WARP;
                 const int yrow = tl.y + q * 32;
                 const int ncol = g.N - (tl.z + half * (BN / 2));
                 const int nch = ncol <= 0 ? 0 : (ncol >= 32 * kChunks ? kChunks : (ncol + 31) / 32);
@@ -545,12 +580,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                 }
             } else {
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + buf * BN;
 #pragma unroll 1
-                for (int c = 0; c < kChunks; ++c) {
-                    const int n0 = tl.z + half * (BN / 2) + c * 32;
+                for (int c = half; c < BN / 32; c += kParts) {  // chunk c to warp c % kParts of the quarter
+                    const int n0 = tl.z + c * 32;
                     if (n0 >= g.N) break;
                     uint32_t r[32];
-                    tmem_ld32(taddr + c * 32, r);
+                    tmem_ld32(tbase + c * 32, r);
                     tmem_ld_wait();
                     if (rv) {
                         if constexpr (EPI == ops::EPI_QKV) {
@@ -694,7 +730,7 @@ void launch_cg(const GemmLaunch& L, int* d_err, cudaStream_t st) {
     const int grid = CG * std::min(L.ntiles, sms[dev] / CG);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kGemmThreads);
+    cfg.blockDim = dim3(gemm_threads(EPI));
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
@@ -805,7 +841,8 @@ void gemm_prepare(const GemmPlanTC& p, int dtype, std::vector<int4>& tiles, Gemm
                       "tc gemm: group does not match the output view");
         }
         bool swapped = false;
-        make_out_map(&L.tmC, p, swapped, p.epi == ops::EPI_ROPE_T ? 64 : kStageRowBytes);
+        make_out_map(&L.tmC, p, swapped,
+                     p.epi == ops::EPI_ROPE_T || p.epi == ops::EPI_GELU_T ? 64 : kStageRowBytes);
         L.c_tma = swapped ? 2 : 1;
     }
     L.ok = true;
