@@ -276,9 +276,14 @@ MBR_API int mbr_op_istft(const float* d_spec, int64_t n, int T, int hop, int64_t
  *    n * T <= 2048 (e.g. one stereo 8 s chunk, 2 x 801 frames); larger calls
  *    fail with MBR_ERR_INVALID.  Every GPU that loads the library holds this
  *    array until the process exits.
+ *  - the device that is current when the call is made must own d_spec,
+ *    d_out and the stream: the array used is the current device's copy.
  *  - the first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture.
+ *    (cudaGetSymbolAddress) with that device current, and with CUDA's lazy
+ *    module loading it may also load the library's module and reserve the
+ *    16 MiB array there, which can allocate and block.  So make that first
+ *    call in set-up code, before any real-time work and before any stream
+ *    capture.
  *  - all calls share the one array: calls whose work overlaps on the GPU
  *    (different streams without ordering, or different host threads) race.
  *    Every frame the call reads is written by the same call first, so nothing

@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdint>
 #include <memory>
 #include <string>
 #include <thread>
@@ -506,6 +507,8 @@ MBR_API int mbr_op_istft(const float* d_spec, int64_t n, int T, int hop, int64_t
         cudaStream_t st = (cudaStream_t)stream;
         int64_t lout = length > 0 ? length : (int64_t)(T - 1) * hop;
         need(lout > 0, "empty output");
+        // n * T * 2048 floats must fit in size_t
+        need(n <= (int64_t)(SIZE_MAX / sizeof(float) / 2048) / T, "n * T too large");
         float* frames = nullptr;
         MBR_CUDA(cudaMallocAsync((void**)&frames, sizeof(float) * (size_t)n * T * 2048, st));
         try {
@@ -527,11 +530,12 @@ MBR_API int mbr_op_istft_noalloc(const float* d_spec, int64_t n, int T, int hop,
         need(d_spec && d_out && n > 0 && T > 0 && hop > 0, "bad argument");
         int64_t lout = length > 0 ? length : (int64_t)(T - 1) * hop;
         need(lout > 0, "empty output");
-        if (n * (int64_t)T * 2048 > mbr::opsapi::kIstftStaticFloats)
+        // compared by division so that no product can overflow
+        const int64_t max_frames = mbr::opsapi::kIstftStaticFloats / 2048;
+        if (n > max_frames / T)
             throw mbr::Error(MBR_ERR_INVALID,
-                             "mbr_op_istft_noalloc: n * T = " + std::to_string(n * (int64_t)T) +
-                                 " frames exceeds the static scratch of " +
-                                 std::to_string(mbr::opsapi::kIstftStaticFloats / 2048) + " frames");
+                             "mbr_op_istft_noalloc: n = " + std::to_string(n) + ", T = " + std::to_string(T) +
+                                 " exceeds the static scratch of " + std::to_string(max_frames) + " frames");
         float* frames = mbr::opsapi::istft_static_scratch();
         mbr::opsapi::istft((const float2*)d_spec, n, T, hop, frames, lout, d_out, (cudaStream_t)stream);
     });

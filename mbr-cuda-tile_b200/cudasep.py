@@ -243,9 +243,24 @@ def op_istft_noalloc(spec, out, hop=441, length=-1, stream=None):
     """Allocation-free iSTFT for callers that must not allocate device memory:
     spec [n, 1025, T, 2] and the caller's out [n, lout] (float32, CUDA).  Its
     frame scratch is a fixed 16 MiB array inside the library (n * T <= 2048);
-    calls that overlap on the GPU share that array and race."""
+    calls that overlap on the GPU share that array and race.  The first call
+    on a device may load the library's module and reserve the array, so make
+    it during set-up."""
+    import torch
+
+    if spec.dim() != 4 or spec.shape[1] != 1025 or spec.shape[3] != 2:
+        raise ValueError(f"spec must be [n, 1025, T, 2], got {tuple(spec.shape)}")
     n, _, T, _ = spec.shape
-    _check(lib().mbr_op_istft_noalloc(_ptr(spec), n, T, hop, length, _ptr(out), _stream(stream)))
+    lout = length if length > 0 else (T - 1) * hop
+    for name, t in (("spec", spec), ("out", out)):
+        if t.dtype != torch.float32 or not t.is_contiguous() or not t.is_cuda:
+            raise ValueError(f"{name} must be a contiguous float32 CUDA tensor")
+    if out.device != spec.device:
+        raise ValueError("spec and out must be on the same device")
+    if tuple(out.shape) != (n, lout):
+        raise ValueError(f"out must have shape {(n, lout)}, got {tuple(out.shape)}")
+    with torch.cuda.device(spec.device):
+        _check(lib().mbr_op_istft_noalloc(_ptr(spec), n, T, hop, length, _ptr(out), _stream(stream)))
     return out
 
 
