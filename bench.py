@@ -45,24 +45,30 @@ WORKLOADS = {
     "large": dict(preset="large", dtype="fp16", seconds=600.0, overlap=2.0, chunk_batch=8,
                   desc="large: dim 512, depth 12, 16x64 heads, 2 stems; 10 min track, 11 s chunks, overlap 2, "
                        "chunk-batch 8"),
+    "pr1": dict(preset="pr1", dtype="fp32", seconds=8.0, overlap=1.0, chunk_batch=1, signal="uniform16",
+                desc="pr1: dim 192, depth 1, 8x32 heads, 1 stem, fp32; one 8 s chunk of 16-bit uniform noise "
+                     "(single-chunk path)"),
+    "r0": dict(preset="r0", dtype="bf16", seconds=30.0, overlap=2.0, chunk_batch=1,
+               desc="r0 (the reference's own shape): dim 256, depth 12, 8x64 heads, 2 stems, bf16; 30 s track, "
+                    "13 s chunks (T = 1301), overlap 2, chunk-batch 1"),
 }
+
+
+def workload_track(wl: dict, seconds: float, seed: int) -> np.ndarray:
+    """The workload's synthetic stereo track: seeded pink noise, or 16-bit
+    uniform noise in [-0.5, 0.5] for PR1."""
+    import csm_tool
+
+    if wl.get("signal") == "uniform16":
+        return csm_tool.uniform_noise16(int(round(seconds * SR)), seed)
+    return pink_noise(seconds, seed)
 
 
 def pink_noise(seconds: float, seed: int, channels: int = 2) -> np.ndarray:
     """Seeded 1/f noise, RMS -18 dBFS, quantised to 16-bit levels (k / 32768)."""
-    n = int(round(seconds * SR))
-    rng = np.random.default_rng(seed)
-    out = np.empty((channels, n), np.float32)
-    for c in range(channels):
-        w = rng.standard_normal(n)
-        X = np.fft.rfft(w)
-        f = np.arange(X.shape[0], dtype=np.float64)
-        f[0] = 1.0
-        X /= np.sqrt(f)
-        x = np.fft.irfft(X, n)
-        x *= (10 ** (-18 / 20)) / np.sqrt(np.mean(x ** 2))
-        out[c] = np.clip(np.round(x * 32768.0), -32768, 32767) / 32768.0
-    return out
+    import csm_tool
+
+    return csm_tool.pink_noise(seconds, seed, channels, SR)
 
 
 def model_flops(cfg: dict, T: int, B: int, bd: list) -> dict:
@@ -158,15 +164,19 @@ class ClockSampler:
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_sample(csm: str, cfg: dict, step_flops: float, seconds_audio: float, excerpt_s: float, reps: int = 1):
-    """Times the CPU oracle (all host threads) on a `excerpt_s` forward of the same
-    model and scales by algorithmic FLOPs to the benchmark step."""
+def cpu_sample(csm: str, cfg: dict, step_flops: float, seconds_audio: float, excerpt_s: float, reps: int = 1,
+               wl: dict | None = None, n_chunks: int = 0):
+    """Times the CPU oracle (all host threads) on one forward of the same model.
+    excerpt_s <= 0: one full chunk, and the step time is that time x the
+    track's chunk count (every chunk is the same work); otherwise an excerpt of
+    excerpt_s seconds scaled by algorithmic FLOPs to the step."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
     m = oracle.Model(csm, 1 if cfg.get("_dtype") == "fp16" else 3 if cfg.get("_dtype") == "bf16" else 0)
-    L = int(excerpt_s * SR)
-    x = pink_noise(excerpt_s, 7)[None]
+    full = excerpt_s <= 0
+    L = cfg["chunk_size"] if full else int(excerpt_s * SR)
+    x = workload_track(wl or {}, L / SR, 7)[None]
     T = L // cfg["stft_hop_length"] + 1
     fl = sum(model_flops(cfg, T, 1, band_dims(cfg)).values())
     ts = []
@@ -175,11 +185,16 @@ def cpu_sample(csm: str, cfg: dict, step_flops: float, seconds_audio: float, exc
         m.forward(x)
         ts.append(time.perf_counter() - t0)
     t = float(np.median(ts))
-    step_s = t * step_flops / fl
+    if full and n_chunks > 0:
+        step_s = t * n_chunks
+        how = (f"CPU oracle forward of one full {L / SR:g} s chunk ({T} frames, {fl / 1e12:.3f} TFLOP) in "
+               f"{t:.2f} s, times the track's {n_chunks} chunks")
+    else:
+        step_s = t * step_flops / fl
+        how = (f"CPU oracle forward of a {L / SR:g} s stereo excerpt ({T} frames, {fl / 1e12:.3f} TFLOP) "
+               f"in {t:.2f} s, scaled by algorithmic FLOPs to the {step_flops / 1e12:.2f} TFLOP step")
     return dict(value=seconds_audio / step_s, unit="audio-s/s", cores=oracle.threads(), kind="port",
-                sample=f"CPU oracle forward of a {excerpt_s:g} s stereo excerpt ({T} frames, {fl / 1e12:.3f} TFLOP) "
-                       f"in {t:.2f} s, scaled by algorithmic FLOPs to the {step_flops / 1e12:.2f} TFLOP step",
-                sample_seconds=t)
+                sample=how, sample_seconds=t)
 
 
 def dist_env():
@@ -207,7 +222,7 @@ def run_reference(args, wl):
         step_flops = step_model_flops(cfg, seconds, wl)
         vals = []
         for i in range(args.warmup + args.steps):
-            r = cpu_sample(csm, cfg, step_flops, seconds, args.cpu_excerpt)
+            r = cpu_sample(csm, cfg, step_flops, seconds, args.cpu_excerpt, wl=wl)
             if i >= args.warmup:
                 vals.append(r)
         v = float(np.mean([r["value"] for r in vals]))
@@ -228,17 +243,27 @@ def run_reference(args, wl):
     return 0
 
 
+def track_chunks(cfg, seconds, wl) -> int:
+    """Chunk count of one whole-track separation (process_chunked's plan)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    N = int(round(seconds * SR))
+    if N <= cfg["chunk_size"]:
+        return 1
+    starts, _, _, _ = oracle.chunk_plan(N, cfg["chunk_size"], -1.0 if wl["overlap"] <= 0 else wl["overlap"],
+                                        cfg["num_overlap"])
+    return len(starts)
+
+
 def step_model_flops(cfg, seconds, wl):
     """Algorithmic FLOPs of one whole-track separation (all chunks)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
-    N = int(round(seconds * SR))
-    starts, step, border, total = oracle.chunk_plan(N, cfg["chunk_size"], -1.0 if wl["overlap"] <= 0 else wl["overlap"],
-                                                    cfg["num_overlap"])
     T = cfg["chunk_size"] // cfg["stft_hop_length"] + 1
     per_chunk = sum(model_flops(cfg, T, 1, band_dims(cfg)).values())
-    return per_chunk * len(starts)
+    return per_chunk * track_chunks(cfg, seconds, wl)
 
 
 def main():
@@ -248,7 +273,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mbr_b200", choices=["mbr_b200", "reference"])
     ap.add_argument("--workload", default="std", choices=sorted(WORKLOADS))
-    ap.add_argument("--cpu-excerpt", type=float, default=1.0, help="seconds of audio in the CPU sample")
+    ap.add_argument("--cpu-excerpt", type=float, default=1.0,
+                    help="seconds of audio per reference-arm step (the reference arm times one excerpt per step)")
+    ap.add_argument("--cpu-chunk", type=float, default=0.0,
+                    help="cpu_baseline of the main line: 0 = one full chunk x the chunk count, >0 = an excerpt of "
+                         "this many seconds scaled by FLOPs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--op-sweep", action="store_true",
                     help="tensor-op sweep: achieved HBM GB/s of every stand-alone op over [B*801*60, D] activations "
@@ -288,7 +317,7 @@ def main():
     m = cudasep.Model(csm, local, wl["dtype"])
     S, C = m.info("num_stems"), m.info("channels")
     seconds = wl["seconds"] * world
-    track = pink_noise(seconds, 1234)
+    track = workload_track(wl, seconds, 1234)
     N = track.shape[1]
     # a dedicated stream (the legacy default stream cannot be graph-captured);
     # made current so that torch's copies and NCCL calls order with our work
@@ -404,9 +433,15 @@ def main():
             kind, cfg["depth"] * (cfg["time_transformer_depth"] + cfg["freq_transformer_depth"]))
         per_launch = flops_fwd[kind] / per_fwd
         achieved = per_launch / (kms / kn / 1e3) / 1e12
-        roof = {"kernel": kind, "bound": "tensor", "achieved": achieved, "peak": peaks["tflops_sustained"],
-                "unit": "TFLOP/s", "frac": achieved / peaks["tflops_sustained"], "traffic": traffic,
-                "peak_source": f"{peaks['source']} bf16_tflops_sustained (kernel timed inside a long step)",
+        if wl["dtype"] == "fp32":
+            # fp32 compute runs on the CUDA cores: nominal FMA peak
+            peak, bound = 148 * 128 * 2 * 1.965e9 / 1e12, "fp32-simt"
+            src = "nominal fp32 CUDA-core peak (148 SMs x 128 FMA/clk x 1965 MHz); no measured figure exists"
+        else:
+            peak, bound = peaks["tflops_sustained"], "tensor"
+            src = f"{peaks['source']} bf16_tflops_sustained (kernel timed inside a long step)"
+        roof = {"kernel": kind, "bound": bound, "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic, "peak_source": src,
                 "avg_launch_ms": kms / kn, "launches_profiled": kn,
                 "algorithmic_flop_per_launch": per_launch}
     breakdown = {k: {"ms": round(v[0], 3), "launches": v[1]} for k, v in prof.items() if v[1] > 0}
@@ -426,7 +461,8 @@ def main():
     }
     if rank == 0 and not args.no_cpu:
         cfg["_dtype"] = wl["dtype"]
-        line["cpu_baseline"] = cpu_sample(csm, cfg, step_model_flops(cfg, seconds, wl), seconds, args.cpu_excerpt)
+        line["cpu_baseline"] = cpu_sample(csm, cfg, step_model_flops(cfg, seconds, wl), seconds, args.cpu_chunk,
+                                          wl=wl, n_chunks=track_chunks(cfg, seconds, wl))
         line["cpu_baseline"].pop("sample_seconds", None)
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -250,6 +250,35 @@ def random_weights(cfg: dict, seed: int = 0, std: float = 0.02) -> dict:
     return t
 
 
+# ---------------------------------------------------------------------------
+# Seeded synthetic tracks (the reference's own test WAVs are private; these
+# stand in for them in benchmarks and parity fixtures)
+# ---------------------------------------------------------------------------
+def pink_noise(seconds: float, seed: int, channels: int = 2, sample_rate: int = 44100) -> np.ndarray:
+    """Seeded 1/f noise, RMS -18 dBFS, quantised to 16-bit levels (k / 32768):
+    [channels, round(seconds * sample_rate)] float32."""
+    n = int(round(seconds * sample_rate))
+    rng = np.random.default_rng(seed)
+    out = np.empty((channels, n), np.float32)
+    for c in range(channels):
+        w = rng.standard_normal(n)
+        X = np.fft.rfft(w)
+        f = np.arange(X.shape[0], dtype=np.float64)
+        f[0] = 1.0
+        X /= np.sqrt(f)
+        x = np.fft.irfft(X, n)
+        x *= (10 ** (-18 / 20)) / np.sqrt(np.mean(x ** 2))
+        out[c] = np.clip(np.round(x * 32768.0), -32768, 32767) / 32768.0
+    return out
+
+
+def uniform_noise16(n: int, seed: int, channels: int = 2, amp: float = 0.5) -> np.ndarray:
+    """Seeded uniform noise in [-amp, amp] quantised to 16-bit levels (a clip
+    stored as a 16-bit WAV and read back): [channels, n] float32."""
+    x = np.random.default_rng(seed).uniform(-amp, amp, (channels, n))
+    return (np.clip(np.round(x * 32768.0), -32768, 32767) / 32768.0).astype(np.float32)
+
+
 def make_random_csm(path: str, preset: str = "std", seed: int = 0, **overrides) -> dict:
     cfg = base_config(**{**PRESETS[preset], **overrides})
     write_csm(path, cfg, random_weights(cfg, seed))

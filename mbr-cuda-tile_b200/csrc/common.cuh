@@ -85,7 +85,12 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// GELU as the reference computes it: 0.5 x (1 + erf(x)) = x Phi(sqrt(2) x).
+// Its erf-based kernels take erf of x itself, not of x / sqrt(2)
+// (add_bias_gelu_kernel, src/mbr_cuda_tile.cu:5536-5558; gelu_erf_approx,
+// :565-583; gelu_erf_poly9_l30, src/mbr_ffn12_cutile.cu:33-66), so it is not
+// torch's nn.GELU; the outputs here follow the reference.
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x)); }
 
 // Single-instruction approximations (PTX rcp.approx / ex2.approx, ~1-2 ulp).
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -99,39 +104,43 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// Exact-erf GELU for the tensor-core epilogues: erf by Abramowitz & Stegun
-// 7.1.26, erf(z) = 1 - (a1 t + ... + a5 t^5) e^{-z^2}, t = 1 / (1 + p z),
-// |error| <= 1.5e-7.  With q = 0.5 x (1 - erf(|x| / sqrt 2)) (the tail, kept
-// as a product so it does not cancel) gelu(x) = x - q for x >= 0, q otherwise.
+// The reference's GELU 0.5 x (1 + erf(x)) (see gelu_erf) for the stand-alone
+// op: erf by Abramowitz & Stegun 7.1.26, erf(z) = 1 - (a1 t + ... + a5 t^5)
+// e^{-z^2}, t = 1 / (1 + p z), |error| <= 1.5e-7.  With q = 0.5 x (1 - erf(|x|))
+// (the tail, kept as a product so it does not cancel) gelu(x) = x - q for
+// x >= 0, q otherwise.
 __device__ __forceinline__ float gelu_as(float x) {
-    const float z = fabsf(x) * 0.70710678118654752f;
+    const float z = fabsf(x);
     const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
     float p = fmaf(1.061405429f, t, -1.453152027f);
     p = fmaf(p, t, 1.421413741f);
     p = fmaf(p, t, -0.284496736f);
     p = fmaf(p, t, 0.254829592f);
-    const float e = ex2_approx(x * x * -0.72134752044448170f);  // e^{-x^2/2} = 2^{-x^2 log2(e) / 2}
+    const float e = ex2_approx(x * x * -1.4426950408889634f);  // e^{-x^2} = 2^{-x^2 log2(e)}
     const float q = 0.5f * x * (p * t) * e;
     return x >= 0.0f ? x - q : q;
 }
 
-// GELU (exact-erf form) of N values (N even) with one exponential each:
-// gelu(x) = x - x Q(x) for x >= 0 and x Q(-x) for x < 0, where the normal tail
-// Q(t) = erfc(t / sqrt 2) / 2 is evaluated as 2^P(t).  P is a degree-7
-// least-squares Chebyshev fit of log2 Q(t) on [0, 5.5] (computed from the
-// log of the normal CDF in double precision, converted to monomial form and
-// rounded to fp32); t is clamped to 5.5, where Q < 2e-8.  Evaluated in fp32
-// the GELU error stays below 5e-7 absolute (Q within 1.1e-5 relative), under
-// a 16-bit output's rounding.  The Horner steps run on packed f32x2 pairs,
-// all N/2 chains advanced together so consecutive instructions are independent.
+// The reference's GELU 0.5 x (1 + erf(x)) (see gelu_erf) of N values (N even)
+// with one exponential each: gelu(x) = x - x Q(u) for x >= 0 and x Q(u) for
+// x < 0, u = |x|, where the tail Q(u) = erfc(u) / 2 is evaluated as 2^P(u).
+// P comes from a degree-7 least-squares Chebyshev fit of log2 of the normal
+// tail, log2(erfc(t / sqrt 2) / 2) on t in [0, 5.5] (fitted in double
+// precision from the log of the normal CDF, converted to monomial form), with
+// t = sqrt(2) u folded into the coefficients (c_i sqrt(2)^i) and rounded to
+// fp32; u is clamped to 5.5 / sqrt(2), where Q < 2e-8.  Evaluated in fp32 the
+// GELU error stays below 5e-7 absolute (Q within 1.1e-5 relative), under a
+// 16-bit output's rounding.  The Horner steps run on packed f32x2 pairs, all
+// N/2 chains advanced together so consecutive instructions are independent.
 template <int N>
 __device__ __forceinline__ void gelu_tail(float (&v)[N]) {
-    constexpr float kC[8] = {-9.999850392e-01f, -1.151344657e+00f, -4.582461119e-01f, -5.417189747e-02f,
-                             8.609841578e-03f,  -9.561956394e-04f, 6.483463949e-05f,  -1.995924322e-06f};
+    constexpr float kC[8] = {-9.999850392e-01f, -1.628247229e+00f, -9.164922238e-01f, -1.532212642e-01f,
+                             3.443936631e-02f,  -5.409059366e-03f, 5.186771159e-04f,  -2.258130597e-05f};
+    constexpr float kClamp = 3.8890873f;  // 5.5 / sqrt(2)
     float2 t[N / 2], p[N / 2];
 #pragma unroll
     for (int j = 0; j < N / 2; ++j) {
-        t[j] = make_float2(fminf(fabsf(v[2 * j]), 5.5f), fminf(fabsf(v[2 * j + 1]), 5.5f));
+        t[j] = make_float2(fminf(fabsf(v[2 * j]), kClamp), fminf(fabsf(v[2 * j + 1]), kClamp));
         p[j] = make_float2(kC[7], kC[7]);
     }
 #pragma unroll

@@ -507,7 +507,22 @@ struct Model {
     std::vector<TransW> tt, ft;
     std::vector<std::vector<std::vector<Lin>>> mask;  // [stem][band][linear]
     std::vector<double> win;
+    // Reference-bf16 mode (weight_dtype 4): activations are rounded to bf16
+    // where the reference's default --bf16 path stores them (see rb()).
+    bool ref_bf16 = false;
 };
+
+// Round v to bf16 in the reference-bf16 mode, keep it otherwise.  With --bf16
+// and no CUDASEP_* overrides the reference takes its custom bf16 path
+// (custom_bf16_path_enabled, src/mbr_cuda_tile.cu:110-112), which turns on
+// every bf16 storage switch (all_bf16_experiments_enabled /
+// remaining_bf16_experiments_enabled, :120-140): bf16 outputs of the band
+// gather (:326), RMSNorm (:147), linear layers (:182, :338), attention P.V
+// (:186), sigmoid gates and the gate merge (:139, :143), the residual stream
+// (:333; src/model_mel_band_roformer.cu:22-26), tanh and GLU inputs / outputs
+// (:317-323) and the masks of the scatter (:305); bf16 norm gammas, biases and
+// rotary tables (:337-354; src/model_mel_band_roformer.cu:28-38, :294-296).
+inline float rb(const Model& m, double v) { return m.ref_bf16 ? round_bf16((float)v) : (float)v; }
 
 Lin get_lin(const Csm& w, const std::string& p, bool bias, int round_mode) {
     Lin l;
@@ -518,9 +533,11 @@ Lin get_lin(const Csm& w, const std::string& p, bool bias, int round_mode) {
     l.w = W.f;
     if (W.dtype == 0 && round_mode == 1)
         for (auto& v : l.w) v = round_fp16(v);
-    if (W.dtype == 0 && round_mode == 3)
+    if (W.dtype == 0 && (round_mode == 3 || round_mode == 4))
         for (auto& v : l.w) v = round_bf16(v);
     if (bias) l.b = w.get(p + ".bias").f;
+    if (round_mode == 4)  // bias_bf16_enabled (src/mbr_cuda_tile.cu:337-339)
+        for (auto& v : l.b) v = round_bf16(v);
     return l;
 }
 
@@ -616,6 +633,20 @@ Model load_model(const std::string& path, int round_mode) {
                                                    std::to_string(b) + ".0." + std::to_string(2 * i),
                                                true, round_mode));
     }
+    if (round_mode == 4) {
+        // norm_gamma_bf16_enabled (src/mbr_cuda_tile.cu:341-344)
+        m.ref_bf16 = true;
+        auto rg = [](std::vector<float>& g) {
+            for (auto& v : g) v = round_bf16(v);
+        };
+        for (auto& g : m.bs_gamma) rg(g);
+        for (auto* tws : {&m.tt, &m.ft})
+            for (auto& tw : *tws) {
+                for (auto& a : tw.attn) rg(a.gamma);
+                for (auto& f : tw.ff) rg(f.gamma);
+                rg(tw.final_gamma);
+            }
+    }
     return m;
 }
 
@@ -627,12 +658,39 @@ inline double dot(const float* a, const float* b, int64_t K) {
     for (int64_t k = 0; k < K; ++k) acc += (double)a[k] * (double)b[k];
     return acc;
 }
+// GELU of the reference's bf16 FFN: erf from an odd degree-17 polynomial in
+// |x| evaluated in fp32 and clamped to [0, 1] (gelu_erf_poly9_l30_fast,
+// src/mbr_ffn12_cutile.cu:53-66; coefficients as published there).
+inline double gelu_poly9(double xd) {
+    float x = (float)xd, ax = std::fabs(x), z = ax * ax;
+    float p = ((((((((0.00000005422539767f * z - 0.000002440964777f) * z + 0.00004855766724f) * z -
+                   0.0005709642654f) * z + 0.004507274577f) * z - 0.02579950512f) * z + 0.1120213868f) * z -
+               0.3758834075f) * z + 1.128367753f);
+    float e = std::min(std::max(ax * p, 0.0f), 1.0f);
+    if (x < 0.0f) e = -e;
+    return (double)(0.5f * x * (1.0f + e));
+}
+// GELU as the reference computes it in every precision: 0.5 v (1 + erf(v)).
+// Its erf-based GELU kernels take erf of the value itself, not of v / sqrt 2
+// (add_bias_gelu_kernel, src/mbr_cuda_tile.cu:5536-5558, the fp32 path;
+// gelu_erf_approx, :565-583; gelu_erf_poly9_l30, src/mbr_ffn12_cutile.cu:33-66),
+// which is v * Phi(sqrt(2) v), not torch's nn.GELU.  The oracle follows the
+// reference.
 inline double act_apply(double v, Act a) {
-    if (a == A_GELU) return 0.5 * v * (1.0 + std::erf(v / std::sqrt(2.0)));
+    if (a == A_GELU) return 0.5 * v * (1.0 + std::erf(v));
     if (a == A_TANH) return std::tanh(v);
     return v;
 }
-void linear(const float* X, int64_t M, int64_t ldx, const Lin& L, float* Y, int64_t ldy, Act act, bool accumulate) {
+// Output rounding of one linear in the reference-bf16 mode:
+//  RB_OUT: bf16(act(acc + b)) — the bf16-output linears (src/mbr_cuda_tile.cu:6880-6885)
+//  RB_ACC: bf16(act(bf16(acc) + b)) — the FFN GEMMs round the accumulator before the
+//          bias (src/mbr_ffn12_cutile.cu:325-330, :366-371), GELU = gelu_poly9
+//  RB_TANH: bf16(tanh(bf16(acc + b))) — tanh with a bf16 input (src/mbr_cuda_tile.cu:3501-3548)
+// A residual linear (accumulate) then stores bf16(y + out).
+enum Rb { RB_OUT, RB_ACC, RB_TANH };
+void linear(const float* X, int64_t M, int64_t ldx, const Lin& L, float* Y, int64_t ldy, Act act, bool accumulate,
+            const Model* rbm = nullptr, Rb rbk = RB_OUT) {
+    if (rbm && !rbm->ref_bf16) rbm = nullptr;
     const int64_t MB = 8;
     int64_t nblk = (M + MB - 1) / MB;
     parallel_for(nblk, [&](int64_t blk) {
@@ -642,9 +700,24 @@ void linear(const float* X, int64_t M, int64_t ldx, const Lin& L, float* Y, int6
             for (int64_t m = m0; m < m1; ++m)
                 for (int n = n0; n < n1; ++n) {
                     double v = dot(X + m * ldx, L.w.data() + (size_t)n * L.in, L.in);
+                    float* y = Y + m * ldy + n;
+                    if (rbm) {
+                        double bias = L.b.empty() ? 0.0 : (double)L.b[n];
+                        double o;
+                        if (rbk == RB_ACC) {
+                            o = (double)round_bf16((float)v) + bias;
+                            o = act == A_GELU ? gelu_poly9(o) : act_apply(o, act);
+                        } else if (rbk == RB_TANH) {
+                            o = std::tanh((double)round_bf16((float)(v + bias)));
+                        } else {
+                            o = act_apply(v + bias, act);
+                        }
+                        float ob = round_bf16((float)o);
+                        *y = accumulate ? round_bf16((float)((double)*y + ob)) : ob;
+                        continue;
+                    }
                     if (!L.b.empty()) v += (double)L.b[n];
                     v = act_apply(v, act);
-                    float* y = Y + m * ldy + n;
                     *y = accumulate ? (float)((double)*y + v) : (float)v;
                 }
         }
@@ -653,7 +726,8 @@ void linear(const float* X, int64_t M, int64_t ldx, const Lin& L, float* Y, int6
 
 // rms_norm (src/mbr_cuda_tile.cu:4791-4813): x * rsqrt(sum x^2 + 1e-12) * gamma * scale
 void rms_norm(const float* X, int64_t M, int D, int64_t ldx, const std::vector<float>& g, float scale, float* Y,
-              int64_t ldy) {
+              int64_t ldy, const Model* rbm = nullptr) {
+    const bool r16 = rbm && rbm->ref_bf16;
     parallel_for((M + 63) / 64, [&](int64_t blk) {
         for (int64_t m = blk * 64; m < std::min(M, blk * 64 + 64); ++m) {
             const float* x = X + m * ldx;
@@ -661,7 +735,10 @@ void rms_norm(const float* X, int64_t M, int D, int64_t ldx, const std::vector<f
             for (int d = 0; d < D; ++d) ss += (double)x[d] * x[d];
             double inv = 1.0 / std::sqrt(ss + 1e-12);
             float* y = Y + m * ldy;
-            for (int d = 0; d < D; ++d) y[d] = (float)((double)x[d] * inv * (double)g[d] * (double)scale);
+            for (int d = 0; d < D; ++d) {
+                double v = (double)x[d] * inv * (double)g[d] * (double)scale;
+                y[d] = r16 ? round_bf16((float)v) : (float)v;
+            }
         }
     });
 }
@@ -692,15 +769,19 @@ void transformer(const Model& m, const TransW& tw, float* R, int64_t ntok, int64
     float attn_scale = 1.0f / std::sqrt((float)dh);
     std::vector<float> cs, sn;
     rotary_tables((int)L, dh, cs, sn);
+    if (m.ref_bf16) {  // rotary_freqs_bf16 (src/model_mel_band_roformer.cu:294-296)
+        for (auto& v : cs) v = round_bf16(v);
+        for (auto& v : sn) v = round_bf16(v);
+    }
     std::vector<float> xn((size_t)ntok * D), qkv((size_t)ntok * 3 * DI), gates((size_t)ntok * H),
         merged((size_t)ntok * DI), hid;
     for (size_t l = 0; l < tw.attn.size(); ++l) {
         const AttnW& a = tw.attn[l];
-        rms_norm(R, ntok, D, D, a.gamma, scale, xn.data(), D);
-        linear(xn.data(), ntok, D, a.qkv, qkv.data(), 3 * DI, A_NONE, false);
+        rms_norm(R, ntok, D, D, a.gamma, scale, xn.data(), D, &m);
+        linear(xn.data(), ntok, D, a.qkv, qkv.data(), 3 * DI, A_NONE, false);  // rounded after RoPE
         // gates = sigmoid(linear(normed)) (src/model_mel_band_roformer.cu:394-398)
         linear(xn.data(), ntok, D, a.gates, gates.data(), H, A_NONE, false);
-        for (auto& g : gates) g = (float)(1.0 / (1.0 + std::exp(-(double)g)));
+        for (auto& g : gates) g = rb(m, 1.0 / (1.0 + std::exp(-(double)g)));
         parallel_for(nseq * H, [&](int64_t sh) {
             int64_t s = sh / H;
             int h = (int)(sh % H);
@@ -713,12 +794,12 @@ void transformer(const Model& m, const TransW& tw, float* R, int64_t ntok, int64
                     double cc = cs[(size_t)pos * half + i], ss = sn[(size_t)pos * half + i];
                     double q0 = row[h * dh + 2 * i], q1 = row[h * dh + 2 * i + 1];
                     double k0 = row[DI + h * dh + 2 * i], k1 = row[DI + h * dh + 2 * i + 1];
-                    q[pos * dh + 2 * i] = q0 * cc - q1 * ss;
-                    q[pos * dh + 2 * i + 1] = q0 * ss + q1 * cc;
-                    k[pos * dh + 2 * i] = k0 * cc - k1 * ss;
-                    k[pos * dh + 2 * i + 1] = k0 * ss + k1 * cc;
-                    v[pos * dh + 2 * i] = row[2 * DI + h * dh + 2 * i];
-                    v[pos * dh + 2 * i + 1] = row[2 * DI + h * dh + 2 * i + 1];
+                    q[pos * dh + 2 * i] = rb(m, q0 * cc - q1 * ss);
+                    q[pos * dh + 2 * i + 1] = rb(m, q0 * ss + q1 * cc);
+                    k[pos * dh + 2 * i] = rb(m, k0 * cc - k1 * ss);
+                    k[pos * dh + 2 * i + 1] = rb(m, k0 * ss + k1 * cc);
+                    v[pos * dh + 2 * i] = rb(m, row[2 * DI + h * dh + 2 * i]);
+                    v[pos * dh + 2 * i + 1] = rb(m, row[2 * DI + h * dh + 2 * i + 1]);
                 }
             }
             for (int64_t i = 0; i < L; ++i) {
@@ -734,6 +815,9 @@ void transformer(const Model& m, const TransW& tw, float* R, int64_t ntok, int64
                 for (int64_t jj = 0; jj < L; ++jj) {
                     p[jj] = std::exp(p[jj] - mx);
                     sum += p[jj];
+                    // P.V takes bf16 probabilities; the row sum uses fp32 ones
+                    // (src/mbr_time_attention_cutile.cu:255-261)
+                    if (m.ref_bf16) p[jj] = round_bf16((float)p[jj]);
                 }
                 int64_t tok = token(s, i);
                 double g = gates[(size_t)tok * H + h];
@@ -741,18 +825,18 @@ void transformer(const Model& m, const TransW& tw, float* R, int64_t ntok, int64
                     double o = 0;
                     for (int64_t jj = 0; jj < L; ++jj) o += p[jj] * v[jj * dh + d];
                     // apply_gates_and_merge_heads (src/mbr_cuda_tile.cu:4603-4628)
-                    merged[(size_t)tok * DI + h * dh + d] = (float)(o / sum * g);
+                    merged[(size_t)tok * DI + h * dh + d] = rb(m, (double)rb(m, o / sum) * g);
                 }
             }
         });
-        linear(merged.data(), ntok, DI, a.out, R, D, A_NONE, true);  // residual add
+        linear(merged.data(), ntok, DI, a.out, R, D, A_NONE, true, &m);  // residual add
         const FfW& f = tw.ff[l];
-        rms_norm(R, ntok, D, D, f.gamma, scale, xn.data(), D);
+        rms_norm(R, ntok, D, D, f.gamma, scale, xn.data(), D, &m);
         hid.resize((size_t)ntok * f.l1.out);
-        linear(xn.data(), ntok, D, f.l1, hid.data(), f.l1.out, A_GELU, false);
-        linear(hid.data(), ntok, f.l1.out, f.l2, R, D, A_NONE, true);
+        linear(xn.data(), ntok, D, f.l1, hid.data(), f.l1.out, A_GELU, false, &m, RB_ACC);
+        linear(hid.data(), ntok, f.l1.out, f.l2, R, D, A_NONE, true, &m, RB_ACC);
     }
-    rms_norm(R, ntok, D, D, tw.final_gamma, scale, R, D);
+    rms_norm(R, ntok, D, D, tw.final_gamma, scale, R, D, &m);
 }
 
 struct FwdOut {
@@ -794,16 +878,17 @@ FwdOut forward(const Model& m, const float* audio, int B, int64_t L, int want_ta
             const std::complex<double>* row = spec.data() + (size_t)mt * F * C;
             float* o = xg.data() + (size_t)mt * 2 * J;
             for (int64_t jj = 0; jj < J; ++jj) {
-                o[2 * jj] = (float)row[m.fi[jj]].real();
-                o[2 * jj + 1] = (float)row[m.fi[jj]].imag();
+                o[2 * jj] = rb(m, row[m.fi[jj]].real());
+                o[2 * jj + 1] = rb(m, row[m.fi[jj]].imag());
             }
         });
         std::vector<float> nrm;
         for (int b = 0; b < NB; ++b) {
             nrm.resize((size_t)MT * m.bd[b]);
             rms_norm(xg.data() + m.boff[b], MT, m.bd[b], 2 * J, m.bs_gamma[b], std::sqrt((float)m.bd[b]), nrm.data(),
-                     m.bd[b]);
-            linear(nrm.data(), MT, m.bd[b], m.bs_lin[b], R.data() + (size_t)b * D, (int64_t)NB * D, A_NONE, false);
+                     m.bd[b], &m);
+            linear(nrm.data(), MT, m.bd[b], m.bs_lin[b], R.data() + (size_t)b * D, (int64_t)NB * D, A_NONE, false,
+                   &m);
         }
     }
     FwdOut out;
@@ -837,7 +922,9 @@ FwdOut forward(const Model& m, const float* audio, int B, int64_t L, int want_ta
             int64_t ld = (int64_t)NB * D;
             for (size_t i = 0; i < mlp.size(); ++i) {
                 h2.resize((size_t)MT * mlp[i].out);
-                linear(in, MT, ld, mlp[i], h2.data(), mlp[i].out, i + 1 < mlp.size() ? A_TANH : A_NONE, false);
+                bool last = i + 1 == mlp.size();
+                linear(in, MT, ld, mlp[i], h2.data(), mlp[i].out, last ? A_NONE : A_TANH, false, &m,
+                       last ? RB_OUT : RB_TANH);
                 h.swap(h2);
                 in = h.data();
                 ld = mlp[i].out;
@@ -846,7 +933,7 @@ FwdOut forward(const Model& m, const float* audio, int B, int64_t L, int want_ta
             for (int64_t mt = 0; mt < MT; ++mt)
                 for (int q = 0; q < bd; ++q) {
                     double a = h[(size_t)mt * 2 * bd + q], g = h[(size_t)mt * 2 * bd + bd + q];
-                    masks[((size_t)s * MT + mt) * 2 * J + m.boff[b] + q] = (float)(a / (1.0 + std::exp(-g)));
+                    masks[((size_t)s * MT + mt) * 2 * J + m.boff[b] + q] = rb(m, a / (1.0 + std::exp(-g)));
                 }
         }
     }

@@ -46,7 +46,10 @@ int orc_istft(const float* spec, int64_t n_sig, int64_t T, int n_fft, int hop,
 
 /* Model handle: loads a .csm file.  weight_dtype: 0 = use weights as stored,
  * 1 = round every 2-D fp32 tensor to fp16, 3 = round to bf16 (this restates
- * ModelWeights::convert_linear_weights_to_{fp16,bf16}, src/weights.cu:511-540). */
+ * ModelWeights::convert_linear_weights_to_{fp16,bf16}, src/weights.cu:511-540),
+ * 4 = the reference's default --bf16 path: weights, biases, norm gammas and
+ * rotary tables in bf16, and every activation rounded to bf16 where that path
+ * stores it (GEMM accumulators stay fp32 / fp64). */
 void* orc_model_load(const char* csm_path, int weight_dtype);
 void orc_model_free(void* model);
 /* Query: 0 dim, 1 depth, 2 num_stems, 3 audio_channels, 4 num_bands,

@@ -2,6 +2,15 @@
 import numpy as np
 
 
+def gelu_ref(x):
+    """The reference's GELU, 0.5 x (1 + erf(x)) (erf of x itself, not of x/sqrt2:
+    add_bias_gelu_kernel, src/mbr_cuda_tile.cu:5536-5558), in float64."""
+    from scipy.special import erf
+
+    x = np.asarray(x, np.float64)
+    return 0.5 * x * (1.0 + erf(x))
+
+
 def rel_max_err(ref: np.ndarray, got: np.ndarray) -> float:
     """max |got - ref| / max |ref| (the fp32 parity measure; bar 1e-4)."""
     ref = np.asarray(ref, np.float64)

@@ -1,15 +1,18 @@
-"""The GEMM epilogue's GELU: x*Phi(x) with the normal tail Q(t) = erfc(t/sqrt2)/2
-evaluated as 2^P(t) for a degree-7 polynomial P (csrc/common.cuh, gelu_tail).
+"""The GEMM epilogue's GELU, the reference's 0.5 x (1 + erf(x)), with the tail
+Q(u) = erfc(u)/2 evaluated as 2^P(u) for a degree-7 polynomial P
+(csrc/common.cuh, gelu_tail).
 
-The coefficients are read from the source and evaluated here the way the
-kernel does (fp32 Horner steps on t = min(|x|, 5.5), then 2^P), so the error
-bound quoted in the source is checked against scipy's erf on the CPU."""
+The coefficients and the clamp are read from the source and evaluated here the
+way the kernel does (fp32 Horner steps on u = min(|x|, clamp), then 2^P), so
+the error bound quoted in the source is checked against scipy's erf on the
+CPU."""
 import os
 import re
 
 import numpy as np
 
 from conftest import PKG
+from metrics import gelu_ref
 
 
 def _coefficients():
@@ -17,12 +20,15 @@ def _coefficients():
     body = src[src.index("void gelu_tail(") :]
     m = re.search(r"kC\[8\]\s*=\s*\{([^}]*)\}", body)
     assert m, "gelu_tail coefficients not found"
-    return np.array([float(v.strip().rstrip("f")) for v in m.group(1).split(",")], np.float32)
+    k = re.search(r"kClamp\s*=\s*([0-9.eE+-]+)f", body)
+    assert k, "gelu_tail clamp not found"
+    return (np.array([float(v.strip().rstrip("f")) for v in m.group(1).split(",")], np.float32),
+            np.float32(float(k.group(1))))
 
 
-def _gelu_tail(x, c):
+def _gelu_tail(x, c, clamp):
     x = x.astype(np.float32)
-    t = np.minimum(np.abs(x), np.float32(5.5))
+    t = np.minimum(np.abs(x), clamp)
     p = np.full_like(t, c[-1])
     for ci in c[-2::-1]:
         p = (p * t + ci).astype(np.float32)  # one rounding per step, as fma.rn.f32x2 gives
@@ -32,13 +38,11 @@ def _gelu_tail(x, c):
 
 
 def test_gelu_tail_matches_erf_gelu():
-    from scipy.special import erf
-
-    c = _coefficients()
+    c, clamp = _coefficients()
     assert c.shape == (8,)
     x = np.concatenate([np.linspace(-12, 12, 400001), np.linspace(-1e-3, 1e-3, 2001)]).astype(np.float32)
-    ref = 0.5 * x.astype(np.float64) * (1 + erf(x.astype(np.float64) / np.sqrt(2)))
-    got = _gelu_tail(x, c).astype(np.float64)
+    ref = gelu_ref(x)
+    got = _gelu_tail(x, c, clamp).astype(np.float64)
     err = np.abs(got - ref)
     # the bound the source states (below 5e-7 absolute over the whole real line),
     # plus the fp32 rounding of results of magnitude up to 12

@@ -11,6 +11,8 @@ and 1e-6 relative (scatter) against numpy on the checkpoint's band map.
 import numpy as np
 import pytest
 
+from metrics import gelu_ref
+
 pytestmark = pytest.mark.gpu
 
 T = 801
@@ -60,9 +62,8 @@ def test_rms_norm_add_gelu(torch_cuda, dtype, D):
     ref = xr / np.sqrt((xr ** 2).sum(-1, keepdims=True) + 1e-12) * gamma.double().numpy() * scale
     _close(cudasep.op_rms_norm(xd, gd, scale), ref, dtype, "rms_norm")
     _close(cudasep.op_add(xd, yd), xr + y.double().numpy(), dtype, "add")
-    from scipy.special import erf
 
-    _close(cudasep.op_gelu(xd), 0.5 * xr * (1 + erf(xr / np.sqrt(2))), dtype, "gelu")
+    _close(cudasep.op_gelu(xd), gelu_ref(xr), dtype, "gelu")
 
 
 @pytest.mark.parametrize("dtype", ["fp32", "fp16", "bf16"])
@@ -80,9 +81,8 @@ def test_ragged_rows(torch_cuda, dtype, rows, D):
     ref = xr / np.sqrt((xr ** 2).sum(-1, keepdims=True) + 1e-12) * gamma.double().numpy() * 3.0
     _close(cudasep.op_rms_norm(xd, gd, 3.0), ref, dtype, "rms_norm")
     _close(cudasep.op_add(xd, yd), xr + y.double().numpy(), dtype, "add")
-    from scipy.special import erf
 
-    _close(cudasep.op_gelu(xd), 0.5 * xr * (1 + erf(xr / np.sqrt(2))), dtype, "gelu")
+    _close(cudasep.op_gelu(xd), gelu_ref(xr), dtype, "gelu")
 
 
 @pytest.mark.parametrize("dtype", ["fp32", "fp16", "bf16"])
@@ -295,9 +295,8 @@ def test_linear_op(torch_cuda, dtype, rows, fin, fout, act):
     xd, wd = x.double().numpy(), w.double().numpy()
     pre = xd @ wd.T + b.double().numpy()
     if act == 1:
-        from scipy.special import erf
 
-        ref = 0.5 * pre * (1 + erf(pre / np.sqrt(2)))
+        ref = gelu_ref(pre)
     elif act == 2:
         ref = np.tanh(pre)
     else:

@@ -1,9 +1,14 @@
 """GPU parity of the CUDA forward and chunk driver against the CPU oracle.
 
 Tolerances (the bar of the port): fp32 compute max relative error
-<= 1e-4 (max |got - ref| / max |ref|); fp16 / bf16 compute stem SNR against the
-oracle >= 60 dB / >= 40 dB respectively (see the per-test constants).  All
-calls go through the C ABI (cudasep -> libmbr_b200.so).
+<= 1e-4 (max |got - ref| / max |ref|); fp16 compute stem SNR against the oracle
+>= 60 dB.  bf16: the reference's own bf16 path rounds its activations to bf16
+and sits ~42 dB from the exact forward (the oracle's reference-bf16 mode), so
+the bar is that this bf16 forward is at least as close to the exact forward as
+that scheme, and >= 40 dB from the reference-bf16 output.  Two bf16 paths of
+this library that round at the same points and differ only in summation order
+must agree to >= 40 dB.  All calls go through the C ABI (cudasep ->
+libmbr_b200.so).
 """
 import numpy as np
 import pytest
@@ -14,7 +19,8 @@ pytestmark = pytest.mark.gpu
 
 FP32_TOL = 1e-4
 FP16_SNR_DB = 60.0
-BF16_SNR_DB = 40.0
+BF16_PAIR_SNR_DB = 40.0
+BF16_VS_REF_BF16_DB = 40.0
 
 
 @pytest.fixture(scope="module")
@@ -79,8 +85,8 @@ def test_taps_fp32_match_oracle(torch_cuda, make_csm):
     assert rel_max_err(ref, got) <= FP32_TOL
 
 
-@pytest.mark.parametrize("dtype,wdt,bar", [("fp16", 1, FP16_SNR_DB), ("bf16", 3, BF16_SNR_DB)])
-def test_forward_16bit_snr(torch_cuda, make_csm, dtype, wdt, bar):
+@pytest.mark.parametrize("dtype,wdt", [("fp16", 1), ("bf16", 3)])
+def test_forward_16bit_snr(torch_cuda, make_csm, dtype, wdt):
     torch = torch_cuda
     path = make_csm("tiny2", seed=5)
     orc = _oracle(path, wdt)
@@ -90,7 +96,13 @@ def test_forward_16bit_snr(torch_cuda, make_csm, dtype, wdt, bar):
     got = m.forward(torch.from_numpy(x).cuda()).cpu().numpy()
     s = snr_db(ref, got)
     print(f"{dtype} forward SNR vs oracle: {s:.2f} dB")
-    assert s >= bar, f"{dtype} SNR {s:.2f} dB < {bar}"
+    if dtype == "fp16":
+        assert s >= FP16_SNR_DB, f"fp16 SNR {s:.2f} dB < {FP16_SNR_DB}"
+    else:
+        refb = _oracle(path, 4).forward(x)  # the reference's bf16 rounding scheme
+        s_scheme, s_refb = snr_db(ref, refb), snr_db(refb, got)
+        print(f"bf16: reference-bf16 scheme vs exact {s_scheme:.2f} dB, this forward vs it {s_refb:.2f} dB")
+        assert s >= s_scheme and s_refb >= BF16_VS_REF_BF16_DB
 
 
 @pytest.mark.parametrize("overlap,chunk_batch", [(-1.0, 1), (4.0, 3), (0.5, 2)])
@@ -156,7 +168,7 @@ def test_tensor_core_gemm_matches_cuda_core_gemm(torch_cuda, make_csm, preset, d
     b = m.forward(x).cpu().numpy()
     s = snr_db(b, a)
     print(f"{preset}/{dtype}: tcgen05 vs CUDA-core GEMM forward SNR {s:.1f} dB")
-    assert s >= FP16_SNR_DB if dtype == "fp16" else s >= BF16_SNR_DB
+    assert s >= FP16_SNR_DB if dtype == "fp16" else s >= BF16_PAIR_SNR_DB
 
 
 @pytest.mark.parametrize("preset,dtype,L", [("tiny2", "fp16", 44100), ("mid", "bf16", 100000)])
@@ -212,7 +224,7 @@ def test_tensor_core_attention_matches_cuda_core(torch_cuda, make_csm, preset, d
     b = m.forward(x).cpu().numpy()
     s = snr_db(b, a)
     print(f"{preset}/{dtype}/L={L}: tcgen05 vs CUDA-core attention forward SNR {s:.1f} dB")
-    assert s >= (FP16_SNR_DB if dtype == "fp16" else BF16_SNR_DB)
+    assert s >= (FP16_SNR_DB if dtype == "fp16" else BF16_PAIR_SNR_DB)
 
 
 def test_separate_two_gpus_matches_one(torch_cuda, make_csm):

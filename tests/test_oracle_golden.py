@@ -124,3 +124,21 @@ def identity_csm(make_csm, preset, **ov):
                 t[p + ".bias"] = bias
         csm_tool.write_csm(out, cfg, t)
     return out
+
+
+def test_oracle_reference_bf16_mode(make_csm):
+    """weight_dtype 4 (the reference's default --bf16 path: activations rounded
+    to bf16 where that path stores them) stays deterministic and differs from
+    the fp32-storage oracle on the same bf16 weights by bf16-scale rounding
+    only: an SNR between 30 and 55 dB (one bf16 rounding is ~-52 dB)."""
+    import oracle
+    from metrics import snr_db
+
+    path = make_csm("tiny", seed=31)
+    x = np.random.default_rng(2).uniform(-0.5, 0.5, (1, 2, 44100)).astype(np.float32)
+    exact = oracle.Model(path, 3).forward(x)
+    m4 = oracle.Model(path, 4)
+    a, b = m4.forward(x), m4.forward(x)
+    assert np.array_equal(a, b) and np.isfinite(a).all()
+    s = snr_db(exact, a)
+    assert 30.0 <= s <= 55.0, s
