@@ -273,6 +273,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mbr_b200", choices=["mbr_b200", "reference"])
     ap.add_argument("--workload", default="std", choices=sorted(WORKLOADS))
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="N > 1: weak = every rank adds the workload's track length; strong = one track of the "
+                         "workload's length split over the ranks")
     ap.add_argument("--cpu-excerpt", type=float, default=1.0,
                     help="seconds of audio per reference-arm step (the reference arm times one excerpt per step)")
     ap.add_argument("--cpu-chunk", type=float, default=0.0,
@@ -316,7 +319,7 @@ def main():
     csm_tool.write_csm(csm, cfg, csm_tool.random_weights(cfg, 0))
     m = cudasep.Model(csm, local, wl["dtype"])
     S, C = m.info("num_stems"), m.info("channels")
-    seconds = wl["seconds"] * world
+    seconds = wl["seconds"] * (world if args.scaling == "weak" else 1)
     track = workload_track(wl, seconds, 1234)
     N = track.shape[1]
     # a dedicated stream (the legacy default stream cannot be graph-captured);
@@ -324,13 +327,18 @@ def main():
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     d_track = torch.from_numpy(track).to(dev)
-    d_out = torch.empty((S, C, N), dtype=torch.float32, device=dev)
 
     if world == 1:
+        d_out = torch.empty((S, C, N), dtype=torch.float32, device=dev)
+
         def step():
             m.separate_device(d_track, wl["overlap"], wl["chunk_batch"], out=d_out, stream=stream)
     else:
+        # this rank's chunk range, the track window it reads, its own output range
         info = m.shard_info(N, wl["overlap"], rank, world)
+        w_lo, w_hi = m.shard_window(N, wl["overlap"], rank, world)
+        d_win = d_track[:, w_lo:w_hi].contiguous()
+        del d_track
         span = info["hi"] - info["lo"]
         acc = torch.empty((S * C, span), dtype=torch.float32, device=dev)
         wsum = torch.empty((span,), dtype=torch.float32, device=dev)
@@ -339,17 +347,33 @@ def main():
         racc = torch.empty((S * C, max(rlen, 1)), dtype=torch.float32, device=dev)
         rws = torch.empty((max(rlen, 1),), dtype=torch.float32, device=dev)
         soff = info["send_lo"] - info["lo"]
+        sacc = torch.empty((S * C, span - soff), dtype=torch.float32, device=dev)
+        sws = torch.empty((span - soff,), dtype=torch.float32, device=dev)
+        # the tail a rank sends is disjoint from the head it receives when every
+        # rank holds at least chunk/step chunks: then all boundaries move at once
+        plans = [m.shard_info(N, wl["overlap"], r, world) for r in range(world)]
+        assert all(plans[r - 1]["hi"] <= plans[r]["send_lo"] for r in range(1, world - 1)), \
+            "too few chunks per rank for a concurrent boundary exchange"
+        wout = info["out_hi"] - info["out_lo"]
+        d_own = torch.empty((S * C, max(wout, 1)), dtype=torch.float32, device=dev)
 
         def step():
-            m.shard_run(d_track, N, wl["overlap"], wl["chunk_batch"], rank, world, acc, wsum, stream=stream)
+            m.shard_run_window(d_win, w_lo, N, wl["overlap"], wl["chunk_batch"], rank, world, acc, wsum,
+                               stream=stream)
+            ops = []
             if rank > 0:
-                dist.recv(racc, rank - 1)
-                dist.recv(rws, rank - 1)
-                m.shard_add_boundary(N, wl["overlap"], rank, world, acc, wsum, racc, rws, rlen, stream=stream)
+                ops += [dist.P2POp(dist.irecv, racc, rank - 1), dist.P2POp(dist.irecv, rws, rank - 1)]
             if rank < world - 1:
-                dist.send(acc[:, soff:].contiguous(), rank + 1)
-                dist.send(wsum[soff:].contiguous(), rank + 1)
-            m.shard_finalize(N, wl["overlap"], rank, world, acc, wsum, d_out.view(S * C, N), N, stream=stream)
+                sacc.copy_(acc[:, soff:])
+                sws.copy_(wsum[soff:])
+                ops += [dist.P2POp(dist.isend, sacc, rank + 1), dist.P2POp(dist.isend, sws, rank + 1)]
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+            if rank > 0:
+                m.shard_add_boundary(N, wl["overlap"], rank, world, acc, wsum, racc, rws, rlen, stream=stream)
+            if wout > 0:
+                m.shard_finalize(N, wl["overlap"], rank, world, acc, wsum, d_own, wout, stream=stream,
+                                 out_col0=info["out_lo"])
 
     for _ in range(args.warmup):
         step()
@@ -380,6 +404,7 @@ def main():
     h_in = torch.from_numpy(track).pin_memory()
     h_out = torch.empty((S, C, N), dtype=torch.float32).pin_memory()
     h_in_np, h_out_np = h_in.numpy(), h_out.numpy()
+    check = None
     if world == 1:
         m.separate(h_in_np, wl["overlap"], wl["chunk_batch"], out=h_out_np)
         t0 = time.perf_counter()
@@ -388,11 +413,13 @@ def main():
         e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
         h2d, d2h = C * N * 4, S * C * N * 4
     else:
+        h_win = h_in[:, w_lo:w_hi].contiguous().pin_memory()  # the rank's input window
+        h_own = torch.empty((S * C, max(wout, 1)), dtype=torch.float32).pin_memory()
+
         def e2e_step():
-            d_track.copy_(h_in, non_blocking=True)
+            d_win.copy_(h_win, non_blocking=True)
             step()
-            lo, hi = info["out_lo"], info["out_hi"]
-            h_out.view(S * C, N)[:, lo:hi].copy_(d_out.view(S * C, N)[:, lo:hi], non_blocking=False)
+            h_own.copy_(d_own, non_blocking=False)
         e2e_step()
         dist.barrier()
         torch.cuda.synchronize(dev)
@@ -404,11 +431,30 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-        h2d, d2h = C * N * 4, S * C * (info["out_hi"] - info["out_lo"]) * 4
+        h2d, d2h = C * (w_hi - w_lo) * 4, S * C * wout * 4
+        # correctness: rank 0 assembles every rank's own range and compares it
+        # with a one-GPU separation of the same track
+        wmax = torch.tensor([wout], device=dev)
+        dist.all_reduce(wmax, op=dist.ReduceOp.MAX)
+        pad = torch.zeros((S * C, int(wmax.item())), dtype=torch.float32, device=dev)
+        pad[:, :wout] = d_own[:, :wout]
+        parts = [torch.empty_like(pad) for _ in range(world)]
+        dist.all_gather(parts, pad)
+        check = None
+        if rank == 0:
+            one = m.separate_device(torch.from_numpy(track).to(dev), wl["overlap"], wl["chunk_batch"],
+                                    stream=stream).view(S * C, N)
+            torch.cuda.synchronize(dev)
+            err = 0.0
+            for r, pr in enumerate(plans):
+                w = pr["out_hi"] - pr["out_lo"]
+                err = max(err, float((parts[r][:, :w] - one[:, pr["out_lo"]:pr["out_hi"]]).abs().max()))
+            check = {"max_abs_err_vs_one_gpu": err, "max_abs_one_gpu": float(one.abs().max())}
+            del one
     e2e = {"value": seconds / (e2e_ms / 1e3), "unit": "audio-s/s", "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
-           "path": "mbr_separate (host track in, stems out)" if world == 1 else
-                   "H2D track + mbr_shard_* + NCCL boundary + D2H of the own range, per rank"}
+           "path": "mbr_separate (host track in, stems out; copies overlapped with the chunks)" if world == 1 else
+                   "H2D of the rank's track window + mbr_shard_* + NCCL boundary exchange + D2H of the own range"}
 
     # ---- roofline of the dominant kernel class (one profiled step) ----
     peaks = load_peaks()
@@ -448,15 +494,22 @@ def main():
 
     line = {
         "metric": "audio-seconds/sec", "value": value, "unit": "audio-s/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "vs_baseline": None, "dtype": "f16" if wl["dtype"] == "fp16" else wl["dtype"].replace("fp", "f"),
         "data": "synthetic: seeded pink noise (1/f, -18 dBFS RMS, 16-bit levels), random-init weights "
                 "N(0,0.02), gamma=1",
-        "config": {"workload": wl["desc"] + (f"; {world} ranks x {wl['seconds']:g} s (weak scaling)" if world > 1 else ""),
+        "config": {"workload": wl["desc"] + (
+                       "" if world == 1 else f"; {world} ranks x {wl['seconds']:g} s (weak scaling)"
+                       if args.scaling == "weak" else f"; one {wl['seconds']:g} s track over {world} ranks"),
                    "track_seconds": seconds, "parallelism": f"chunk-range shards x{world}",
+                   "chunks": track_chunks(cfg, seconds, wl),
+                   "max_chunks_per_rank": (max(pr["c1"] - pr["c0"] for pr in plans) if world > 1
+                                           else track_chunks(cfg, seconds, wl)),
                    "l2": "no flush: the per-step working set (activations ~1 GB, mask-estimator weights "
                          "~400 MB) exceeds the 126 MB L2"},
         "roofline": roof, "profile_ms_per_step": breakdown, "e2e": e2e, "gpu_launches": int(launches),
+        "scaling": args.scaling if world > 1 else "weak",
+        "multi_gpu_check": check if world > 1 else None,
         "clocks": clk.summary(),
     }
     if rank == 0 and not args.no_cpu:

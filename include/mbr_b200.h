@@ -111,11 +111,18 @@ MBR_API int mbr_separate_device(mbr_handle* h, const float* d_track, int64_t N, 
                                 float* d_out, void* stream);
 
 /* Whole-track separation from host memory (copies in, separates, copies out,
- * synchronises): h_track [C][N] -> h_out [S][C][N].  With n_gpus > 1 the
- * chunk list is split into contiguous ranges run on devices
- * device .. device+n_gpus-1 in parallel; only the overlap-add boundary is
- * exchanged (peer copies).  Replaces run_inference (src/inference_app.cpp:313-357)
- * without the WAV file I/O. */
+ * synchronises): h_track [C][N] -> h_out [S][C][N].  On one GPU the copies
+ * overlap the chunks: each chunk batch's new input samples are uploaded on a
+ * copy stream ahead of it, and every output range that no later chunk
+ * touches is normalised and downloaded while later batches run (pinned host
+ * buffers make these copies asynchronous).  With n_gpus > 1 the chunk list is
+ * split into contiguous ranges run on devices device .. device+n_gpus-1 in
+ * parallel; each device receives only its input window and holds only its
+ * own output range, and only the overlap-add boundaries are exchanged (peer
+ * copies, all at once when every range holds enough chunks that no boundary
+ * depends on another).  Replaces run_inference
+ * (src/inference_app.cpp:313-357; its chunk-batch loop :92-128) without the
+ * WAV file I/O. */
 MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float overlap, int chunk_batch, int n_gpus,
                          float* h_out);
 
@@ -134,6 +141,22 @@ MBR_API int mbr_plan_shard(int64_t N, int chunk_size, float overlap, int default
 /* Runs the shard's chunks: d_acc [S*C][hi-lo], d_wsum [hi-lo] (overwritten). */
 MBR_API int mbr_shard_run(mbr_handle* h, const float* d_track, int64_t N, float overlap, int chunk_batch, int rank,
                           int world, float* d_acc, float* d_wsum, void* stream);
+/* The track samples [*in_lo, *in_hi) a shard reads (its chunks through the
+ * reflect padding), so that a rank uploads only that window.  The
+ * reference's process_chunked reads the whole padded track
+ * (src/inference_app.cpp:78-89); this is its per-rank restriction. */
+MBR_API int mbr_shard_window(mbr_handle* h, int64_t N, float overlap, int rank, int world, int64_t* in_lo,
+                             int64_t* in_hi);
+/* mbr_shard_window without a handle or GPU (host arithmetic only), for the
+ * checkpoint's chunk_size and default num_overlap. */
+MBR_API int mbr_plan_shard_window(int64_t N, int chunk_size, float overlap, int default_overlap, int rank, int world,
+                                  int64_t* in_lo, int64_t* in_hi);
+/* mbr_shard_run over a track window: d_window [C][win_len] holds track
+ * samples [win_lo, win_lo + win_len) of each channel and must cover the
+ * shard's mbr_shard_window. */
+MBR_API int mbr_shard_run_window(mbr_handle* h, const float* d_window, int64_t win_lo, int64_t win_len, int64_t N,
+                                 float overlap, int chunk_batch, int rank, int world, float* d_acc, float* d_wsum,
+                                 void* stream);
 /* Adds the previous rank's boundary (d_recv_acc [S*C][recv_len],
  * d_recv_wsum [recv_len], recv_len = previous hi - this lo) into the
  * shard's accumulators (call before sending this shard's own boundary). */
@@ -141,7 +164,9 @@ MBR_API int mbr_shard_add_boundary(mbr_handle* h, int64_t N, float overlap, int 
                                    float* d_wsum, const float* d_recv_acc, const float* d_recv_wsum,
                                    int64_t recv_len, void* stream);
 /* Normalises the shard's own range into d_out [S*C][out_stride] at columns
- * [out_lo, out_hi) (track coordinates). */
+ * [out_lo, out_hi) (track coordinates); only those columns are written, so a
+ * caller holding just its own range passes its buffer's address minus out_lo
+ * columns with out_stride = out_hi - out_lo. */
 MBR_API int mbr_shard_finalize(mbr_handle* h, int64_t N, float overlap, int rank, int world, float* d_acc,
                                float* d_wsum, float* d_out, int64_t out_stride, void* stream);
 

@@ -23,6 +23,7 @@ struct mbr_handle {
     std::unique_ptr<mbr::MelBandRoformer> model;
     std::unique_ptr<mbr::Separator> sep;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy_stream = nullptr;  // host <-> device copies of mbr_separate
     // host-path buffers
     float* d_track = nullptr;
     float* d_out = nullptr;
@@ -36,6 +37,7 @@ struct mbr_handle {
         if (d_track) cudaFree(d_track);
         if (d_out) cudaFree(d_out);
         if (stream) cudaStreamDestroy(stream);
+        if (copy_stream) cudaStreamDestroy(copy_stream);
         sep.reset();
         model.reset();
     }
@@ -80,6 +82,7 @@ std::unique_ptr<mbr_handle> make_handle(const char* path, int device, int dtype)
     h->model = std::make_unique<mbr::MelBandRoformer>(w, device, dtype);
     h->sep = std::make_unique<mbr::Separator>(*h->model);
     MBR_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    MBR_CUDA(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking));
     return h;
 }
 
@@ -179,12 +182,9 @@ MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float o
         mbr::ChunkPlan plan = mbr::make_chunk_plan(N, cfg.chunk_size, overlap, cfg.num_overlap);
         int world = (plan.single || (int)plan.starts.size() < n_gpus) ? 1 : n_gpus;
         if (world == 1) {
+            // copies overlapped with the chunks (Separator::separate_host)
             MBR_CUDA(cudaSetDevice(h->device));
-            float* dt = ensure(h->d_track, h->track_cap, sizeof(float) * C * N);
-            float* dout = ensure(h->d_out, h->out_cap, sizeof(float) * SC * N);
-            MBR_CUDA(cudaMemcpyAsync(dt, h_track, sizeof(float) * C * N, cudaMemcpyHostToDevice, h->stream));
-            h->sep->separate(dt, N, overlap, chunk_batch, dout, h->stream);
-            MBR_CUDA(cudaMemcpyAsync(h_out, dout, sizeof(float) * SC * N, cudaMemcpyDeviceToHost, h->stream));
+            h->sep->separate_host(h_track, N, overlap, chunk_batch, h_out, h->stream, h->copy_stream);
             MBR_CUDA(cudaStreamSynchronize(h->stream));
             h->launches = h->sep->last_launches();
             h->model->check_device_error();
@@ -196,21 +196,33 @@ MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float o
         std::vector<mbr_handle*> hs{h};
         for (auto& p : h->peers) hs.push_back(p.get());
         std::vector<mbr::Shard> sh(world);
-        std::vector<float*> acc(world), ws(world);
+        std::vector<int64_t> rlen(world, 0);
+        for (int r = 0; r < world; ++r) {
+            sh[r] = mbr::make_shard(plan, r, world);
+            if (r > 0) rlen[r] = sh[r - 1].hi - sh[r - 1].send_lo;
+        }
+        // per-rank device layout: accumulators [SC][span], weight sum [span],
+        // received boundary [SC + 1][rlen], own output range [SC][out width];
+        // the track buffer holds only the rank's input window
+        std::vector<float*> acc(world), ws(world), racc(world), dout(world);
         std::vector<std::string> errs(world);
-        for (int r = 0; r < world; ++r) sh[r] = mbr::make_shard(plan, r, world);
         auto run = [&](int r) {
             try {
                 mbr_handle* x = hs[r];
                 MBR_CUDA(cudaSetDevice(x->device));
-                int64_t span = sh[r].hi - sh[r].lo;
-                float* dt = ensure(x->d_track, x->track_cap, sizeof(float) * C * N);
-                // accumulators followed by the receive buffer for the previous boundary
-                float* buf = ensure(x->d_out, x->out_cap, sizeof(float) * ((size_t)(SC + 1) * span * 2 + SC * N));
+                const int64_t span = sh[r].hi - sh[r].lo, win = sh[r].in_hi - sh[r].in_lo;
+                const int64_t wout = sh[r].out_hi - sh[r].out_lo;
+                float* dt = ensure(x->d_track, x->track_cap, sizeof(float) * C * win);
+                float* buf = ensure(x->d_out, x->out_cap,
+                                    sizeof(float) * ((size_t)(SC + 1) * span + (size_t)(SC + 1) * rlen[r] +
+                                                     (size_t)SC * wout));
                 acc[r] = buf;
                 ws[r] = buf + (size_t)SC * span;
-                MBR_CUDA(cudaMemcpyAsync(dt, h_track, sizeof(float) * C * N, cudaMemcpyHostToDevice, x->stream));
-                x->sep->run_shard(plan, sh[r], dt, chunk_batch, acc[r], ws[r], x->stream);
+                racc[r] = ws[r] + span;
+                dout[r] = racc[r] + (size_t)(SC + 1) * rlen[r];
+                MBR_CUDA(cudaMemcpy2DAsync(dt, sizeof(float) * win, h_track + sh[r].in_lo, sizeof(float) * N,
+                                           sizeof(float) * win, C, cudaMemcpyHostToDevice, x->stream));
+                x->sep->run_shard(plan, sh[r], dt, sh[r].in_lo, win, chunk_batch, acc[r], ws[r], x->stream);
                 MBR_CUDA(cudaStreamSynchronize(x->stream));
             } catch (const std::exception& e) {
                 errs[r] = e.what();
@@ -221,37 +233,36 @@ MBR_API int mbr_separate(mbr_handle* h, const float* h_track, int64_t N, float o
         for (auto& t : th) t.join();
         for (auto& e : errs)
             if (!e.empty()) throw mbr::Error(MBR_ERR_CUDA, e);
-        // boundary chain: rank r-1's tail [send_lo, hi) is added into rank r
+        // Boundary exchange: rank r-1's tail [send_lo, hi) is added into rank
+        // r's head.  When no rank's tail overlaps the head it receives (every
+        // rank holds enough chunks), the tails are final after run_shard and all
+        // exchanges go at once; otherwise they run as a chain in rank order.
+        bool independent = true;
+        for (int r = 1; r + 1 < world; ++r) independent = independent && sh[r - 1].hi <= sh[r].send_lo;
         for (int r = 1; r < world; ++r) {
             mbr_handle* x = hs[r];
-            int64_t rlen = sh[r - 1].hi - sh[r - 1].send_lo;
-            int64_t off = sh[r - 1].send_lo - sh[r - 1].lo, span_prev = sh[r - 1].hi - sh[r - 1].lo;
-            int64_t span = sh[r].hi - sh[r].lo;
-            float* racc = ws[r] + span;  // receive area after the accumulators
-            float* rws = racc + (size_t)SC * rlen;
+            const int64_t off = sh[r - 1].send_lo - sh[r - 1].lo, span_prev = sh[r - 1].hi - sh[r - 1].lo;
+            float* rws = racc[r] + (size_t)SC * rlen[r];
             MBR_CUDA(cudaSetDevice(x->device));
             for (int o = 0; o < SC; ++o)
-                MBR_CUDA(cudaMemcpyPeerAsync(racc + (size_t)o * rlen, x->device,
+                MBR_CUDA(cudaMemcpyPeerAsync(racc[r] + (size_t)o * rlen[r], x->device,
                                              acc[r - 1] + (size_t)o * span_prev + off, hs[r - 1]->device,
-                                             sizeof(float) * rlen, x->stream));
-            MBR_CUDA(cudaMemcpyPeerAsync(rws, x->device, ws[r - 1] + off, hs[r - 1]->device, sizeof(float) * rlen,
+                                             sizeof(float) * rlen[r], x->stream));
+            MBR_CUDA(cudaMemcpyPeerAsync(rws, x->device, ws[r - 1] + off, hs[r - 1]->device, sizeof(float) * rlen[r],
                                          x->stream));
-            x->sep->add_boundary(sh[r], acc[r], ws[r], racc, rws, rlen, x->stream);
-            MBR_CUDA(cudaStreamSynchronize(x->stream));
+            x->sep->add_boundary(sh[r], acc[r], ws[r], racc[r], rws, rlen[r], x->stream);
+            if (!independent) MBR_CUDA(cudaStreamSynchronize(x->stream));
         }
-        // normalise each own range and copy it out
+        // normalise each own range into the rank's output buffer and copy it out
         for (int r = 0; r < world; ++r) {
             mbr_handle* x = hs[r];
             MBR_CUDA(cudaSetDevice(x->device));
-            int64_t span = sh[r].hi - sh[r].lo;
-            int64_t rlen = r > 0 ? sh[r - 1].hi - sh[r - 1].send_lo : 0;
-            float* dout = ws[r] + span + (size_t)(SC + 1) * rlen;
-            x->sep->finalize_shard(plan, sh[r], acc[r], ws[r], dout, N, x->stream);
-            int64_t w = sh[r].out_hi - sh[r].out_lo;
-            if (w > 0)
-                MBR_CUDA(cudaMemcpy2DAsync(h_out + sh[r].out_lo, sizeof(float) * N, dout + sh[r].out_lo,
-                                           sizeof(float) * N, sizeof(float) * w, SC, cudaMemcpyDeviceToHost,
-                                           x->stream));
+            const int64_t wout = sh[r].out_hi - sh[r].out_lo;
+            if (wout <= 0) continue;
+            // finalize_shard writes track column t at dout[o * wout + t - out_lo]
+            x->sep->finalize_shard(plan, sh[r], acc[r], ws[r], dout[r] - sh[r].out_lo, wout, x->stream);
+            MBR_CUDA(cudaMemcpy2DAsync(h_out + sh[r].out_lo, sizeof(float) * N, dout[r], sizeof(float) * wout,
+                                       sizeof(float) * wout, SC, cudaMemcpyDeviceToHost, x->stream));
         }
         for (int r = 0; r < world; ++r) {
             MBR_CUDA(cudaSetDevice(hs[r]->device));
@@ -294,7 +305,48 @@ MBR_API int mbr_shard_run(mbr_handle* h, const float* d_track, int64_t N, float 
         mbr::ChunkPlan p = mbr::make_chunk_plan(N, c.chunk_size, overlap, c.num_overlap);
         need(!p.single, "track fits one chunk: nothing to shard");
         MBR_CUDA(cudaSetDevice(h->device));
-        h->sep->run_shard(p, mbr::make_shard(p, rank, world), d_track, chunk_batch, d_acc, d_wsum,
+        h->sep->run_shard(p, mbr::make_shard(p, rank, world), d_track, 0, N, chunk_batch, d_acc, d_wsum,
+                          (cudaStream_t)stream);
+        h->launches = h->sep->last_launches();
+    });
+}
+
+MBR_API int mbr_shard_window(mbr_handle* h, int64_t N, float overlap, int rank, int world, int64_t* in_lo,
+                             int64_t* in_hi) {
+    return guard([&] {
+        need(h && in_lo && in_hi, "null argument");
+        const mbr::MBRConfig& c = h->model->config();
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, c.chunk_size, overlap, c.num_overlap);
+        need(!p.single, "track fits one chunk: nothing to shard");
+        mbr::Shard s = mbr::make_shard(p, rank, world);
+        *in_lo = s.in_lo;
+        *in_hi = s.in_hi;
+    });
+}
+
+MBR_API int mbr_plan_shard_window(int64_t N, int chunk_size, float overlap, int default_overlap, int rank, int world,
+                                  int64_t* in_lo, int64_t* in_hi) {
+    return guard([&] {
+        need(in_lo && in_hi && N > 0 && chunk_size > 0, "bad argument");
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, chunk_size, overlap, default_overlap);
+        need(!p.single, "track fits one chunk: nothing to shard");
+        mbr::Shard s = mbr::make_shard(p, rank, world);
+        *in_lo = s.in_lo;
+        *in_hi = s.in_hi;
+    });
+}
+
+MBR_API int mbr_shard_run_window(mbr_handle* h, const float* d_window, int64_t win_lo, int64_t win_len, int64_t N,
+                                 float overlap, int chunk_batch, int rank, int world, float* d_acc, float* d_wsum,
+                                 void* stream) {
+    return guard([&] {
+        need(h && d_window && d_acc && d_wsum, "null argument");
+        need(win_lo >= 0 && win_len > 0 && win_lo + win_len <= N, "bad track window");
+        const mbr::MBRConfig& c = h->model->config();
+        mbr::ChunkPlan p = mbr::make_chunk_plan(N, c.chunk_size, overlap, c.num_overlap);
+        need(!p.single, "track fits one chunk: nothing to shard");
+        MBR_CUDA(cudaSetDevice(h->device));
+        h->sep->run_shard(p, mbr::make_shard(p, rank, world), d_window, win_lo, win_len, chunk_batch, d_acc, d_wsum,
                           (cudaStream_t)stream);
         h->launches = h->sep->last_launches();
     });

@@ -24,7 +24,19 @@ size_t CudaMemoryPool::round_up(size_t b) {
     return (b + kLarge - 1) / kLarge * kLarge;
 }
 
-void* CudaMemoryPool::allocate(size_t requested) {
+cudaEvent_t CudaMemoryPool::take_event_locked(int device) {
+    std::vector<cudaEvent_t>& spare = spare_events_[device];
+    if (!spare.empty()) {
+        cudaEvent_t e = spare.back();
+        spare.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    MBR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    return e;
+}
+
+void* CudaMemoryPool::allocate(size_t requested, cudaStream_t stream) {
     if (requested == 0) return nullptr;
     int dev = 0;
     MBR_CUDA(cudaGetDevice(&dev));
@@ -33,8 +45,23 @@ void* CudaMemoryPool::allocate(size_t requested) {
     // smallest cached block of at least `size` that wastes at most half of itself
     auto it = free_.lower_bound({dev, size});
     if (it != free_.end() && it->first.first == dev && it->first.second <= 2 * size && !it->second.empty()) {
-        void* p = it->second.back();
-        it->second.pop_back();
+        std::vector<Cached>& v = it->second;
+        // a block freed on this stream needs no ordering; else the most recent
+        size_t pick = v.size() - 1;
+        for (size_t i = v.size(); i-- > 0;)
+            if (v[i].stream == stream) {
+                pick = i;
+                break;
+            }
+        const Cached c = v[pick];
+        v.erase(v.begin() + (std::ptrdiff_t)pick);
+        if (c.stream != stream && c.event) {
+            // the free's stream order carries over to this stream
+            MBR_CUDA(cudaStreamWaitEvent(stream, c.event, 0));
+            stats_.cross_stream_reuses++;
+        }
+        if (c.event) spare_events_[dev].push_back(c.event);
+        void* p = c.ptr;
         live_[p] = {it->first.second, dev};
         stats_.allocations++;
         stats_.cache_hits++;
@@ -62,7 +89,7 @@ void* CudaMemoryPool::allocate(size_t requested) {
     return p;
 }
 
-void CudaMemoryPool::deallocate(void* p) {
+void CudaMemoryPool::deallocate(void* p, cudaStream_t stream) {
     if (!p) return;
     std::lock_guard<std::mutex> lock(mutex_);
     auto it = live_.find(p);
@@ -70,7 +97,18 @@ void CudaMemoryPool::deallocate(void* p) {
         cudaFree(p);  // not ours: hand back to the runtime
         return;
     }
-    free_[{it->second.device, it->second.size}].push_back(p);
+    // the legacy default stream orders itself with every blocking stream, so a
+    // block freed there needs no event
+    cudaEvent_t ev = nullptr;
+    if (stream != nullptr) {
+        int cur = 0;
+        cudaGetDevice(&cur);
+        if (cur != it->second.device) cudaSetDevice(it->second.device);
+        ev = take_event_locked(it->second.device);
+        MBR_CUDA(cudaEventRecord(ev, stream));
+        if (cur != it->second.device) cudaSetDevice(cur);
+    }
+    free_[{it->second.device, it->second.size}].push_back({p, stream, ev});
     stats_.deallocations++;
     stats_.active_bytes -= it->second.size;
     live_.erase(it);
@@ -80,9 +118,10 @@ void CudaMemoryPool::release_cached_locked() {
     int cur = 0;
     cudaGetDevice(&cur);
     for (auto& kv : free_) {
-        for (void* p : kv.second) {
+        for (const Cached& c : kv.second) {
             cudaSetDevice(kv.first.first);
-            cudaFree(p);
+            cudaFree(c.ptr);  // cudaFree waits for the device, so pending uses are done
+            if (c.event) cudaEventDestroy(c.event);
             stats_.total_freed += kv.first.second;
         }
         kv.second.clear();
@@ -122,6 +161,7 @@ size_t CudaMemoryPool::cached_bytes() const {
 void CudaMemoryPool::print_stats() const {
     Stats s = get_stats();
     std::cout << "[MemPool] allocs=" << s.allocations << " frees=" << s.deallocations << " hits=" << s.cache_hits
+              << " cross-stream=" << s.cross_stream_reuses
               << " active=" << (s.active_bytes >> 20) << "MB peak=" << (s.peak_bytes >> 20)
               << "MB cached=" << (cached_bytes() >> 20) << "MB" << std::endl;
 }

@@ -83,8 +83,12 @@ void istft_ola(const float* frames, int64_t nsig, int T, int hop, const float* w
                cudaStream_t st);
 
 // Chunk driver kernels (process_chunked restated on the device).
-void prepare_chunks(const float* track, int C, int64_t N, int64_t border, bool padded, const int64_t* starts,
-                    int nchunks, int64_t total, int chunk, float* in, cudaStream_t st);
+// prepare_chunks reads track samples [track_lo, track_lo + track_ld) of each
+// channel from `track` (row stride track_ld): the whole track (0, N) or a
+// shard's input window.
+void prepare_chunks(const float* track, int C, int64_t N, int64_t track_lo, int64_t track_ld, int64_t border,
+                    bool padded, const int64_t* starts, int nchunks, int64_t total, int chunk, float* in,
+                    cudaStream_t st);
 // acc [SC][acc_stride] / wsum [acc_stride] hold padded samples [acc_lo, acc_lo + acc_stride).
 void accumulate_chunks(const float* y, int nchunks, int SC, int64_t lout, const int64_t* starts, int64_t total,
                        int chunk, int fade, float* acc, float* wsum, int64_t acc_lo, int64_t acc_stride,

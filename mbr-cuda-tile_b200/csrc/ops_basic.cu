@@ -492,9 +492,10 @@ __device__ __forceinline__ float fade_weight(int64_t q, int chunk, int fade, boo
     return 1.0f;
 }
 
-__global__ void prepare_chunks_kernel(const float* __restrict__ track, int C, int64_t N, int64_t border,
-                                      bool padded, const int64_t* __restrict__ starts, int nchunks, int64_t total,
-                                      int chunk, float* __restrict__ in) {
+__global__ void prepare_chunks_kernel(const float* __restrict__ track, int C, int64_t N, int64_t track_lo,
+                                      int64_t track_ld, int64_t border, bool padded,
+                                      const int64_t* __restrict__ starts, int nchunks, int64_t total, int chunk,
+                                      float* __restrict__ in) {
     int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)nchunks * C * chunk) return;
     int64_t q = idx % chunk;
@@ -506,7 +507,7 @@ __global__ void prepare_chunks_kernel(const float* __restrict__ track, int C, in
     int64_t pp = -1;
     if (q < al) pp = st + q;
     else if (al > chunk / 2) pp = st + reflect_idx(q, al);
-    if (pp >= 0) v = track[(int64_t)ch * N + (padded ? reflect_idx(pp - border, N) : pp)];
+    if (pp >= 0) v = track[(int64_t)ch * track_ld + (padded ? reflect_idx(pp - border, N) : pp) - track_lo];
     in[idx] = v;
 }
 
@@ -667,11 +668,12 @@ void istft_ola(const float* frames, int64_t nsig, int T, int hop, const float* w
     MBR_CUDA(cudaGetLastError());
 }
 
-void prepare_chunks(const float* track, int C, int64_t N, int64_t border, bool padded, const int64_t* starts,
-                    int nchunks, int64_t total, int chunk, float* in, cudaStream_t st) {
+void prepare_chunks(const float* track, int C, int64_t N, int64_t track_lo, int64_t track_ld, int64_t border,
+                    bool padded, const int64_t* starts, int nchunks, int64_t total, int chunk, float* in,
+                    cudaStream_t st) {
     int64_t n = (int64_t)nchunks * C * chunk;
-    prepare_chunks_kernel<<<nblk(n, 256), 256, 0, st>>>(track, C, N, border, padded, starts, nchunks, total, chunk,
-                                                        in);
+    prepare_chunks_kernel<<<nblk(n, 256), 256, 0, st>>>(track, C, N, track_lo, track_ld, border, padded, starts,
+                                                        nchunks, total, chunk, in);
     MBR_CUDA(cudaGetLastError());
 }
 

@@ -36,6 +36,7 @@ struct Shard {
     int64_t own_lo = 0, own_hi = 0;  // samples this shard finalises (disjoint across shards)
     int64_t send_lo = 0;             // [send_lo, hi) is added into the next shard
     int64_t out_lo = 0, out_hi = 0;  // own range in output (track) coordinates
+    int64_t in_lo = 0, in_hi = 0;    // input (track) samples the range reads: [in_lo, in_hi)
 };
 Shard make_shard(const ChunkPlan& p, int rank, int world);
 
@@ -46,9 +47,18 @@ public:
     // d_track [C][N] -> d_out [S][C][N] (device, fp32).
     void separate(const float* d_track, int64_t N, float overlap, int chunk_batch, float* d_out, cudaStream_t st);
     // Runs the chunks of `sh` and accumulates into d_acc [S*C][hi-lo] and
-    // d_wsum [hi-lo] (zeroed here first).
-    void run_shard(const ChunkPlan& p, const Shard& sh, const float* d_track, int chunk_batch, float* d_acc,
-                   float* d_wsum, cudaStream_t st);
+    // d_wsum [hi-lo] (zeroed here first).  d_track holds track samples
+    // [track_lo, track_lo + track_ld) of each channel, rows track_ld apart
+    // (the whole track: 0, N; or at least the shard's [in_lo, in_hi)).
+    void run_shard(const ChunkPlan& p, const Shard& sh, const float* d_track, int64_t track_lo, int64_t track_ld,
+                   int chunk_batch, float* d_acc, float* d_wsum, cudaStream_t st);
+    // Host track in, host stems out, with the copies overlapped with the
+    // chunks: each chunk batch's new input samples go up on `copy_st` ahead of
+    // it, and every output range that no later chunk touches is normalised
+    // and copied down while the next batches run.  h_track [C][N], h_out
+    // [S][C][N] (pinned host memory lets the copies run asynchronously).
+    void separate_host(const float* h_track, int64_t N, float overlap, int chunk_batch, float* h_out,
+                       cudaStream_t st, cudaStream_t copy_st);
     // Adds the previous shard's boundary (its [send_lo, hi) = this shard's
     // [lo, lo + recv_len)): d_recv_acc [S*C][recv_len], d_recv_wsum [recv_len].
     void add_boundary(const Shard& sh, float* d_acc, float* d_wsum, const float* d_recv_acc,
@@ -64,6 +74,7 @@ private:
     MelBandRoformer& m_;
     void* bufs_[8] = {};
     size_t caps_[8] = {};
+    cudaEvent_t ev_[3] = {};  // separate_host: input batch uploaded, output range ready, last download done
     int64_t launches_ = 0;
 };
 

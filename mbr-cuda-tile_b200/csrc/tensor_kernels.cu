@@ -1,9 +1,26 @@
-// tensor_kernels.cu — generic strided kernels behind the Tensor API: copy /
-// dtype conversion, fill, broadcast binary ops, scalar ops, reductions over
-// one dim, reflect padding, index_select, arange.  Shapes and strides travel
-// by value in the launch parameters (the reference uploads them with a
-// blocking cudaMemcpy per call, src/tensor_cuda_glue.cu:47-55), so no op
-// synchronises the host.
+// tensor_kernels.cu — kernels behind the Tensor API: copy / dtype conversion,
+// fill, broadcast binary ops, scalar ops, reductions over one dim, reflect
+// padding, index_select, arange.
+//
+// Restates the elementwise, broadcast and reduction kernels of the reference
+// tensor library (src/tensor_cuda_tile.cu:264-338, src/tensor_cuda_glue.cu:57-559)
+// for sm_100a:
+//  * contiguous operands of one floating dtype (the common case) take
+//    vectorised kernels: every thread moves 16-byte vectors (8 x 16-bit or
+//    2 x 4 x fp32 per step), grid-stride, with the dtype and the operation as
+//    template parameters, so the inner loop has no branches or conversions
+//    other than the element's own; a [D] operand broadcast over rows and a
+//    scalar operand have their own vector paths;
+//  * reductions over a contiguous last dim use one warp per row: 16-byte
+//    loads along the row, fp32 accumulation, a shuffle butterfly at the end;
+//    other reductions keep one thread per output, whose strided walk is
+//    coalesced across neighbouring outputs;
+//  * everything else (views with arbitrary strides, mixed dtypes) takes the
+//    generic strided kernels, with 32-bit index arithmetic when the element
+//    count allows.
+// Shapes and strides travel by value in the launch parameters (the reference
+// uploads them with a blocking cudaMemcpy per call, src/tensor_cuda_glue.cu:47-55),
+// so no op synchronises the host.
 #include "common.cuh"
 #include "tensor_kernels.h"
 
@@ -11,6 +28,8 @@ namespace cudasep {
 namespace tk {
 
 namespace {
+
+enum Dt { F32 = 0, F16 = 1, I64 = 2, BF16 = 3 };
 
 struct Geo {
     int nd;
@@ -31,69 +50,273 @@ Geo make_geo(int nd, const int64_t* shape, const int64_t* s0, const int64_t* s1,
     return g;
 }
 
-__device__ __forceinline__ void offsets(const Geo& g, int64_t lin, int64_t& o0, int64_t& o1, int64_t& o2) {
+// Element offsets of linear index `lin` (row-major over g.shape) in the three
+// operands; I is the index type (uint32_t when every offset fits).
+template <typename I>
+__device__ __forceinline__ void offsets(const Geo& g, I lin, int64_t& o0, int64_t& o1, int64_t& o2) {
     o0 = o1 = o2 = 0;
     for (int d = g.nd - 1; d >= 0; --d) {
-        const int64_t i = lin % g.shape[d];
-        lin /= g.shape[d];
-        o0 += i * g.s[0][d];
-        o1 += i * g.s[1][d];
-        o2 += i * g.s[2][d];
+        const I n = (I)g.shape[d];
+        const I q = lin / n;
+        const I i = lin - q * n;
+        lin = q;
+        o0 += (int64_t)i * g.s[0][d];
+        o1 += (int64_t)i * g.s[1][d];
+        o2 += (int64_t)i * g.s[2][d];
     }
 }
 
-__device__ __forceinline__ double ld(const void* p, int dt, int64_t off) {
+// ---- scalar element access (generic paths) ----
+__device__ __forceinline__ float ldf(const void* p, int dt, int64_t off) {
     switch (dt) {
-        case 0: return ((const float*)p)[off];
-        case 1: return __half2float(((const __half*)p)[off]);
-        case 2: return (double)((const int64_t*)p)[off];
+        case F32: return ((const float*)p)[off];
+        case F16: return __half2float(((const __half*)p)[off]);
+        case I64: return (float)((const int64_t*)p)[off];
         default: return __bfloat162float(((const __nv_bfloat16*)p)[off]);
     }
 }
-
-__device__ __forceinline__ void st(void* p, int dt, int64_t off, double v) {
+__device__ __forceinline__ void stf(void* p, int dt, int64_t off, float v) {
     switch (dt) {
-        case 0: ((float*)p)[off] = (float)v; break;
-        case 1: ((__half*)p)[off] = __float2half_rn((float)v); break;
-        case 2: ((int64_t*)p)[off] = (int64_t)v; break;
-        default: ((__nv_bfloat16*)p)[off] = __float2bfloat16_rn((float)v); break;
+        case F32: ((float*)p)[off] = v; break;
+        case F16: ((__half*)p)[off] = __float2half_rn(v); break;
+        case I64: ((int64_t*)p)[off] = (int64_t)v; break;
+        default: ((__nv_bfloat16*)p)[off] = __float2bfloat16_rn(v); break;
     }
+}
+
+// ---- 8-element vectors: one 16-byte access for 16-bit types, two for fp32 ----
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        v[2 * i] = f.x, v[2 * i + 1] = f.y;
+    }
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[2 * i] = f.x, v[2 * i + 1] = f.y;
+    }
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float (&v)[8]) {
+    uint4 u;
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+template <typename T>
+__device__ __forceinline__ float tof(T x) {
+    return mbr::to_f32(x);
+}
+template <typename T>
+__device__ __forceinline__ T fromf(float x) {
+    return mbr::from_f32<T>(x);
+}
+
+template <int OP>
+__device__ __forceinline__ float bin(float x, float y) {
+    if constexpr (OP == BIN_ADD) return x + y;
+    else if constexpr (OP == BIN_SUB) return x - y;
+    else if constexpr (OP == BIN_MUL) return x * y;
+    else return x / y;
+}
+template <int OP>
+__device__ __forceinline__ float un(float x, float p0, float p1) {
+    if constexpr (OP == UN_ADD_SCALAR) return x + p0;
+    else if constexpr (OP == UN_MUL_SCALAR) return x * p0;
+    else if constexpr (OP == UN_CLAMP) return fminf(fmaxf(x, p0), p1);
+    else if constexpr (OP == UN_NEG) return -x;
+    else return x > p0 ? 1.0f : 0.0f;  // UN_GT
 }
 
 #define GRID_STRIDE(i, n) for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (n); \
                                i += (int64_t)gridDim.x * blockDim.x)
 
+// Two independent 8-element vectors in flight per thread per step: units
+// i and i + stride of the grid-stride loop.
+#define VEC_LOOP(n8, ...)                                                              \
+    do {                                                                               \
+        const int64_t stride_ = (int64_t)gridDim.x * blockDim.x;                       \
+        int64_t i_ = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;                   \
+        for (; i_ + stride_ < (n8); i_ += 2 * stride_) {                               \
+            { const int64_t u = i_; __VA_ARGS__; }                                     \
+            { const int64_t u = i_ + stride_; __VA_ARGS__; }                           \
+        }                                                                              \
+        if (i_ < (n8)) { const int64_t u = i_; __VA_ARGS__; }                          \
+    } while (0)
+
+// y = convert(a), contiguous (S == D: a vector copy)
+template <typename S, typename D>
+__global__ void __launch_bounds__(256) cvt_vec_kernel(const S* __restrict__ a, D* __restrict__ y, int64_t n) {
+    const int64_t n8 = n >> 3;
+    VEC_LOOP(n8, {
+        float v[8];
+        load8(a + 8 * u, v);
+        store8(y + 8 * u, v);
+    });
+    if (blockIdx.x == 0 && threadIdx.x < (n & 7)) {
+        const int64_t i = 8 * n8 + threadIdx.x;
+        y[i] = fromf<D>(tof(a[i]));
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) fill_vec_kernel(T* __restrict__ y, int64_t n, float val) {
+    const int64_t n8 = n >> 3;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = val;
+    VEC_LOOP(n8, store8(y + 8 * u, v));
+    if (blockIdx.x == 0 && threadIdx.x < (n & 7)) y[8 * n8 + threadIdx.x] = fromf<T>(val);
+}
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(256) unary_vec_kernel(const T* __restrict__ a, T* __restrict__ y, int64_t n,
+                                                        float p0, float p1) {
+    const int64_t n8 = n >> 3;
+    VEC_LOOP(n8, {
+        float v[8];
+        load8(a + 8 * u, v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = un<OP>(v[k], p0, p1);
+        store8(y + 8 * u, v);
+    });
+    if (blockIdx.x == 0 && threadIdx.x < (n & 7)) {
+        const int64_t i = 8 * n8 + threadIdx.x;
+        y[i] = fromf<T>(un<OP>(tof(a[i]), p0, p1));
+    }
+}
+
+// y = a (op) b, a and y contiguous [n]; BM 0: b contiguous [n]; 1: b [D]
+// broadcast over rows (D % 8 == 0); 2: b a scalar.
+template <typename T, int OP, int BM>
+__global__ void __launch_bounds__(256) binary_vec_kernel(const T* __restrict__ a, const T* __restrict__ b,
+                                                         T* __restrict__ y, int64_t n, int64_t D) {
+    const int64_t n8 = n >> 3;
+    const float bs = BM == 2 ? tof(b[0]) : 0.f;
+    VEC_LOOP(n8, {
+        float v[8], w[8];
+        load8(a + 8 * u, v);
+        if constexpr (BM == 0) load8(b + 8 * u, w);
+        else if constexpr (BM == 1) load8(b + (8 * u) % D, w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = bin<OP>(v[k], BM == 2 ? bs : w[k]);
+        store8(y + 8 * u, v);
+    });
+    if (blockIdx.x == 0 && threadIdx.x < (n & 7)) {
+        const int64_t i = 8 * n8 + threadIdx.x;
+        const float bv = BM == 0 ? tof(b[i]) : BM == 1 ? tof(b[i % D]) : bs;
+        y[i] = fromf<T>(bin<OP>(tof(a[i]), bv));
+    }
+}
+
+// out[r] = reduce(src[r][0..len)), contiguous rows: one warp per row.
+template <typename T, int OP>
+__global__ void __launch_bounds__(256) reduce_rows_kernel(const T* __restrict__ src, T* __restrict__ out,
+                                                          int64_t rows, int64_t len, bool vec) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = warp0; r < rows; r += nwarps) {
+        const T* row = src + r * len;
+        float acc0 = OP == RED_MAX ? -INFINITY : 0.f, acc1 = acc0;
+        int64_t k = 0;
+        if (vec) {
+            // 16-byte vectors: 8 elements per lane, two vectors in flight
+            for (; k + 512 <= len; k += 512) {
+                float v[8], w[8];
+                load8(row + k + 8 * lane, v);
+                load8(row + k + 256 + 8 * lane, w);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    acc0 = OP == RED_MAX ? fmaxf(acc0, v[e]) : acc0 + v[e];
+                    acc1 = OP == RED_MAX ? fmaxf(acc1, w[e]) : acc1 + w[e];
+                }
+            }
+            for (; k + 256 <= len; k += 256) {
+                float v[8];
+                load8(row + k + 8 * lane, v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc0 = OP == RED_MAX ? fmaxf(acc0, v[e]) : acc0 + v[e];
+            }
+        }
+        for (int64_t q = k + lane; q < len; q += 32) {
+            const float v = tof(row[q]);
+            acc1 = OP == RED_MAX ? fmaxf(acc1, v) : acc1 + v;
+        }
+        float acc = OP == RED_MAX ? fmaxf(acc0, acc1) : acc0 + acc1;
+        acc = OP == RED_MAX ? mbr::warp_max(acc) : mbr::warp_sum(acc);
+        if (lane == 0) out[r] = fromf<T>(OP == RED_MEAN ? acc / (float)len : acc);
+    }
+}
+
+// ---- generic strided kernels ----
+template <typename I>
 __global__ void copy_kernel(Geo g, const void* src, int sdt, void* dst, int ddt, int64_t n) {
     GRID_STRIDE(i, n) {
         int64_t os, od, unused;
-        offsets(g, i, os, od, unused);
+        offsets<I>(g, (I)i, os, od, unused);
         if (sdt == ddt) {
             switch (sdt) {
-                case 0: ((float*)dst)[od] = ((const float*)src)[os]; break;
-                case 2: ((int64_t*)dst)[od] = ((const int64_t*)src)[os]; break;
+                case F32: ((float*)dst)[od] = ((const float*)src)[os]; break;
+                case I64: ((int64_t*)dst)[od] = ((const int64_t*)src)[os]; break;
                 default: ((uint16_t*)dst)[od] = ((const uint16_t*)src)[os]; break;
             }
         } else {
-            st(dst, ddt, od, ld(src, sdt, os));
+            stf(dst, ddt, od, ldf(src, sdt, os));
         }
     }
 }
 
+template <typename I>
 __global__ void fill_kernel(Geo g, void* dst, int dt, double v, int64_t n) {
     GRID_STRIDE(i, n) {
         int64_t od, u1, u2;
-        offsets(g, i, od, u1, u2);
-        st(dst, dt, od, v);
+        offsets<I>(g, (I)i, od, u1, u2);
+        if (dt == I64) ((int64_t*)dst)[od] = (int64_t)v;
+        else stf(dst, dt, od, (float)v);
     }
 }
 
+template <typename I>
 __global__ void binary_kernel(Geo g, int op, const void* a, int adt, const void* b, int bdt, void* out, int odt,
                               int64_t n) {
     GRID_STRIDE(i, n) {
         int64_t oa, ob, oo;
-        offsets(g, i, oa, ob, oo);
+        offsets<I>(g, (I)i, oa, ob, oo);
         // fp32 arithmetic (the reference computes its elementwise ops in fp32)
-        const float x = (float)ld(a, adt, oa), y = (float)ld(b, bdt, ob);
+        const float x = ldf(a, adt, oa), y = ldf(b, bdt, ob);
         float r;
         switch (op) {
             case BIN_ADD: r = x + y; break;
@@ -101,16 +324,17 @@ __global__ void binary_kernel(Geo g, int op, const void* a, int adt, const void*
             case BIN_MUL: r = x * y; break;
             default: r = x / y; break;
         }
-        st(out, odt, oo, r);
+        stf(out, odt, oo, r);
     }
 }
 
+template <typename I>
 __global__ void unary_kernel(Geo g, int op, const void* a, int adt, void* out, int odt, float p0, float p1,
                              int64_t n) {
     GRID_STRIDE(i, n) {
         int64_t oa, oo, u;
-        offsets(g, i, oa, oo, u);
-        const float x = (float)ld(a, adt, oa);
+        offsets<I>(g, (I)i, oa, oo, u);
+        const float x = ldf(a, adt, oa);
         float r;
         switch (op) {
             case UN_ADD_SCALAR: r = x + p0; break;
@@ -119,23 +343,24 @@ __global__ void unary_kernel(Geo g, int op, const void* a, int adt, void* out, i
             case UN_NEG: r = -x; break;
             default: r = x > p0 ? 1.0f : 0.0f; break;  // UN_GT
         }
-        st(out, odt, oo, r);
+        stf(out, odt, oo, r);
     }
 }
 
 // One thread per output element; the reduced dim is walked with its stride.
+template <typename I>
 __global__ void reduce_kernel(Geo g, int op, const void* src, int sdt, int64_t len, int64_t rstride, void* out,
                               int odt, int64_t n) {
     GRID_STRIDE(i, n) {
         int64_t os, oo, u;
-        offsets(g, i, os, oo, u);
+        offsets<I>(g, (I)i, os, oo, u);
         float acc = op == RED_MAX ? -INFINITY : 0.f;
         for (int64_t k = 0; k < len; ++k) {
-            const float v = (float)ld(src, sdt, os + k * rstride);
+            const float v = ldf(src, sdt, os + k * rstride);
             acc = op == RED_MAX ? fmaxf(acc, v) : acc + v;
         }
         if (op == RED_MEAN) acc /= (float)len;
-        st(out, odt, oo, acc);
+        stf(out, odt, oo, acc);
     }
 }
 
@@ -144,8 +369,8 @@ __global__ void pad_reflect_kernel(const void* src, int dt, int64_t L, int64_t l
     GRID_STRIDE(i, n) {
         const int64_t r = i / Lo, q = i % Lo;
         const int64_t p = mbr::reflect_idx(q - left, L);
-        if (dt == 0) ((float*)dst)[i] = ((const float*)src)[r * L + p];
-        else if (dt == 2) ((int64_t*)dst)[i] = ((const int64_t*)src)[r * L + p];
+        if (dt == F32) ((float*)dst)[i] = ((const float*)src)[r * L + p];
+        else if (dt == I64) ((int64_t*)dst)[i] = ((const int64_t*)src)[r * L + p];
         else ((uint16_t*)dst)[i] = ((const uint16_t*)src)[r * L + p];
     }
 }
@@ -163,45 +388,178 @@ __global__ void index_select_kernel(const void* src, int dt, int64_t dsrc, int64
             continue;
         }
         const int64_t s = (o * dsrc + k) * inner + in;
-        if (dt == 0) ((float*)dst)[i] = ((const float*)src)[s];
-        else if (dt == 2) ((int64_t*)dst)[i] = ((const int64_t*)src)[s];
+        if (dt == F32) ((float*)dst)[i] = ((const float*)src)[s];
+        else if (dt == I64) ((int64_t*)dst)[i] = ((const int64_t*)src)[s];
         else ((uint16_t*)dst)[i] = ((const uint16_t*)src)[s];
     }
 }
 
 __global__ void arange_kernel(void* dst, int dt, int64_t start, int64_t n) {
-    GRID_STRIDE(i, n) st(dst, dt, i, (double)(start + i));
+    GRID_STRIDE(i, n) {
+        if (dt == I64) ((int64_t*)dst)[i] = start + i;
+        else stf(dst, dt, i, (float)(start + i));
+    }
 }
 
-unsigned grid(int64_t n) { return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)); }
+// ---- host-side classification and dispatch ----
+int sm_count() {
+    static int n = [] {
+        int dev = 0, v = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        return v > 0 ? v : 148;
+    }();
+    return n;
+}
+// grid of the generic kernels: one element per thread, at most 32 CTAs per SM
+unsigned grid(int64_t n) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 32));
+}
+// grid of the vector kernels (256 threads, two 8-element units per thread
+// per step): enough CTAs to fill every SM several times over
+unsigned vgrid(int64_t n8) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n8 + 511) / 512, (int64_t)sm_count() * 8));
+}
+
+bool is_contig(int nd, const int64_t* shape, const int64_t* st) {
+    int64_t e = 1;
+    for (int d = nd - 1; d >= 0; --d) {
+        if (shape[d] != 1 && st[d] != e) return false;
+        e *= shape[d];
+    }
+    return true;
+}
+// b is a [D] vector along the last dim broadcast over all other dims
+bool is_row_bcast(int nd, const int64_t* shape, const int64_t* st) {
+    if (nd < 1 || st[nd - 1] != 1) return false;
+    for (int d = 0; d < nd - 1; ++d)
+        if (shape[d] != 1 && st[d] != 0) return false;
+    return true;
+}
+bool is_scalar_bcast(int nd, const int64_t* shape, const int64_t* st) {
+    for (int d = 0; d < nd; ++d)
+        if (shape[d] != 1 && st[d] != 0) return false;
+    return true;
+}
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+bool fits32(int64_t n, int nd, const int64_t* shape) {
+    (void)shape;
+    (void)nd;
+    return n < (int64_t)1 << 31;
+}
+
+// Calls f with the C++ type of a floating dtype (f32 / f16 / bf16); false for i64.
+template <class F>
+bool with_float_type(int dt, F&& f) {
+    switch (dt) {
+        case F32: f((float*)nullptr); return true;
+        case F16: f((__half*)nullptr); return true;
+        case BF16: f((__nv_bfloat16*)nullptr); return true;
+        default: return false;
+    }
+}
 
 }  // namespace
 
 void copy(const void* src, int sdt, const int64_t* sstride, void* dst, int ddt, const int64_t* dstride, int nd,
           const int64_t* shape, int64_t n, cudaStream_t st) {
     if (n <= 0) return;
-    copy_kernel<<<grid(n), 256, 0, st>>>(make_geo(nd, shape, sstride, dstride, nullptr), src, sdt, dst, ddt, n);
+    if (is_contig(nd, shape, sstride) && is_contig(nd, shape, dstride) && aligned16(src) && aligned16(dst) &&
+        sdt != I64 && ddt != I64) {
+        with_float_type(sdt, [&](auto* s) {
+            using S = std::remove_pointer_t<decltype(s)>;
+            with_float_type(ddt, [&](auto* d) {
+                using D = std::remove_pointer_t<decltype(d)>;
+                cvt_vec_kernel<S, D><<<vgrid(n >> 3), 256, 0, st>>>((const S*)src, (D*)dst, n);
+            });
+        });
+        MBR_CUDA(cudaGetLastError());
+        return;
+    }
+    const Geo g = make_geo(nd, shape, sstride, dstride, nullptr);
+    if (fits32(n, nd, shape)) copy_kernel<uint32_t><<<grid(n), 256, 0, st>>>(g, src, sdt, dst, ddt, n);
+    else copy_kernel<uint64_t><<<grid(n), 256, 0, st>>>(g, src, sdt, dst, ddt, n);
     MBR_CUDA(cudaGetLastError());
 }
 
 void fill(void* dst, int dt, const int64_t* stride, int nd, const int64_t* shape, int64_t n, double v,
           cudaStream_t st) {
     if (n <= 0) return;
-    fill_kernel<<<grid(n), 256, 0, st>>>(make_geo(nd, shape, stride, nullptr, nullptr), dst, dt, v, n);
+    if (is_contig(nd, shape, stride) && aligned16(dst) &&
+        with_float_type(dt, [&](auto* t) {
+            using T = std::remove_pointer_t<decltype(t)>;
+            fill_vec_kernel<T><<<vgrid(n >> 3), 256, 0, st>>>((T*)dst, n, (float)v);
+        })) {
+        MBR_CUDA(cudaGetLastError());
+        return;
+    }
+    const Geo g = make_geo(nd, shape, stride, nullptr, nullptr);
+    if (fits32(n, nd, shape)) fill_kernel<uint32_t><<<grid(n), 256, 0, st>>>(g, dst, dt, v, n);
+    else fill_kernel<uint64_t><<<grid(n), 256, 0, st>>>(g, dst, dt, v, n);
     MBR_CUDA(cudaGetLastError());
 }
 
 void binary(int op, const void* a, int adt, const int64_t* sa, const void* b, int bdt, const int64_t* sb, void* out,
             int odt, const int64_t* so, int nd, const int64_t* shape, int64_t n, cudaStream_t st) {
     if (n <= 0) return;
-    binary_kernel<<<grid(n), 256, 0, st>>>(make_geo(nd, shape, sa, sb, so), op, a, adt, b, bdt, out, odt, n);
+    if (adt == bdt && adt == odt && is_contig(nd, shape, sa) && is_contig(nd, shape, so) && aligned16(a) &&
+        aligned16(out) && op >= BIN_ADD && op <= BIN_DIV) {
+        int bm = -1;
+        const int64_t D = nd > 0 ? shape[nd - 1] : 1;
+        if (is_contig(nd, shape, sb) && aligned16(b)) bm = 0;
+        else if (is_scalar_bcast(nd, shape, sb)) bm = 2;
+        else if (is_row_bcast(nd, shape, sb) && D % 8 == 0 && aligned16(b)) bm = 1;
+        if (bm >= 0 && with_float_type(adt, [&](auto* t) {
+                using T = std::remove_pointer_t<decltype(t)>;
+                const T* A = (const T*)a;
+                const T* B = (const T*)b;
+                T* Y = (T*)out;
+                const unsigned gr = vgrid(n >> 3);
+                auto go = [&](auto opc) {
+                    constexpr int OP = decltype(opc)::value;
+                    if (bm == 0) binary_vec_kernel<T, OP, 0><<<gr, 256, 0, st>>>(A, B, Y, n, D);
+                    else if (bm == 1) binary_vec_kernel<T, OP, 1><<<gr, 256, 0, st>>>(A, B, Y, n, D);
+                    else binary_vec_kernel<T, OP, 2><<<gr, 256, 0, st>>>(A, B, Y, n, D);
+                };
+                switch (op) {
+                    case BIN_ADD: go(std::integral_constant<int, BIN_ADD>()); break;
+                    case BIN_SUB: go(std::integral_constant<int, BIN_SUB>()); break;
+                    case BIN_MUL: go(std::integral_constant<int, BIN_MUL>()); break;
+                    default: go(std::integral_constant<int, BIN_DIV>()); break;
+                }
+            })) {
+            MBR_CUDA(cudaGetLastError());
+            return;
+        }
+    }
+    const Geo g = make_geo(nd, shape, sa, sb, so);
+    if (fits32(n, nd, shape)) binary_kernel<uint32_t><<<grid(n), 256, 0, st>>>(g, op, a, adt, b, bdt, out, odt, n);
+    else binary_kernel<uint64_t><<<grid(n), 256, 0, st>>>(g, op, a, adt, b, bdt, out, odt, n);
     MBR_CUDA(cudaGetLastError());
 }
 
 void unary(int op, const void* a, int adt, const int64_t* sa, void* out, int odt, const int64_t* so, int nd,
            const int64_t* shape, int64_t n, float p0, float p1, cudaStream_t st) {
     if (n <= 0) return;
-    unary_kernel<<<grid(n), 256, 0, st>>>(make_geo(nd, shape, sa, so, nullptr), op, a, adt, out, odt, p0, p1, n);
+    if (adt == odt && is_contig(nd, shape, sa) && is_contig(nd, shape, so) && aligned16(a) && aligned16(out) &&
+        with_float_type(adt, [&](auto* t) {
+            using T = std::remove_pointer_t<decltype(t)>;
+            const T* A = (const T*)a;
+            T* Y = (T*)out;
+            const unsigned gr = vgrid(n >> 3);
+            switch (op) {
+                case UN_ADD_SCALAR: unary_vec_kernel<T, UN_ADD_SCALAR><<<gr, 256, 0, st>>>(A, Y, n, p0, p1); break;
+                case UN_MUL_SCALAR: unary_vec_kernel<T, UN_MUL_SCALAR><<<gr, 256, 0, st>>>(A, Y, n, p0, p1); break;
+                case UN_CLAMP: unary_vec_kernel<T, UN_CLAMP><<<gr, 256, 0, st>>>(A, Y, n, p0, p1); break;
+                case UN_NEG: unary_vec_kernel<T, UN_NEG><<<gr, 256, 0, st>>>(A, Y, n, p0, p1); break;
+                default: unary_vec_kernel<T, UN_GT><<<gr, 256, 0, st>>>(A, Y, n, p0, p1); break;
+            }
+        })) {
+        MBR_CUDA(cudaGetLastError());
+        return;
+    }
+    const Geo g = make_geo(nd, shape, sa, so, nullptr);
+    if (fits32(n, nd, shape)) unary_kernel<uint32_t><<<grid(n), 256, 0, st>>>(g, op, a, adt, out, odt, p0, p1, n);
+    else unary_kernel<uint64_t><<<grid(n), 256, 0, st>>>(g, op, a, adt, out, odt, p0, p1, n);
     MBR_CUDA(cudaGetLastError());
 }
 
@@ -214,8 +572,40 @@ void reduce(int op, const void* src, int sdt, const int64_t* s_outer, int nd, co
         so[d] = acc;
         acc *= outer_shape[d];
     }
-    reduce_kernel<<<grid(n_outer), 256, 0, st>>>(make_geo(nd, outer_shape, s_outer, so.data(), nullptr), op, src,
-                                                 sdt, len, rstride, out, odt, n_outer);
+    // rows of `len` contiguous elements laid one after another: warp per row
+    std::vector<int64_t> row_st(nd);
+    for (int d = 0; d < nd; ++d) row_st[d] = so[d] * len;
+    if (rstride == 1 && sdt == odt &&
+        [&] {
+            for (int d = 0; d < nd; ++d)
+                if (outer_shape[d] != 1 && s_outer[d] != row_st[d]) return false;
+            return true;
+        }() &&
+        with_float_type(sdt, [&](auto* t) {
+            using T = std::remove_pointer_t<decltype(t)>;
+            const bool vec = aligned16(src) && len % 8 == 0;
+            const unsigned gr = (unsigned)std::max<int64_t>(
+                1, std::min<int64_t>((n_outer + 7) / 8, (int64_t)sm_count() * 16));
+            switch (op) {
+                case RED_SUM:
+                    reduce_rows_kernel<T, RED_SUM><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len, vec);
+                    break;
+                case RED_MEAN:
+                    reduce_rows_kernel<T, RED_MEAN><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len, vec);
+                    break;
+                default:
+                    reduce_rows_kernel<T, RED_MAX><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len, vec);
+                    break;
+            }
+        })) {
+        MBR_CUDA(cudaGetLastError());
+        return;
+    }
+    const Geo g = make_geo(nd, outer_shape, s_outer, so.data(), nullptr);
+    if (fits32(n_outer, nd, outer_shape))
+        reduce_kernel<uint32_t><<<grid(n_outer), 256, 0, st>>>(g, op, src, sdt, len, rstride, out, odt, n_outer);
+    else
+        reduce_kernel<uint64_t><<<grid(n_outer), 256, 0, st>>>(g, op, src, sdt, len, rstride, out, odt, n_outer);
     MBR_CUDA(cudaGetLastError());
 }
 

@@ -27,7 +27,7 @@ INFO = dict(dim=0, depth=1, num_stems=2, channels=3, num_bands=4, sample_rate=5,
 EXPORTS = [
     "mbr_last_error", "mbr_version", "mbr_create", "mbr_destroy", "mbr_get_info", "mbr_output_length",
     "mbr_forward_chunk", "mbr_forward_tap", "mbr_separate_device", "mbr_separate", "mbr_shard_info",
-    "mbr_shard_run", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_graphs", "mbr_set_backend", "mbr_last_launches",
+    "mbr_shard_run", "mbr_shard_window", "mbr_plan_shard_window", "mbr_shard_run_window", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_graphs", "mbr_set_backend", "mbr_last_launches",
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
     "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_op_attention", "mbr_op_linear",
     "mbr_rope_tables",
@@ -70,6 +70,10 @@ def lib():
         L.mbr_separate.argtypes = [vp, fp, i64, c_float, c_int, c_int, fp]
         L.mbr_shard_info.argtypes = [vp, i64, c_float, c_int, c_int, i64p]
         L.mbr_shard_run.argtypes = [vp, fp, i64, c_float, c_int, c_int, c_int, fp, fp, vp]
+        L.mbr_shard_window.argtypes = [vp, i64, c_float, c_int, c_int, ctypes.POINTER(i64), ctypes.POINTER(i64)]
+        L.mbr_plan_shard_window.argtypes = [i64, c_int, c_float, c_int, c_int, c_int, ctypes.POINTER(i64),
+                                            ctypes.POINTER(i64)]
+        L.mbr_shard_run_window.argtypes = [vp, fp, i64, i64, i64, c_float, c_int, c_int, c_int, fp, fp, vp]
         L.mbr_shard_add_boundary.argtypes = [vp, i64, c_float, c_int, c_int, fp, fp, fp, fp, i64, vp]
         L.mbr_shard_finalize.argtypes = [vp, i64, c_float, c_int, c_int, fp, fp, fp, i64, vp]
         L.mbr_set_backend.argtypes = [vp, c_int, c_int]
@@ -227,6 +231,14 @@ def op_istft(spec, hop=441, length=-1, stream=None):
     out = torch.empty((n, lout), dtype=torch.float32, device=spec.device)
     _check(lib().mbr_op_istft(_ptr(spec), n, T, hop, length, _ptr(out), _stream(stream)))
     return out
+
+
+def plan_shard_window(N: int, chunk_size: int, overlap: float, default_overlap: int, rank: int, world: int):
+    """Host-only: track samples (lo, hi) the shard of `rank` reads."""
+    lo, hi = ctypes.c_int64(), ctypes.c_int64()
+    _check(lib().mbr_plan_shard_window(int(N), int(chunk_size), float(overlap), int(default_overlap), rank, world,
+                                       ctypes.byref(lo), ctypes.byref(hi)))
+    return lo.value, hi.value
 
 
 SHARD_KEYS = ["c0", "c1", "lo", "hi", "send_lo", "out_lo", "out_hi", "n_chunks", "step", "border", "total"]
@@ -405,10 +417,25 @@ class Model:
         _check(lib().mbr_shard_run(self.h, _ptr(track), int(N), float(overlap), int(chunk_batch), rank, world,
                                    _ptr(acc), _ptr(wsum), _stream(stream)))
 
+    def shard_window(self, N: int, overlap: float, rank: int, world: int):
+        """Track samples (lo, hi) the shard of `rank` reads."""
+        lo, hi = ctypes.c_int64(), ctypes.c_int64()
+        _check(lib().mbr_shard_window(self.h, int(N), float(overlap), rank, world, ctypes.byref(lo), ctypes.byref(hi)))
+        return lo.value, hi.value
+
+    def shard_run_window(self, window, win_lo, N, overlap, chunk_batch, rank, world, acc, wsum, stream=None):
+        """shard_run over window [C, win_len] = track samples [win_lo, win_lo + win_len)."""
+        _check(lib().mbr_shard_run_window(self.h, _ptr(window), int(win_lo), int(window.shape[-1]), int(N),
+                                          float(overlap), int(chunk_batch), rank, world, _ptr(acc), _ptr(wsum),
+                                          _stream(stream)))
+
     def shard_add_boundary(self, N, overlap, rank, world, acc, wsum, racc, rwsum, rlen, stream=None):
         _check(lib().mbr_shard_add_boundary(self.h, int(N), float(overlap), rank, world, _ptr(acc), _ptr(wsum),
                                             _ptr(racc), _ptr(rwsum), int(rlen), _stream(stream)))
 
-    def shard_finalize(self, N, overlap, rank, world, acc, wsum, out, out_stride, stream=None):
+    def shard_finalize(self, N, overlap, rank, world, acc, wsum, out, out_stride, stream=None, out_col0=0):
+        """Writes the shard's own track columns [out_lo, out_hi) into `out`
+        ([S*C][out_stride]); with out_col0 = out_lo, `out` holds only those
+        columns (column t at t - out_col0)."""
         _check(lib().mbr_shard_finalize(self.h, int(N), float(overlap), rank, world, _ptr(acc), _ptr(wsum),
-                                        _ptr(out), int(out_stride), _stream(stream)))
+                                        _ptr(out) - 4 * int(out_col0), int(out_stride), _stream(stream)))

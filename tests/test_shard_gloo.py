@@ -1,10 +1,12 @@
 """Multi-rank chunk sharding on CPU (gloo, world sizes 2 and 3).
 
 Each rank takes its contiguous chunk range from the library's shard planner
-(mbr_plan_shard, host-only), runs a stand-in per-chunk model, overlap-adds its
-chunks with the reference fade windows (src/inference_app.cpp:186-218), receives
-the previous rank's boundary, sends its own tail to the next rank, and
-normalises its disjoint output range — the protocol bench.py runs with NCCL.
+(mbr_plan_shard, host-only), holds only the track window its chunks read
+(mbr_plan_shard_window), runs a stand-in per-chunk model, overlap-adds its
+chunks with the reference fade windows (src/inference_app.cpp:186-218),
+exchanges boundaries with both neighbours at once (its tail to rank + 1, the
+previous rank's tail into its head: one batched isend / irecv), and normalises
+its disjoint output range — the protocol bench.py runs with NCCL.
 The assembled result must equal a single-process restatement of
 process_chunked (src/inference_app.cpp:72-232) with the same stand-in model.
 """
@@ -45,18 +47,28 @@ def _fade(chunk: int):
     return w, fade
 
 
-def _chunk_input(track, total, border, padded, st):
+def _read_index(total, border, padded, st, q, Ntr):
+    """Track sample chunk position q of the chunk at padded start st reads (or None)."""
+    al = min(CHUNK, total - st)
+    if q < al:
+        pp = st + q
+    elif al > CHUNK // 2:
+        pp = st + _reflect(q, al)
+    else:
+        return None
+    return _reflect(pp - border, Ntr) if padded else pp
+
+
+def _chunk_input(track, total, border, padded, st, tr_lo=0, Ntr=None):
+    """Chunk input from `track`, which holds track samples [tr_lo, tr_lo + width)."""
+    Ntr = track.shape[1] if Ntr is None else Ntr
     al = min(CHUNK, total - st)
     out = np.zeros((C, CHUNK), np.float32)
-    Ntr = track.shape[1]
     for q in range(CHUNK):
-        if q < al:
-            pp = st + q
-        elif al > CHUNK // 2:
-            pp = st + _reflect(q, al)
-        else:
-            continue
-        out[:, q] = track[:, _reflect(pp - border, Ntr) if padded else pp]
+        t = _read_index(total, border, padded, st, q, Ntr)
+        if t is not None:
+            assert tr_lo <= t < tr_lo + track.shape[1], "chunk reads outside the track window"
+            out[:, q] = track[:, t - tr_lo]
     return out, al
 
 
@@ -71,14 +83,14 @@ def _window(st, al, total, fade, fw):
     return w[:al]
 
 
-def _accumulate(track, plan, c0, c1, lo, hi):
+def _accumulate(track, plan, c0, c1, lo, hi, tr_lo=0, Ntr=None):
     step, border, total = plan["step"], plan["border"], plan["total"]
     fw, fade = _fade(CHUNK)
     acc = np.zeros((S * C, hi - lo), np.float32)
     ws = np.zeros(hi - lo, np.float32)
     for c in range(c0, c1):
         st = c * step
-        x, al = _chunk_input(track, total, border, border > 0, st)
+        x, al = _chunk_input(track, total, border, border > 0, st, tr_lo, Ntr)
         y = _stand_in_model(x).reshape(S * C, CHUNK)[:, :al]
         w = _window(st, al, total, fade, fw)
         acc[:, st - lo:st - lo + al] += y * w
@@ -105,20 +117,28 @@ def _rank_main(rank, world, port, track, result_path):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     p = cudasep.plan_shard(N, CHUNK, OVERLAP, DEFAULT, rank, world)
-    acc, ws = _accumulate(track, p, p["c0"], p["c1"], p["lo"], p["hi"])
+    w_lo, w_hi = cudasep.plan_shard_window(N, CHUNK, OVERLAP, DEFAULT, rank, world)
+    window = np.ascontiguousarray(track[:, w_lo:w_hi])  # all the rank receives of the track
+    acc, ws = _accumulate(window, p, p["c0"], p["c1"], p["lo"], p["hi"], w_lo, N)
+    # the tail sent on is disjoint from the head received, so both go at once
+    ops = []
+    rlen = 0
     if rank > 0:
         prev = cudasep.plan_shard(N, CHUNK, OVERLAP, DEFAULT, rank - 1, world)
         rlen = prev["hi"] - prev["send_lo"]
+        assert rank == world - 1 or prev["hi"] <= p["send_lo"]
         racc = torch.empty((S * C, rlen))
         rws = torch.empty((rlen,))
-        dist.recv(racc, rank - 1)
-        dist.recv(rws, rank - 1)
-        acc[:, :rlen] += racc.numpy()
-        ws[:rlen] += rws.numpy()
+        ops += [dist.P2POp(dist.irecv, racc, rank - 1), dist.P2POp(dist.irecv, rws, rank - 1)]
     if rank < world - 1:
         off = p["send_lo"] - p["lo"]
-        dist.send(torch.from_numpy(np.ascontiguousarray(acc[:, off:])), rank + 1)
-        dist.send(torch.from_numpy(np.ascontiguousarray(ws[off:])), rank + 1)
+        ops += [dist.P2POp(dist.isend, torch.from_numpy(np.ascontiguousarray(acc[:, off:])), rank + 1),
+                dist.P2POp(dist.isend, torch.from_numpy(np.ascontiguousarray(ws[off:])), rank + 1)]
+    for req in dist.batch_isend_irecv(ops):
+        req.wait()
+    if rank > 0:
+        acc[:, :rlen] += racc.numpy()
+        ws[:rlen] += rws.numpy()
     # own range: padded samples [max(lo, border), min(own_hi, border + N))
     own_hi = p["send_lo"] if rank < world - 1 else p["total"]
     b = p["border"]
@@ -171,3 +191,18 @@ def test_shard_plan_partitions_chunks():
             assert a["c1"] == b["c0"] and a["send_lo"] == b["lo"] and a["out_hi"] == b["out_lo"]
             assert a["hi"] - a["send_lo"] == 352800 - plans[0]["step"]  # the exchanged boundary
         assert plans[0]["out_lo"] == 0 and plans[-1]["out_hi"] == Nn
+
+
+@pytest.mark.parametrize("n_sec,world,overlap", [(7.3, 1, 4.0), (7.3, 3, 4.0), (9.0, 4, 2.0), (2.6, 2, 0.5)])
+def test_shard_window_covers_reads(n_sec, world, overlap):
+    """mbr_plan_shard_window is exactly the span of track samples the shard's
+    chunks read (through the reflect padding and the last chunk's fold)."""
+    import cudasep
+
+    Nn = int(n_sec * 44100)
+    for r in range(world):
+        p = cudasep.plan_shard(Nn, CHUNK, overlap, DEFAULT, r, world)
+        lo, hi = cudasep.plan_shard_window(Nn, CHUNK, overlap, DEFAULT, r, world)
+        reads = [t for c in range(p["c0"], p["c1"]) for q in range(CHUNK)
+                 if (t := _read_index(p["total"], p["border"], p["border"] > 0, c * p["step"], q, Nn)) is not None]
+        assert (lo, hi) == (min(reads), max(reads) + 1), (r, lo, hi, min(reads), max(reads) + 1)
