@@ -285,6 +285,10 @@ def main():
     ap.add_argument("--op-sweep", action="store_true",
                     help="tensor-op sweep: achieved HBM GB/s of every stand-alone op over [B*801*60, D] activations "
                          "(one JSON line per case, then a summary line)")
+    ap.add_argument("--tensor-sweep", action="store_true",
+                    help="Tensor API op sweep: achieved HBM GB/s of the Tensor class's elementwise, broadcast, "
+                         "conversion and reduction kernels over the same activations (runs the native "
+                         "tensor_bench; one JSON line per case, then a summary line)")
     ap.add_argument("--single-chunk", action="store_true",
                     help="profiling aid: run exactly warmup+steps forwards of one chunk batch and print their time "
                          "(not the benchmark line)")
@@ -296,6 +300,8 @@ def main():
         return run_single_chunk(args, wl)
     if args.op_sweep:
         return run_op_sweep(args)
+    if args.tensor_sweep:
+        return run_tensor_sweep(args)
 
     import torch
 
@@ -528,6 +534,28 @@ def main():
         os.rmdir(tmpdir)
     except OSError:
         pass
+    return 0
+
+
+def run_tensor_sweep(args):
+    """Tensor API sweep (the reference tensor library's kernels): runs the
+    native tensor_bench, which times every op alone after an L2 flush with CUDA
+    events on the legacy stream the Tensor API uses, and summarises the
+    fraction of the measured HBM copy peak per op."""
+    peak = load_peaks()["hbm_gbs"]
+    exe = os.path.join(PKG, "tensor_bench")
+    if not os.path.exists(exe):
+        raise SystemExit("tensor_bench missing: build with make -C mbr-cuda-tile_b200")
+    out = subprocess.run([exe, str(max(args.steps, 1)), str(peak)], capture_output=True, text=True, check=True)
+    rows = [json.loads(l) for l in out.stdout.splitlines() if l.startswith("{")]
+    for r in rows:
+        print(json.dumps(r), flush=True)
+    summ = {}
+    for r in rows:
+        summ.setdefault(r["op"], []).append(r["frac"])
+    print(json.dumps({"summary": "tensor_sweep", "peak_gbs": peak, "peak_source": load_peaks()["source"],
+                      "per_op": {k: {"median": float(np.median(v)), "min": float(np.min(v)), "n": len(v)}
+                                 for k, v in summ.items()}}), flush=True)
     return 0
 
 

@@ -551,9 +551,10 @@ __device__ __forceinline__ float exp2_fma(float x) {
     return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
-// 320 threads x 200 registers fit the SM's 64 K registers (one CTA per SM).
+// 10 warps: three share one SM sub-partition's 16 K registers, so at most 168
+// registers per thread.
 template <typename T>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(320, 1)
     attn_time_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, int n_lo, float scale_log2,
                      const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
@@ -763,17 +764,17 @@ __global__ void __maxnreg__(200)
                 tc_fence_after();
                 if (wact) {
                     const int kend = min(TKB, L - j * TKB);  // valid keys of this block (warp-uniform)
-                    uint32_t sv[4][32];
-                    // S -> registers (S keeps its TMEM columns: P has its own)
-                    auto load_s = [&]() {
+                    // S is read from TMEM one 64-column half at a time (S keeps its
+                    // columns: P has its own), so a thread holds 64 scores, not 128
+                    uint32_t sv[2][32];
+                    auto load_half = [&](int hf) {
 #pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            if (c * 32 < kend) tmem_ld32(tS + 32 * c, sv[c]);
+                        for (int c = 0; c < 2; ++c)
+                            if ((2 * hf + c) * 32 < kend) tmem_ld32(tS + 32 * (2 * hf + c), sv[c]);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) reg_pin32(sv[c]);
+                        for (int c = 0; c < 2; ++c) reg_pin32(sv[c]);
                     };
-                    load_s();
                     // probabilities with offset mo -> P columns as 16-bit pairs
                     // (masked keys 0); returns the block's row sum
                     auto emit = [&](float mo) {
@@ -781,43 +782,55 @@ __global__ void __maxnreg__(200)
 #pragma unroll
                         for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t pk[16];
-                            if (c * 32 >= kend) {
+                        for (int hf = 0; hf < 2; ++hf) {
+                            if (hf * 64 < kend) load_half(hf);
 #pragma unroll
-                                for (int i = 0; i < 16; ++i) pk[i] = 0u;
-                            } else {
-                                const int nv = kend - c * 32;
+                            for (int c2 = 0; c2 < 2; ++c2) {
+                                const int c = 2 * hf + c2;
+                                uint32_t pk[16];
+                                if (c * 32 >= kend) {
 #pragma unroll
-                                for (int i = 0; i < 32; i += 2) {
-                                    float p2[2];
+                                    for (int i = 0; i < 16; ++i) pk[i] = 0u;
+                                } else {
+                                    const int nv = kend - c * 32;
 #pragma unroll
-                                    for (int e = 0; e < 2; ++e) {
-                                        const int ii = i + e;
-                                        const float xx = fmaf(__uint_as_float(sv[c][ii]), scale_log2, -mo);
-                                        float p = (ii & 3) == 3 ? exp2_fma(xx) : fast_exp2(xx);
-                                        if (nv < 32 && ii >= nv) p = 0.f;
-                                        rsp[ii & 7] += p;
-                                        p2[e] = p;
+                                    for (int i = 0; i < 32; i += 2) {
+                                        float p2[2];
+#pragma unroll
+                                        for (int e = 0; e < 2; ++e) {
+                                            const int ii = i + e;
+                                            const float xx = fmaf(__uint_as_float(sv[c2][ii]), scale_log2, -mo);
+                                            float p = (ii & 3) == 3 ? exp2_fma(xx) : fast_exp2(xx);
+                                            if (nv < 32 && ii >= nv) p = 0.f;
+                                            rsp[ii & 7] += p;
+                                            p2[e] = p;
+                                        }
+                                        pk[i >> 1] = pack2(p2[0], p2[1], (T*)nullptr);
                                     }
-                                    pk[i >> 1] = pack2(p2[0], p2[1], (T*)nullptr);
                                 }
+                                tmem_st16(tP + 16 * c, pk);
                             }
-                            tmem_st16(tP + 16 * c, pk);
                         }
                         return ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
                     };
+                    // row max of the valid scores of this block (log2 units)
                     auto row_max = [&]() {
                         float mxp[8];
 #pragma unroll
                         for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            if (c * 32 >= kend) continue;
-                            const int nv = kend - c * 32;
+                        for (int hf = 0; hf < 2; ++hf) {
+                            if (hf * 64 >= kend) continue;
+                            load_half(hf);
 #pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                if (nv >= 32 || i < nv) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c][i]));
+                            for (int c2 = 0; c2 < 2; ++c2) {
+                                const int c = 2 * hf + c2;
+                                if (c * 32 >= kend) continue;
+                                const int nv = kend - c * 32;
+#pragma unroll
+                                for (int i = 0; i < 32; ++i)
+                                    if (nv >= 32 || i < nv) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c2][i]));
+                            }
                         }
                         const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                                                fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
@@ -838,7 +851,6 @@ __global__ void __maxnreg__(200)
                             ok = __all_sync(0xffffffffu, ok);
                             if (ok) {
                                 tc_fence_after();
-                                load_s();  // S again, from TMEM (keeps the registers free of a second copy)
                                 const float m_new = need ? fmaxf(m, row_max()) : m;
                                 const float alpha = fast_exp2(m - m_new);
                                 m = m_new;

@@ -13,15 +13,21 @@
 //    scalar operand have their own vector paths;
 //  * reductions over a contiguous last dim use one warp per row: 16-byte
 //    loads along the row, fp32 accumulation, a shuffle butterfly at the end;
-//    other reductions keep one thread per output, whose strided walk is
-//    coalesced across neighbouring outputs;
+//    reductions over the leading dim of a contiguous [len][n] tensor with few
+//    outputs (column sums) split the rows over CTAs (coalesced rows, a shared
+//    memory combine, fp32 partials from the stream-ordered pool, then a
+//    second pass); other reductions keep one thread per output, whose strided
+//    walk is coalesced across neighbouring outputs;
 //  * everything else (views with arbitrary strides, mixed dtypes) takes the
 //    generic strided kernels, with 32-bit index arithmetic when the element
 //    count allows.
 // Shapes and strides travel by value in the launch parameters (the reference
 // uploads them with a blocking cudaMemcpy per call, src/tensor_cuda_glue.cu:47-55),
 // so no op synchronises the host.
+#include <type_traits>
+
 #include "common.cuh"
+#include "memory_pool.h"
 #include "tensor_kernels.h"
 
 namespace cudasep {
@@ -278,6 +284,39 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const T* __restrict__ 
         float acc = OP == RED_MAX ? fmaxf(acc0, acc1) : acc0 + acc1;
         acc = OP == RED_MAX ? mbr::warp_max(acc) : mbr::warp_sum(acc);
         if (lane == 0) out[r] = fromf<T>(OP == RED_MEAN ? acc / (float)len : acc);
+    }
+}
+
+// Column partials: CTA (bx, by) reduces columns [32 bx, 32 bx + 32) over rows
+// by, by + gridDim.y, ... (each warp a strided subset, lanes = consecutive
+// columns) into part[by][col].
+template <typename T, int OP>
+__global__ void __launch_bounds__(256) reduce_cols_partial_kernel(const T* __restrict__ src, float* __restrict__ part,
+                                                                  int64_t len, int64_t n) {
+    __shared__ float sm[8][33];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t col = (int64_t)blockIdx.x * 32 + lane;
+    float acc = OP == RED_MAX ? -INFINITY : 0.f;
+    if (col < n)
+        for (int64_t r = (int64_t)blockIdx.y * 8 + w; r < len; r += (int64_t)gridDim.y * 8) {
+            const float v = tof(src[r * n + col]);
+            acc = OP == RED_MAX ? fmaxf(acc, v) : acc + v;
+        }
+    sm[w][lane] = acc;
+    __syncthreads();
+    if (w == 0) {
+#pragma unroll
+        for (int k = 1; k < 8; ++k) acc = OP == RED_MAX ? fmaxf(acc, sm[k][lane]) : acc + sm[k][lane];
+        if (col < n) part[(int64_t)blockIdx.y * n + col] = acc;
+    }
+}
+template <typename T, int OP>
+__global__ void reduce_cols_final_kernel(const float* __restrict__ part, T* __restrict__ out, int splits, int64_t len,
+                                         int64_t n) {
+    GRID_STRIDE(c, n) {
+        float acc = OP == RED_MAX ? -INFINITY : 0.f;
+        for (int k = 0; k < splits; ++k) acc = OP == RED_MAX ? fmaxf(acc, part[(int64_t)k * n + c]) : acc + part[(int64_t)k * n + c];
+        out[c] = fromf<T>(OP == RED_MEAN ? acc / (float)len : acc);
     }
 }
 
@@ -597,6 +636,29 @@ void reduce(int op, const void* src, int sdt, const int64_t* s_outer, int nd, co
                     reduce_rows_kernel<T, RED_MAX><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len, vec);
                     break;
             }
+        })) {
+        MBR_CUDA(cudaGetLastError());
+        return;
+    }
+    // leading dim of a contiguous [len][n_outer]: column partials over CTAs
+    if (nd == 1 && s_outer[0] == 1 && rstride == n_outer && sdt == odt && n_outer < (int64_t)sm_count() * 1024 &&
+        len >= 64 &&
+        with_float_type(sdt, [&](auto* t) {
+            using T = std::remove_pointer_t<decltype(t)>;
+            const int64_t bx = (n_outer + 31) / 32;
+            const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((len + 63) / 64,
+                                                                            (sm_count() * 8 + bx - 1) / bx));
+            float* part = (float*)CudaMemoryPool::instance().allocate(sizeof(float) * (size_t)splits * n_outer, st);
+            const dim3 g1((unsigned)bx, (unsigned)splits);
+            auto go = [&](auto opc) {
+                constexpr int OP = decltype(opc)::value;
+                reduce_cols_partial_kernel<T, OP><<<g1, 256, 0, st>>>((const T*)src, part, len, n_outer);
+                reduce_cols_final_kernel<T, OP><<<grid(n_outer), 256, 0, st>>>(part, (T*)out, splits, len, n_outer);
+            };
+            if (op == RED_SUM) go(std::integral_constant<int, RED_SUM>());
+            else if (op == RED_MEAN) go(std::integral_constant<int, RED_MEAN>());
+            else go(std::integral_constant<int, RED_MAX>());
+            CudaMemoryPool::instance().deallocate(part, st);  // reusable in stream order
         })) {
         MBR_CUDA(cudaGetLastError());
         return;

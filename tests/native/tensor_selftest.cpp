@@ -159,6 +159,93 @@ int main() {
     for (int j = 0; j < 12; ++j) s0[j] = h[j] + h[12 + j];
     expect(near(a.sum(0).to_cpu_f32(), s0), "sum dim0");
 
+    // vectorised paths (contiguous operands of one dtype, 16-byte vectors,
+    // tails, row / scalar broadcast, warp-per-row and column reductions),
+    // checked per dtype against host arithmetic on the stored values
+    for (DType dt : {DType::Float32, DType::Float16, DType::BFloat16}) {
+        const std::string tn = dt == DType::Float32 ? "f32" : dt == DType::Float16 ? "f16" : "bf16";
+        const float tol = dt == DType::Float32 ? 1e-5f : dt == DType::Float16 ? 2e-3f : 1.6e-2f;
+        for (int cols : {64, 70}) {  // 70: rows not a multiple of 8 elements (vector tails / scalar rows)
+            const int rows = 1000, n = rows * cols;
+            std::vector<float> hx(n), hy(n), hr(cols);
+            for (int i = 0; i < n; ++i) {
+                hx[i] = (float)((i * 37) % 101) / 16.0f - 3.0f;  // exact in every dtype
+                hy[i] = (float)((i * 53) % 89) / 32.0f + 0.5f;
+            }
+            for (int k = 0; k < cols; ++k) hr[k] = (float)(k % 7) / 4.0f + 1.0f;
+            Tensor x = Tensor::from_cpu_f32(hx.data(), {rows, cols}).to_dtype(dt);
+            Tensor y = Tensor::from_cpu_f32(hy.data(), {rows, cols}).to_dtype(dt);
+            Tensor r = Tensor::from_cpu_f32(hr.data(), {cols}).to_dtype(dt);
+            Tensor s1 = Tensor::full({1}, 0.75f, dt);
+            const std::string tag = " " + tn + " [1000 x " + std::to_string(cols) + "]";
+            std::vector<float> e_add(n), e_div(n), e_row(n), e_sc(n), e_cl(n);
+            for (int i = 0; i < n; ++i) {
+                e_add[i] = hx[i] + hy[i];
+                e_div[i] = hx[i] / hy[i];
+                e_row[i] = hx[i] * hr[i % cols];
+                e_sc[i] = hx[i] - 0.75f;
+                e_cl[i] = std::min(1.0f, std::max(-1.0f, hx[i] * 0.5f));
+            }
+            expect(near((x + y).to_f32().to_cpu_f32(), e_add, tol), "vec add" + tag);
+            expect(near((x / y).to_f32().to_cpu_f32(), e_div, tol), "vec div" + tag);
+            expect(near((x * r).to_f32().to_cpu_f32(), e_row, tol), "vec row broadcast" + tag);
+            expect(near((x - s1).to_f32().to_cpu_f32(), e_sc, tol), "vec scalar broadcast" + tag);
+            Tensor xc = x.clone();
+            xc.mul_scalar_(0.5f).clamp_(-1.0f, 1.0f);
+            expect(near(xc.to_f32().to_cpu_f32(), e_cl, tol), "vec scalar ops" + tag);
+            expect(near(x.to_f32().to_cpu_f32(), hx, 0.f), "vec convert" + tag);
+            std::vector<float> e_sum(rows), e_max(rows), e_col(cols, 0.f), e_cmax(cols, -1e30f);
+            for (int i = 0; i < rows; ++i) {
+                float acc = 0.f, m = -1e30f;
+                for (int k = 0; k < cols; ++k) {
+                    acc += hx[i * cols + k];
+                    m = std::max(m, hx[i * cols + k]);
+                    e_col[k] += hx[i * cols + k];
+                    e_cmax[k] = std::max(e_cmax[k], hx[i * cols + k]);
+                }
+                e_sum[i] = acc;
+                e_max[i] = m;
+            }
+            // sums are rounded once to the output dtype: compare relative to the sum's scale
+            const float stol = dt == DType::Float32 ? 1e-4f : dt == DType::Float16 ? 1e-3f : 8e-3f;
+            expect(near(x.sum(-1).to_f32().to_cpu_f32(), e_sum, stol), "row sum" + tag);
+            expect(near(x.max(-1).to_f32().to_cpu_f32(), e_max, 0.f), "row max" + tag);
+            expect(near(x.sum(0).to_f32().to_cpu_f32(), e_col, stol), "column sum" + tag);
+            expect(near(x.max(0).to_f32().to_cpu_f32(), e_cmax, 0.f), "column max" + tag);
+        }
+    }
+
+    // stream order of the pool: a block freed on one stream and taken on
+    // another is handed over behind an event, with no host wait
+    {
+        cudaStream_t s1, s2;
+        CUDA_CHECK(cudaStreamCreateWithFlags(&s1, cudaStreamNonBlocking));
+        CUDA_CHECK(cudaStreamCreateWithFlags(&s2, cudaStreamNonBlocking));
+        auto& pool = cudasep::CudaMemoryPool::instance();
+        const size_t nb = 3 << 20;
+        void* p = pool.allocate(nb, s1);
+        CUDA_CHECK(cudaMemsetAsync(p, 0x11, nb, s1));
+        pool.deallocate(p, s1);
+        const auto st0 = pool.get_stats();
+        void* q = pool.allocate(nb, s2);
+        const auto st1 = pool.get_stats();
+        expect(q == p && st1.cross_stream_reuses == st0.cross_stream_reuses + 1, "pool cross-stream reuse");
+        CUDA_CHECK(cudaMemsetAsync(q, 0x22, nb, s2));
+        std::vector<unsigned char> back(nb);
+        CUDA_CHECK(cudaMemcpyAsync(back.data(), q, nb, cudaMemcpyDeviceToHost, s2));
+        CUDA_CHECK(cudaStreamSynchronize(s2));
+        bool all22 = true;
+        for (unsigned char c : back) all22 = all22 && c == 0x22;
+        expect(all22, "pool cross-stream reuse ordered behind the free");
+        pool.deallocate(q, s2);
+        void* r2 = pool.allocate(nb, s2);  // same stream: no event wait
+        expect(r2 == q && pool.get_stats().cross_stream_reuses == st1.cross_stream_reuses, "pool same-stream reuse");
+        pool.deallocate(r2, s2);
+        CUDA_CHECK(cudaStreamSynchronize(s2));
+        CUDA_CHECK(cudaStreamDestroy(s1));
+        CUDA_CHECK(cudaStreamDestroy(s2));
+    }
+
     // copy_from
     Tensor d = Tensor::empty({24});
     d.copy_from(a);
