@@ -208,6 +208,25 @@ MBR_API int mbr_wav_info(const char* path, int* sample_rate, int* channels, int6
 MBR_API int mbr_wav_read(const char* path, float* h_planar, int64_t capacity);
 MBR_API int mbr_wav_write(const char* path, const float* h_planar, int channels, int64_t frames, int sample_rate);
 
+/* ---- WAV I/O with the sample conversion on the GPU ------------------------
+ * The reference converts samples on the host (src/audio_io.cpp:200-334).
+ * mbr_pcm_to_planar: interleaved PCM bytes already in device memory
+ * ([frames][channels], 16 / 24 / 32-bit integer or, with is_float, 32-bit
+ * float) -> planar fp32 d_planar [channels][frames], integer PCM scaled by
+ * 1/2^(bits-1): the same values the host reader gives.
+ * mbr_wav_read_device: parses the file on the host, uploads its data chunk
+ * as raw bytes and converts it on the device into d_planar (capacity in
+ * floats); with d_planar == NULL it only reports the format.  Synchronises
+ * `stream` before returning.
+ * mbr_wav_write_device: interleaves d_planar [channels][frames] on the device
+ * and writes a float32 WAV (synchronises `stream`). */
+MBR_API int mbr_pcm_to_planar(const void* d_pcm, int64_t frames, int channels, int bits, int is_float,
+                              float* d_planar, void* stream);
+MBR_API int mbr_wav_read_device(const char* path, float* d_planar, int64_t capacity, int* sample_rate, int* channels,
+                                int64_t* frames, void* stream);
+MBR_API int mbr_wav_write_device(const char* path, const float* d_planar, int channels, int64_t frames,
+                                 int sample_rate, void* stream);
+
 /* ---- stand-alone ops in the reference op library's layouts ------------
  * All buffers are device memory; dtype is MBR_FP32 / MBR_FP16 / MBR_BF16;
  * element counts of the elementwise ops are multiples of 8. */

@@ -343,6 +343,14 @@ __global__ void __maxnreg__(168)
             pos = q0 + r;
             valid = pos < L;
         }
+        // this row's token and gate, loaded now so the load is long done by the epilogue
+        int64_t tok = 0;
+        float gate = 1.0f;
+        if (valid) {
+            const int64_t s = sh / H;
+            tok = mode == ops::SEQ_TIME ? ((s / NB) * Tn + pos) * NB + (s % NB) : s * NB + pos;
+            if (gates) gate = __ldg(gates + tok * H + sh % H);
+        }
         float m = 0.f, l = 0.f;
         for (int j = 0; j < nkv; ++j) {
             const int g = tl * nkv + j;
@@ -464,11 +472,7 @@ __global__ void __maxnreg__(168)
             tmem_ld_wait();
             if (valid) {
                 const int hd = sh % H;
-                const int64_t s = sh / H;
-                int64_t tok;
-                if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
-                else tok = s * NB + pos;
-                const float gs = (gates ? gates[tok * H + hd] : 1.0f) / l;
+                const float gs = gate / l;
                 uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH);
 #pragma unroll
                 for (int q = 0; q < DH / 8; ++q) {
@@ -757,6 +761,14 @@ __global__ void __launch_bounds__(320, 1)
             const int qs = q0 + QT * x;
             const int pos = qs + r;
             const bool wact = qs + 32 * qw < L;  // this warp has valid query rows
+            // this row's token and gate, loaded now so the load is long done by the epilogue
+            int64_t tok = 0;
+            float gate = 1.0f;
+            if (pos < L) {
+                const int64_t s = sh / H;
+                tok = mode == ops::SEQ_TIME ? ((s / NB) * Tn + pos) * NB + (s % NB) : s * NB + pos;
+                if (gates) gate = __ldg(gates + tok * H + sh % H);
+            }
             float m = 0.f, l = 0.f;
             for (int j = 0; j < nkv; ++j) {
                 ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_s[x], cnt & 1, err));
@@ -890,11 +902,7 @@ __global__ void __launch_bounds__(320, 1)
                 tmem_ld_wait();
                 if (pos < L) {
                     const int hd = sh % H;
-                    const int64_t s = sh / H;
-                    int64_t tok;
-                    if (mode == ops::SEQ_TIME) tok = ((s / NB) * Tn + pos) * NB + (s % NB);
-                    else tok = s * NB + pos;
-                    const float gs = (gates ? gates[tok * H + hd] : 1.0f) / l;
+                    const float gs = gate / l;
                     uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH);
 #pragma unroll
                     for (int q = 0; q < DH / 8; ++q) {

@@ -23,10 +23,19 @@ void put32(std::ofstream& f, uint32_t v) {
 
 }  // namespace
 
-HostAudio read_wav_host(const std::string& path) {
+std::vector<uint8_t> read_file(const std::string& path) {
     std::ifstream f(path, std::ios::binary);
     if (!f) throw std::runtime_error("Failed to open WAV file: " + path);
-    std::vector<uint8_t> buf((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    return std::vector<uint8_t>((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+}
+
+WavLayout parse_wav(const uint8_t* bytes, size_t size, const std::string& path) {
+    struct View {
+        const uint8_t* p;
+        size_t n;
+        size_t size() const { return n; }
+        const uint8_t* data() const { return p; }
+    } buf{bytes, size};
     if (buf.size() < 12 || std::memcmp(buf.data(), "RIFF", 4) != 0)
         throw std::runtime_error("Not a valid WAV file (missing RIFF header): " + path);
     if (std::memcmp(buf.data() + 8, "WAVE", 4) != 0)
@@ -61,11 +70,27 @@ HostAudio read_wav_host(const std::string& path) {
         throw std::runtime_error("Unsupported PCM bit depth: " + std::to_string(bits) + ": " + path);
     if (fmt == 3 && bits != 32) throw std::runtime_error("Unsupported float bit depth: " + std::to_string(bits) + ": " + path);
     if (ch == 0) throw std::runtime_error("WAV file has zero channels: " + path);
+    WavLayout w;
+    w.format = fmt;
+    w.channels = ch;
+    w.bits = bits;
+    w.sample_rate = (int)sr;
+    w.data_off = (size_t)(data - buf.data());
+    w.frames = (int64_t)(data_size / ((size_t)(bits / 8) * ch));
+    w.data_bytes = (size_t)w.frames * (bits / 8) * ch;
+    return w;
+}
+
+HostAudio read_wav_host(const std::string& path) {
+    std::vector<uint8_t> buf = read_file(path);
+    const WavLayout w = parse_wav(buf.data(), buf.size(), path);
+    const int fmt = w.format, bits = w.bits, ch = w.channels;
+    const uint8_t* data = buf.data() + w.data_off;
     const int bps = bits / 8;
     HostAudio a;
-    a.sample_rate = (int)sr;
+    a.sample_rate = w.sample_rate;
     a.channels = ch;
-    a.frames = (int64_t)(data_size / ((size_t)bps * ch));
+    a.frames = w.frames;
     a.planar.resize((size_t)a.frames * ch);
     for (int64_t i = 0; i < a.frames; ++i)
         for (int c = 0; c < ch; ++c) {
@@ -88,6 +113,13 @@ HostAudio read_wav_host(const std::string& path) {
 }
 
 void write_wav_host(const std::string& path, const float* planar, int ch, int64_t frames, int sr) {
+    std::vector<float> inter((size_t)frames * ch);
+    for (int64_t i = 0; i < frames; ++i)
+        for (int c = 0; c < ch; ++c) inter[(size_t)i * ch + c] = planar[(size_t)c * frames + i];
+    write_wav_interleaved(path, inter.data(), ch, frames, sr);
+}
+
+void write_wav_interleaved(const std::string& path, const float* inter, int ch, int64_t frames, int sr) {
     std::ofstream f(path, std::ios::binary);
     if (!f) throw std::runtime_error("Failed to create WAV file: " + path);
     const uint32_t data_bytes = (uint32_t)(frames * ch * 4);
@@ -104,10 +136,7 @@ void write_wav_host(const std::string& path, const float* planar, int ch, int64_
     put16(f, 32);
     f.write("data", 4);
     put32(f, data_bytes);
-    std::vector<float> inter((size_t)frames * ch);
-    for (int64_t i = 0; i < frames; ++i)
-        for (int c = 0; c < ch; ++c) inter[(size_t)i * ch + c] = planar[(size_t)c * frames + i];
-    f.write((const char*)inter.data(), (std::streamsize)inter.size() * 4);
+    f.write((const char*)inter, (std::streamsize)((size_t)frames * ch * 4));
     if (!f) throw std::runtime_error("Failed to write WAV file: " + path);
 }
 

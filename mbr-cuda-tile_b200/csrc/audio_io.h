@@ -31,6 +31,20 @@ struct HostAudio {
     std::vector<float> planar;  // [channels][frames]
 };
 HostAudio read_wav_host(const std::string& path);
+
+// The fmt and data chunks of a WAV file held in memory (validated as
+// read_wav_host validates them): data_off / data_bytes locate the interleaved
+// samples in `bytes`; format 1 = integer PCM, 3 = IEEE float.
+struct WavLayout {
+    int format = 0, channels = 0, bits = 0, sample_rate = 0;
+    size_t data_off = 0, data_bytes = 0;
+    int64_t frames = 0;
+};
+WavLayout parse_wav(const uint8_t* bytes, size_t size, const std::string& what);
+std::vector<uint8_t> read_file(const std::string& path);
 void write_wav_host(const std::string& path, const float* planar, int channels, int64_t frames, int sample_rate);
+// Float WAV from samples already interleaved [frames][channels].
+void write_wav_interleaved(const std::string& path, const float* interleaved, int channels, int64_t frames,
+                           int sample_rate);
 
 }  // namespace cudasep

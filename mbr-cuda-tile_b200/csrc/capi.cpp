@@ -11,6 +11,7 @@
 #include "../../include/mbr_b200.h"
 #include "common.h"
 #include "model.h"
+#include "audio_device.h"
 #include "audio_io.h"
 #include "ops_api.h"
 #include "separator.h"
@@ -453,6 +454,66 @@ MBR_API int mbr_wav_write(const char* path, const float* h_planar, int channels,
     return guard([&] {
         need(path && h_planar && channels > 0 && frames >= 0 && sample_rate > 0, "bad argument");
         cudasep::write_wav_host(path, h_planar, channels, frames, sample_rate);
+    });
+}
+
+MBR_API int mbr_pcm_to_planar(const void* d_pcm, int64_t frames, int channels, int bits, int is_float,
+                              float* d_planar, void* stream) {
+    return guard([&] {
+        need(d_pcm && d_planar && frames >= 0 && channels > 0, "bad argument");
+        mbr::audio::pcm_to_planar(d_pcm, frames, channels, bits, is_float != 0, d_planar, (cudaStream_t)stream);
+    });
+}
+
+MBR_API int mbr_wav_read_device(const char* path, float* d_planar, int64_t capacity, int* sample_rate, int* channels,
+                                int64_t* frames, void* stream) {
+    return guard([&] {
+        need(path && sample_rate && channels && frames, "null argument");
+        std::vector<uint8_t> bytes = cudasep::read_file(path);
+        const cudasep::WavLayout w = cudasep::parse_wav(bytes.data(), bytes.size(), path);
+        *sample_rate = w.sample_rate;
+        *channels = w.channels;
+        *frames = w.frames;
+        if (!d_planar) return;  // size query
+        need(w.frames * w.channels <= capacity, "mbr_wav_read_device: buffer too small");
+        if (w.frames == 0) return;
+        cudaStream_t st = (cudaStream_t)stream;
+        // the data chunk's raw bytes go up once; conversion happens on the device
+        void* d_pcm = nullptr;
+        MBR_CUDA(cudaMallocAsync(&d_pcm, w.data_bytes, st));
+        try {
+            MBR_CUDA(cudaMemcpyAsync(d_pcm, bytes.data() + w.data_off, w.data_bytes, cudaMemcpyHostToDevice, st));
+            mbr::audio::pcm_to_planar(d_pcm, w.frames, w.channels, w.bits, w.format == 3, d_planar, st);
+        } catch (...) {
+            cudaFreeAsync(d_pcm, st);
+            throw;
+        }
+        MBR_CUDA(cudaFreeAsync(d_pcm, st));
+        MBR_CUDA(cudaStreamSynchronize(st));  // `bytes` is released on return
+    });
+}
+
+MBR_API int mbr_wav_write_device(const char* path, const float* d_planar, int channels, int64_t frames,
+                                 int sample_rate, void* stream) {
+    return guard([&] {
+        need(path && d_planar && channels > 0 && frames >= 0 && sample_rate > 0, "bad argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        std::vector<float> inter((size_t)frames * channels);
+        if (frames > 0) {
+            float* d_inter = nullptr;
+            MBR_CUDA(cudaMallocAsync((void**)&d_inter, sizeof(float) * inter.size(), st));
+            try {
+                mbr::audio::planar_to_interleaved(d_planar, frames, channels, d_inter, st);
+                MBR_CUDA(cudaMemcpyAsync(inter.data(), d_inter, sizeof(float) * inter.size(), cudaMemcpyDeviceToHost,
+                                         st));
+            } catch (...) {
+                cudaFreeAsync(d_inter, st);
+                throw;
+            }
+            MBR_CUDA(cudaFreeAsync(d_inter, st));
+            MBR_CUDA(cudaStreamSynchronize(st));
+        }
+        cudasep::write_wav_interleaved(path, inter.data(), channels, frames, sample_rate);
     });
 }
 

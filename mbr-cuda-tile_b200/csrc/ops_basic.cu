@@ -127,7 +127,7 @@ __device__ __forceinline__ void store4(T* p, float4 y) {
 // staged in shared memory once per CTA).  Each lane holds up to MAXC float4
 // chunks of the row in registers.  D % 4 == 0, D <= 128 * MAXC, H <= 32.
 template <typename T, int MAXC>
-__global__ void __launch_bounds__(256, 3) rms_norm_kernel(const float* __restrict__ R, int64_t M, int D,
+__global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restrict__ R, int64_t M, int D,
                                                           const float* __restrict__ gamma, float scale,
                                                           T* __restrict__ xn, int64_t band_major_mt, int NB,
                                                           float* r_out, const float* __restrict__ wg,
@@ -148,21 +148,35 @@ __global__ void __launch_bounds__(256, 3) rms_norm_kernel(const float* __restric
     const float4* h4 = reinterpret_cast<const float4*>(gamma2);
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    // software pipeline: the next row pair's loads are in flight while this
+    // pair is reduced, normalised and stored
+    float4 nx[2][MAXC];
+    auto load_pair = [&](int64_t mp) {
+        const bool two_p = mp + 1 < M;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float4* x4 = reinterpret_cast<const float4*>(R + (mp + (r && two_p ? 1 : 0)) * D);
+#pragma unroll
+            for (int i = 0; i < MAXC; ++i) {
+                const int c = lane + 32 * i;
+                nx[r][i] = c < D4 ? __ldcs(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    };
+    if (2 * wid < M) load_pair(2 * wid);
     for (int64_t m0 = 2 * wid; m0 < M; m0 += 2 * warps) {
         const bool two = m0 + 1 < M;
         float4 v[2][MAXC];
         float ss[2] = {0.f, 0.f};
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const float4* x4 = reinterpret_cast<const float4*>(R + (m0 + (r && two ? 1 : 0)) * D);
+        for (int r = 0; r < 2; ++r)
 #pragma unroll
             for (int i = 0; i < MAXC; ++i) {
-                const int c = lane + 32 * i;
-                v[r][i] = c < D4 ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[r][i] = nx[r][i];
                 ss[r] += v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y + v[r][i].z * v[r][i].z +
                          v[r][i].w * v[r][i].w;
             }
-        }
+        if (m0 + 2 * warps < M) load_pair(m0 + 2 * warps);
         ss[0] = warp_sum(ss[0]);
         ss[1] = warp_sum(ss[1]);
 #pragma unroll
@@ -603,7 +617,7 @@ void rms_norm(const float* R, int64_t M, int D, const float* gamma, float scale,
         MBR_CUDA(cudaGetDevice(&dev));
         MBR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     }
-    unsigned grid = (unsigned)std::min<int64_t>(ceil_div(M, 16), (int64_t)sms * 6);  // 2 rows per warp, 3 blocks / SM x 2 waves
+    unsigned grid = (unsigned)std::min<int64_t>(ceil_div(M, 16), (int64_t)sms * 2);  // 2 rows per warp, 2 resident CTAs per SM
     MBR_DISPATCH_DTYPE(dtype, T, {
         auto run = [&](auto kern) {
             if (sm > 48 * 1024)

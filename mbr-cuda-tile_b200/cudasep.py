@@ -33,6 +33,7 @@ EXPORTS = [
     "mbr_rope_tables",
     "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft", "mbr_op_istft_noalloc",
     "mbr_plan_shard", "mbr_wav_info", "mbr_wav_read", "mbr_wav_write",
+    "mbr_pcm_to_planar", "mbr_wav_read_device", "mbr_wav_write_device",
 ]
 
 # Kernel classes of mbr_profile_read.
@@ -99,6 +100,10 @@ def lib():
         L.mbr_wav_info.argtypes = [ctypes.c_char_p, ctypes.POINTER(c_int), ctypes.POINTER(c_int), i64p]
         L.mbr_wav_read.argtypes = [ctypes.c_char_p, fp, i64]
         L.mbr_wav_write.argtypes = [ctypes.c_char_p, fp, c_int, i64, c_int]
+        L.mbr_pcm_to_planar.argtypes = [vp, i64, c_int, c_int, c_int, fp, vp]
+        L.mbr_wav_read_device.argtypes = [ctypes.c_char_p, fp, i64, ctypes.POINTER(c_int), ctypes.POINTER(c_int),
+                                          i64p, vp]
+        L.mbr_wav_write_device.argtypes = [ctypes.c_char_p, fp, c_int, i64, c_int, vp]
         _lib = L
     return _lib
 
@@ -239,6 +244,34 @@ def plan_shard_window(N: int, chunk_size: int, overlap: float, default_overlap: 
     _check(lib().mbr_plan_shard_window(int(N), int(chunk_size), float(overlap), int(default_overlap), rank, world,
                                        ctypes.byref(lo), ctypes.byref(hi)))
     return lo.value, hi.value
+
+
+def wav_read_device(path: str, stream=None):
+    """WAV file -> (planar float32 CUDA tensor [channels, frames], sample_rate),
+    the samples converted on the GPU."""
+    import torch
+
+    sr, ch, n = ctypes.c_int(), ctypes.c_int(), ctypes.c_int64()
+    _check(lib().mbr_wav_read_device(path.encode(), None, 0, ctypes.byref(sr), ctypes.byref(ch), ctypes.byref(n),
+                                     _stream(stream)))
+    out = torch.empty((ch.value, n.value), dtype=torch.float32, device="cuda")
+    _check(lib().mbr_wav_read_device(path.encode(), _ptr(out), out.numel(), ctypes.byref(sr), ctypes.byref(ch),
+                                     ctypes.byref(n), _stream(stream)))
+    return out, sr.value
+
+
+def wav_write_device(path: str, planar, sample_rate: int, stream=None) -> None:
+    """planar float32 CUDA tensor [channels, frames] -> float32 WAV file."""
+    ch, n = planar.shape
+    _check(lib().mbr_wav_write_device(path.encode(), _ptr(planar.contiguous()), ch, n, int(sample_rate),
+                                      _stream(stream)))
+
+
+def pcm_to_planar(d_pcm, frames: int, channels: int, bits: int, is_float: bool, out, stream=None):
+    """Interleaved PCM bytes on the device (uint8 CUDA tensor) -> out [channels, frames] float32."""
+    _check(lib().mbr_pcm_to_planar(_ptr(d_pcm), int(frames), int(channels), int(bits), int(is_float), _ptr(out),
+                                   _stream(stream)))
+    return out
 
 
 SHARD_KEYS = ["c0", "c1", "lo", "hi", "send_lo", "out_lo", "out_hi", "n_chunks", "step", "border", "total"]
