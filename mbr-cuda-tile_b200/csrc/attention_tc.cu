@@ -863,7 +863,10 @@ __global__ void __launch_bounds__(320, 1)
                             ok = __all_sync(0xffffffffu, ok);
                             if (ok) {
                                 tc_fence_after();
-                                const float m_new = need ? fmaxf(m, row_max()) : m;
+                                // row_max reads S with warp-collective TMEM loads: every
+                                // lane calls it, each then keeps or raises its own offset
+                                const float mx = row_max();
+                                const float m_new = need ? fmaxf(m, mx) : m;
                                 const float alpha = fast_exp2(m - m_new);
                                 m = m_new;
                                 l *= alpha;
