@@ -1137,6 +1137,35 @@ int orc_istft(const float* spec, int64_t n_sig, int64_t T, int n_fft, int hop, i
     });
 }
 
+// softmax(q k^T * scale) v per slice, as the transformer's attention above
+// computes it (src/mbr_cuda_tile.cu:6419-6462 is the reference's op).
+int orc_attention(const float* q, const float* k, const float* v, int64_t nsh, int64_t L, int dh, float scale,
+                  float* out) {
+    return guard([&] {
+        if (nsh <= 0 || L <= 0 || dh <= 0) throw std::runtime_error("orc_attention: bad shape");
+        parallel_for(nsh * L, [&](int64_t si) {
+            const int64_t s = si / L, i = si % L;
+            const float* qi = q + (s * L + i) * dh;
+            std::vector<double> p(L);
+            double mx = -1e300;
+            for (int64_t j = 0; j < L; ++j) {
+                const float* kj = k + (s * L + j) * dh;
+                double sc = 0;
+                for (int d = 0; d < dh; ++d) sc += (double)qi[d] * kj[d];
+                p[j] = sc * (double)scale;
+                mx = std::max(mx, p[j]);
+            }
+            double sum = 0;
+            for (int64_t j = 0; j < L; ++j) sum += (p[j] = std::exp(p[j] - mx));
+            for (int d = 0; d < dh; ++d) {
+                double o = 0;
+                for (int64_t j = 0; j < L; ++j) o += p[j] * v[(s * L + j) * dh + d];
+                out[(s * L + i) * dh + d] = (float)(o / sum);
+            }
+        });
+    });
+}
+
 void* orc_model_load(const char* path, int weight_dtype) {
     Model* m = nullptr;
     int rc = guard([&] { m = new Model(load_model(path, weight_dtype)); });

@@ -44,6 +44,13 @@ int orc_stft(const float* sig, int64_t n_sig, int64_t L, int n_fft, int hop,
 int orc_istft(const float* spec, int64_t n_sig, int64_t T, int n_fft, int hop,
               int64_t length, float* out, int64_t* len_out);
 
+/* Scaled dot-product attention of nsh independent (sequence, head) slices:
+ * q, k, v, out [nsh][L][dh]; out = softmax(q k^T * scale) v with fp64 sums and
+ * an exact softmax (the attention inside orc_forward, exposed alone so it can
+ * be checked against the reference's own attention validators). */
+int orc_attention(const float* q, const float* k, const float* v, int64_t nsh, int64_t L, int dh, float scale,
+                  float* out);
+
 /* Model handle: loads a .csm file.  weight_dtype: 0 = use weights as stored,
  * 1 = round every 2-D fp32 tensor to fp16, 3 = round to bf16 (this restates
  * ModelWeights::convert_linear_weights_to_{fp16,bf16}, src/weights.cu:511-540),

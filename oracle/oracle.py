@@ -48,6 +48,7 @@ def lib():
         L.orc_chunk_plan.argtypes = [ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int, i64p,
                                      ctypes.c_int64, i64p, i64p, i64p]
         L.orc_set_threads.argtypes = [ctypes.c_int]
+        L.orc_attention.argtypes = [fp, fp, fp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_float, fp]
         L.orc_get_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -106,6 +107,16 @@ def istft(spec: np.ndarray, n_fft=2048, hop=441, length=-1) -> np.ndarray:
     out = np.zeros((n, int(lo[0])), np.float32)
     _check(lib().orc_istft(_fp(spec), n, T, n_fft, hop, length, _fp(out), _ip(lo)))
     return out.reshape(*lead, int(lo[0]))
+
+
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.ndarray:
+    """softmax(q k^T * scale) v over [..., L, dh] slices (fp64 sums)."""
+    q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    L, dh = q.shape[-2:]
+    nsh = int(np.prod(q.shape[:-2])) if q.ndim > 2 else 1
+    out = np.empty_like(q)
+    _check(lib().orc_attention(_fp(q), _fp(k), _fp(v), nsh, L, dh, scale, _fp(out)))
+    return out
 
 
 def chunk_plan(N, chunk_size, overlap, default_overlap):

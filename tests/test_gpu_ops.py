@@ -305,3 +305,25 @@ def test_linear_op(torch_cuda, dtype, rows, fin, fout, act):
     bound = TOL[dtype] * np.maximum(np.abs(ref), 1e-3) * 1.01 + acc + 1e-6
     err = np.abs(got - ref)
     assert np.all(err <= bound), f"linear {dtype} {rows}x{fin}x{fout} act {act}: max err/bound {(err / bound).max():.3f}"
+
+
+@pytest.mark.parametrize("dtype,L", [("bf16", 1301), ("bf16", 60), ("fp16", 1301), ("fp16", 60)])
+def test_attention_matches_reference_validators(torch_cuda, dtype, L):
+    """mbr_op_attention on the reference's own validator inputs (the time-axis
+    tcgen05 kernel at L = 1301, the packed band-axis kernel at L = 60) against
+    the restated validators: within 2 bf16 ulps (both round probabilities and
+    outputs to 16 bits, in different places)."""
+    torch = torch_cuda
+    import attn_validators as av
+    import cudasep
+
+    x = av.inputs(L)
+    t = torch.from_numpy(x).to(_tdt(torch, dtype))[None, None].cuda()
+    got = cudasep.op_attention(t, t, t, 0.125).float().cpu().numpy()[0]
+    if L > 64:
+        ref = av.time_rows(x)
+        err = max(av.err_ulps(got[r], ref[r]) for r in ref)
+    else:
+        err = av.err_ulps(got, av.band_rows(x))
+    print(f"attention {dtype} L={L} vs the reference validator: {err:.2f} bf16 ulps")
+    assert err <= 2.0, err

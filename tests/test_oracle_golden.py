@@ -142,3 +142,22 @@ def test_oracle_reference_bf16_mode(make_csm):
     assert np.array_equal(a, b) and np.isfinite(a).all()
     s = snr_db(exact, a)
     assert 30.0 <= s <= 55.0, s
+
+
+@pytest.mark.parametrize("L", [1301, 60])
+def test_oracle_attention_matches_reference_validators(L):
+    """The oracle's attention against the reference's own CPU attention
+    validators (restated in tests/attn_validators.py) on their deterministic
+    inputs: within one bf16 ulp (the validators round their probabilities and
+    outputs to bf16; measured 0.52 ulp)."""
+    import oracle
+    import attn_validators as av
+
+    x = av.inputs(L)
+    got = oracle.attention(x[None], x[None], x[None], 0.125)[0]
+    if L > 64:
+        ref = av.time_rows(x)
+        err = max(av.err_ulps(got[r], ref[r]) for r in ref)
+    else:
+        err = av.err_ulps(got, av.band_rows(x))
+    assert err <= 1.0, err
