@@ -285,6 +285,9 @@ def main():
     ap.add_argument("--op-sweep", action="store_true",
                     help="tensor-op sweep: achieved HBM GB/s of every stand-alone op over [B*801*60, D] activations "
                          "(one JSON line per case, then a summary line)")
+    ap.add_argument("--ops", default="", help="op sweep: comma-separated ops to run (default all)")
+    ap.add_argument("--dtypes", default="fp32,fp16,bf16", help="op sweep: comma-separated dtypes")
+    ap.add_argument("--batches", default="1,4,8", help="op sweep: comma-separated B values")
     ap.add_argument("--tensor-sweep", action="store_true",
                     help="Tensor API op sweep: achieved HBM GB/s of the Tensor class's elementwise, broadcast, "
                          "conversion and reduction kernels over the same activations (runs the native "
@@ -600,6 +603,11 @@ def run_op_sweep(args):
 
     results = []
 
+    want_ops = set(o for o in args.ops.split(",") if o)
+
+    def want(op):
+        return not want_ops or op in want_ops
+
     def report(op, dtype, D, B, nbytes, sec):
         gbs = nbytes / sec / 1e9
         line = {"op": op, "dtype": dtype, "D": D, "B": B, "bytes": int(nbytes), "us": sec * 1e6, "GB/s": gbs,
@@ -612,40 +620,48 @@ def run_op_sweep(args):
         cfg = csm_tool.base_config(**csm_tool.PRESETS["tiny"])
         csm_tool.write_csm(csm, cfg, csm_tool.random_weights(cfg, 0))
         model = cudasep.Model(csm, 0, "fp32")
-        for dtype in ("fp32", "fp16", "bf16"):
+        for dtype in [d for d in args.dtypes.split(",") if d]:
             dt, e = tdt[dtype], torch.tensor([], dtype=tdt[dtype]).element_size()
-            for B in (1, 4, 8):
+            for B in [int(b) for b in args.batches.split(",") if b]:
                 rows = B * T * NB
-                for D in (192, 384, 512):
+                for D in ((192, 384, 512) if any(want(o) for o in ("rms_norm", "add", "gelu", "sigmoid_gate", "rope"))
+                          else ()):
                     N = rows * D
                     x = torch.randn(rows, D, generator=gen, device="cuda").to(dt)
                     y = torch.empty_like(x)
                     gamma = torch.ones(D, device="cuda")
-                    report("rms_norm", dtype, D, B, 2 * N * e + D * 4,
-                           timed(lambda: cudasep.op_rms_norm(x, gamma, D ** 0.5, y=y)))
-                    x2 = torch.randn(rows, D, generator=gen, device="cuda").to(dt)
-                    report("add", dtype, D, B, 3 * N * e, timed(lambda: cudasep.op_add(x, x2, y=y)))
-                    del x2
-                    report("gelu", dtype, D, B, 2 * N * e, timed(lambda: cudasep.op_gelu(x, y=y)))
+                    if want("rms_norm"):
+                        report("rms_norm", dtype, D, B, 2 * N * e + D * 4,
+                               timed(lambda: cudasep.op_rms_norm(x, gamma, D ** 0.5, y=y)))
+                    if want("add"):
+                        x2 = torch.randn(rows, D, generator=gen, device="cuda").to(dt)
+                        report("add", dtype, D, B, 3 * N * e, timed(lambda: cudasep.op_add(x, x2, y=y)))
+                        del x2
+                    if want("gelu"):
+                        report("gelu", dtype, D, B, 2 * N * e, timed(lambda: cudasep.op_gelu(x, y=y)))
                     H = D // 64
                     gate = torch.rand(rows, H, generator=gen, device="cuda").to(dt)
-                    report("sigmoid_gate", dtype, D, B, 2 * N * e + rows * H * e,
-                           timed(lambda: cudasep.op_sigmoid_gate(x, gate, H, y=y)))
+                    if want("sigmoid_gate"):
+                        report("sigmoid_gate", dtype, D, B, 2 * N * e + rows * H * e,
+                               timed(lambda: cudasep.op_sigmoid_gate(x, gate, H, y=y)))
                     c, s_ = cudasep.rope_tables(T, 64)
                     ct, st = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
                     xr, yr = x.view(B * NB, T, H, 64), y.view(B * NB, T, H, 64)
-                    report("rope", dtype, D, B, 2 * N * e + 2 * c.nbytes,
-                           timed(lambda: cudasep.op_rope(xr, ct, st, y=yr)))
+                    if want("rope"):
+                        report("rope", dtype, D, B, 2 * N * e + 2 * c.nbytes,
+                               timed(lambda: cudasep.op_rope(xr, ct, st, y=yr)))
                     del x, y, gate
                 # band ops (independent of D)
                 spec = torch.randn(B, 2, 1025, T, 2, generator=gen, device="cuda")
                 xb = torch.empty(B, T, J2, dtype=dt, device="cuda")
-                report("band_gather", dtype, 0, B, spec.numel() * 4 + xb.numel() * e,
-                       timed(lambda: model.op_band_gather(spec, out_dtype=dt)))
+                if want("band_gather"):
+                    report("band_gather", dtype, 0, B, spec.numel() * 4 + xb.numel() * e,
+                           timed(lambda: model.op_band_gather(spec, out_dtype=dt)))
                 masks = torch.randn(1, B * T, J2, generator=gen, device="cuda").to(dt)
-                report("mask_scatter", dtype, 0, B,
-                       masks.numel() * e + spec.numel() * 4 + 1025 * 4 + B * 2 * 1025 * T * 2 * 4,
-                       timed(lambda: model.op_mask_scatter(spec, masks)))
+                if want("mask_scatter"):
+                    report("mask_scatter", dtype, 0, B,
+                           masks.numel() * e + spec.numel() * 4 + 1025 * 4 + B * 2 * 1025 * T * 2 * 4,
+                           timed(lambda: model.op_mask_scatter(spec, masks)))
                 del spec, xb, masks
         model.close()
     by_op = {}
