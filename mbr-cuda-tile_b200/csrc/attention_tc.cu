@@ -13,9 +13,15 @@
 // do not wait for the tensor cores; K and V stream through a 4-stage ring.
 // V keeps the [seq][H][L][64] layout of q and k: its 64-key tile is the
 // MN-major B operand of the P.V product.  The epilogue multiplies by the
-// sigmoid gate and writes the merged-head row of each token
-// (apply_gates_and_merge_heads).  All waits are bounded (error word instead of
-// a hang).
+// sigmoid gate (loaded at the tile's start) and writes the merged-head row of
+// each token (apply_gates_and_merge_heads).  All waits are bounded (error word
+// instead of a hang).
+//
+// The time axis is bound by the 16-per-clock exponential unit (one exponential
+// per score against 2 x 64 MACs on the tensor core): every fourth exponential
+// of a full 32-column chunk runs on the FMA pipe (exp2_fma), and warps whose
+// 32 query rows all lie past the sequence end (the last tile's tail) compute
+// none.
 #include <cuda.h>
 
 #include <algorithm>
@@ -97,6 +103,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// 2^x on the FMA pipe for x <= 64 (smaller x clamped to -126, whose result,
+// ~1e-38, is as good as 0 here): x = n + f with n = round(x) (the 1.5 * 2^23
+// shift leaves n in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f by a
+// degree-3 polynomial (relative-error fit on [-0.5, 0.5] by iteratively
+// reweighted least squares, max relative error 7.5e-5 in fp32, below a
+// 16-bit probability's rounding); 2^n added to the exponent field as n << 23.
+__device__ __forceinline__ float exp2_fma(float x) {
+    x = fminf(fmaxf(x, -126.0f), 64.0f);
+    const float t = x + 12582912.0f;
+    const float f = x - (t - 12582912.0f);
+    float p = fmaf(5.517166853e-02f, f, 2.426111400e-01f);
+    p = fmaf(p, f, 6.932609677e-01f);
+    p = fmaf(p, f, 9.999280572e-01f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// 10 warps: three share one SM sub-partition's 16 K registers, so at most 168
+// registers per thread.
 template <typename T, bool PACK>
 __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -352,6 +376,9 @@ __global__ void __maxnreg__(168)
             if (gates) gate = __ldg(gates + tok * H + sh % H);
         }
         float m = 0.f, l = 0.f;
+        // a warp with no valid query row (the tail of the last query tile)
+        // computes no exponentials: its P rows are written as zeros
+        const bool wact = __any_sync(0xffffffffu, valid);
         for (int j = 0; j < nkv; ++j) {
             const int g = tl * nkv + j;
             const int b = g & 1;
@@ -359,7 +386,7 @@ __global__ void __maxnreg__(168)
             if (!ok) break;
             tc_fence_after();
             // valid key columns of this row in block j: [0, kend) (warp-uniform)
-            const int kend = PACK ? (j == seg ? min(L, KB) : 0) : min(KB, L - j * KB);
+            const int kend = !wact ? 0 : PACK ? (j == seg ? min(L, KB) : 0) : min(KB, L - j * KB);
             uint32_t sv[2][32];
 #pragma unroll
             for (int c = 0; c < 2; ++c)
@@ -386,7 +413,9 @@ __global__ void __maxnreg__(168)
                     if (c * 32 + 32 <= kend) {  // whole chunk valid: no per-element masking
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            p[i] = fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo));
+                            const float xx = fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo);
+                            // time axis: every fourth exponential on the FMA pipe
+                            p[i] = (!PACK && (i & 3) == 3) ? exp2_fma(xx) : fast_exp2(xx);
                             rsp[i & 7] += p[i];
                         }
                     } else {
@@ -496,440 +525,6 @@ __global__ void __maxnreg__(168)
     }
 }
 
-// ---------------------------------------------------------------------------
-// Time axis (L > 64 positions): the softmax issues one exponential per score
-// while the tensor core spends only 2 x 64 MACs per score, so the kernel is
-// bound by the 16-per-clock exponential unit.  It is organised to keep that
-// unit busy and to take part of its work onto the FMA pipe:
-//  * one CTA per SM, persistent; a work unit is a pair of 128-query tiles of
-//    one (sequence, head), slots 0 and 1, which share every K / V block;
-//  * 128-key blocks; per slot S (128 x 128 fp32), O (128 x 64 fp32) and P
-//    (16-bit pairs) have their own TMEM columns (512 in all);
-//  * warp 9 streams Q (double-buffered per unit) and K / V (4-stage ring) by
-//    TMA; warp 8 issues the MMAs in the order S0(j) S1(j) | PV0(j) S0(j+1)
-//    PV1(j) S1(j+1) ..., so each slot's softmax (warps 0-3 and 4-7, thread =
-//    query row = TMEM lane) runs its exponentials while the tensor core serves
-//    the other slot;
-//  * a quarter of the exponentials (every fourth column) are evaluated by
-//    exp2_fma on the FMA pipe, the rest by ex2.approx.
-// The exponent offset scheme (first block's row max, raised only when a block's
-// probabilities sum past kRescaleSum) is the one of the kernel above.
-// ---------------------------------------------------------------------------
-constexpr int TKB = 128;  // keys per block
-struct TimeCfg {
-    static constexpr int NS = 4;            // K / V stages (128 keys x 64 x 2 B = 16 KB each)
-    static constexpr int Q = 0;             // [2 unit buffers][2 slots] 128 x 64 Q tiles
-    static constexpr int K = 4 * 16384;
-    static constexpr int V = K + NS * 16384;
-    static constexpr int BAR = V + NS * 16384;
-    static constexpr int TOTAL = BAR + 256;
-    static_assert(TOTAL + 1024 <= 232448, "one CTA per SM");
-};
-// TMEM columns: S of slot x at 128 x, O at 256 + 64 x, P at 384 + 64 x.
-constexpr uint32_t kTS = 0, kTO = 256, kTP = 384;
-
-// An empty instruction that "rewrites" r: placed after tcgen05.wait::ld it
-// keeps every use of a TMEM load's registers behind the wait.
-__device__ __forceinline__ void reg_pin32(uint32_t (&r)[32]) {
-    asm volatile(""
-                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
-                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
-                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
-}
-
-// 2^x on the FMA pipe for x <= 64 (smaller x clamped to -126, whose result,
-// ~1e-38, is as good as 0 here): x = n + f with n = round(x) (the 1.5 * 2^23
-// shift leaves n in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f by a
-// degree-3 polynomial (relative-error fit on [-0.5, 0.5] by iteratively
-// reweighted least squares, max relative error 7.5e-5 in fp32, below a
-// 16-bit probability's rounding); 2^n added to the exponent field as n << 23.
-__device__ __forceinline__ float exp2_fma(float x) {
-    x = fminf(fmaxf(x, -126.0f), 64.0f);
-    const float t = x + 12582912.0f;
-    const float f = x - (t - 12582912.0f);
-    float p = fmaf(5.517166853e-02f, f, 2.426111400e-01f);
-    p = fmaf(p, f, 6.932609677e-01f);
-    p = fmaf(p, f, 9.999280572e-01f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
-// 10 warps: three share one SM sub-partition's 16 K registers, so at most 168
-// registers per thread.
-template <typename T>
-__global__ void __launch_bounds__(320, 1)
-    attn_time_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, int n_lo, float scale_log2,
-                     const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
-    using C = TimeCfg;
-    constexpr int NS = C::NS;
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    if (!smem_aligned_or_flag(smem_raw, err)) return;  // uniform over the CTA
-    uint8_t* sm = smem_raw;
-    uint64_t* bar = (uint64_t*)(sm + C::BAR);
-    uint64_t* bar_q = bar;              // [2] Q tiles of a unit buffer landed
-    uint64_t* bar_qfree = bar + 2;      // [2] the last S of the buffer's unit completed
-    uint64_t* bar_k = bar + 4;          // [NS] K stage landed
-    uint64_t* bar_v = bar_k + NS;       // [NS] V stage landed
-    uint64_t* bar_free = bar_v + NS;    // [NS] the stage's last P.V completed
-    uint64_t* bar_s = bar_free + NS;    // [2] slot's S computed
-    uint64_t* bar_p = bar_s + 2;        // [2] slot's P written, S consumed (4 warps)
-    uint64_t* bar_o = bar_p + 2;        // [2] slot's P.V completed
-    uint32_t* tmem_slot = (uint32_t*)(bar_o + 2);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qtiles = (L + QT - 1) / QT;
-    const int npairs = (qtiles + 1) / 2;
-    const int nkv = (L + TKB - 1) / TKB;
-    const int nunits = nsh * npairs;
-    const int my_units = (int)blockIdx.x < nunits ? (nunits - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int total = my_units * nkv;
-    // unit tl of this CTA: sequence-head sh, first query q0 of slot 0; slot 1
-    // (queries q0 + 128 ..) exists when `two`
-    auto unit_of = [&](int tl, int& sh, int& q0, bool& two) {
-        const int u = (int)blockIdx.x + tl * (int)gridDim.x;
-        sh = u / npairs;
-        q0 = (u - sh * npairs) * 2 * QT;
-        two = q0 + QT < L;
-    };
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bar_q[i], 1);
-            mbar_init(&bar_qfree[i], 1);
-            mbar_init(&bar_s[i], 1);
-            mbar_init(&bar_p[i], 4);
-            mbar_init(&bar_o[i], 1);
-        }
-        for (int i = 0; i < NS; ++i) {
-            mbar_init(&bar_k[i], 1);
-            mbar_init(&bar_v[i], 1);
-            mbar_init(&bar_free[i], 1);
-        }
-        fence_barrier_init();
-    }
-    if (warp == 8) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == 9) {
-        // ---- TMA producer (one lane) ----
-        if (lane == 0) {
-            prefetch_tensormap(&tmQ);
-            prefetch_tensormap(&tmK);
-            prefetch_tensormap(&tmV);
-            bool ok = true;
-            int g = 0;
-            for (int tl = 0; tl < my_units && ok; ++tl) {
-                int sh, q0;
-                bool two;
-                unit_of(tl, sh, q0, two);
-                const int s = sh / H, h = sh - s * H, shi = s / n_lo, slo = s - shi * n_lo;
-                const int qb = tl & 1;
-                if (tl >= 2) ok = mbar_wait(&bar_qfree[qb], ((tl - 2) >> 1) & 1, err);
-                if (!ok) break;
-                uint8_t* qdst = sm + C::Q + qb * 32768;
-                mbar_arrive_expect_tx(&bar_q[qb], two ? 32768 : 16384);
-                tma_load_5d(qdst, &tmQ, 0, h, q0, slo, shi, &bar_q[qb]);
-                if (two) tma_load_5d(qdst + 16384, &tmQ, 0, h, q0 + QT, slo, shi, &bar_q[qb]);
-                for (int j = 0; j < nkv; ++j, ++g) {
-                    const int st = g % NS;
-                    if (g >= NS && !(ok = mbar_wait(&bar_free[st], (g / NS - 1) & 1, err))) break;
-                    mbar_arrive_expect_tx(&bar_k[st], 16384);
-                    tma_load_5d(sm + C::K + st * 16384, &tmK, 0, h, j * TKB, slo, shi, &bar_k[st]);
-                    mbar_arrive_expect_tx(&bar_v[st], 16384);
-                    tma_load_5d(sm + C::V + st * 16384, &tmV, 0, h, j * TKB, slo, shi, &bar_v[st]);
-                }
-            }
-        }
-    } else if (warp == 8) {
-        // ---- MMA issuer: lane 0 issues and commits, all lanes wait ----
-        auto wait_all = [&](uint64_t* b, uint32_t parity) -> bool {
-            return __all_sync(0xffffffffu, mbar_wait(b, parity, err));
-        };
-        constexpr uint32_t idS = idesc_f16(QT, TKB, IsBf16<T>::value);
-        constexpr uint32_t idO = idesc_f16(QT, DH, IsBf16<T>::value, /*b_mn_major=*/true);
-        // descriptor start addresses count 16-byte units: +2 per 32 bytes of K,
-        // +1024 per 16 KB tile
-        const uint64_t dQ = sdesc_sw128(smem_u32(sm + C::Q));
-        const uint64_t dK = sdesc_sw128(smem_u32(sm + C::K));
-        const uint64_t dV = sdesc_sw128_mn(smem_u32(sm + C::V));
-        auto issue_s = [&](int x, int tl, int g) {  // S(x) = Q(unit tl, slot x) K(g)^T
-            const uint64_t q = dQ + (uint64_t)(2048 * (tl & 1) + 1024 * x);
-            const uint64_t k0 = dK + (uint64_t)(1024 * (g % NS));
-            const uint32_t d = tmem + kTS + 128 * x;
-#pragma unroll
-            for (int k = 0; k < DH / 16; ++k) mma_f16(d, q + 2 * k, k0 + 2 * k, idS, k > 0);
-            mma_commit(&bar_s[x]);
-        };
-        auto issue_pv = [&](int x, int g, bool first) {  // O(x) (+)= P(x) V(g), P read from TMEM
-            const uint32_t a0 = tmem + kTP + 64 * x;
-            const uint64_t b0 = dV + (uint64_t)(1024 * (g % NS));
-#pragma unroll
-            for (int k = 0; k < TKB / 16; ++k)  // A: keys 16k.. = 8 packed columns; B: V keys 16k.. (2 KB)
-                mma_f16_ts(tmem + kTO + 64 * x, a0 + 8 * k, b0 + 128 * k, idO, !first || k > 0);
-            mma_commit(&bar_o[x]);
-        };
-        bool ok = total > 0;
-        int tl = 0, j = 0, sh, q0;
-        bool two = false;
-        if (ok) {
-            unit_of(0, sh, q0, two);
-            ok = wait_all(&bar_q[0], 0) && wait_all(&bar_k[0], 0);
-            if (ok) {
-                tc_fence_after();
-                if (lane == 0) {
-                    issue_s(0, 0, 0);
-                    if (two) issue_s(1, 0, 0);
-                    if (nkv == 1) mma_commit(&bar_qfree[0]);
-                }
-                __syncwarp();
-            }
-        }
-        int cnt[2] = {0, 0};  // P blocks consumed per slot
-        for (int g = 0; g < total && ok; ++g) {
-            // the next block (tl2, j2) and whether its unit has slot 1
-            int tl2 = tl, j2 = j + 1, sh2, q02;
-            bool two2 = two;
-            if (j2 == nkv) {
-                j2 = 0;
-                ++tl2;
-                two2 = false;
-                if (tl2 < my_units) unit_of(tl2, sh2, q02, two2);
-            }
-            const bool has_next = g + 1 < total;
-            // slot 0: P.V(g), then S(g + 1) into its S columns
-            ok = wait_all(&bar_p[0], cnt[0] & 1) && wait_all(&bar_v[g % NS], (g / NS) & 1);
-            if (!ok) break;
-            tc_fence_after();
-            if (lane == 0) issue_pv(0, g, j == 0);
-            __syncwarp();
-            ++cnt[0];
-            if (has_next) {
-                if (j2 == 0) ok = wait_all(&bar_q[tl2 & 1], (tl2 >> 1) & 1);
-                ok = ok && wait_all(&bar_k[(g + 1) % NS], ((g + 1) / NS) & 1);
-                if (!ok) break;
-                tc_fence_after();
-                if (lane == 0) {
-                    issue_s(0, tl2, g + 1);
-                    if (j2 == nkv - 1 && !two2) mma_commit(&bar_qfree[tl2 & 1]);
-                }
-                __syncwarp();
-            }
-            // slot 1
-            if (two) {
-                ok = wait_all(&bar_p[1], cnt[1] & 1);
-                if (!ok) break;
-                tc_fence_after();
-                if (lane == 0) issue_pv(1, g, j == 0);
-                __syncwarp();
-                ++cnt[1];
-            }
-            if (lane == 0) mma_commit(&bar_free[g % NS]);  // every reader of stage g % NS issued
-            if (has_next && two2) {
-                if (lane == 0) {
-                    issue_s(1, tl2, g + 1);
-                    if (j2 == nkv - 1) mma_commit(&bar_qfree[tl2 & 1]);
-                }
-                __syncwarp();
-            }
-            tl = tl2;
-            j = j2;
-            two = two2;
-        }
-    } else {
-        // ---- softmax: slot x = warp / 4, thread = query row = TMEM lane ----
-        const int x = warp >> 2, qw = warp & 3;
-        const int r = 32 * qw + lane;
-        const uint32_t lane_off = (uint32_t)(qw * 32) << 16;
-        const uint32_t tS = tmem + lane_off + kTS + 128 * x;
-        const uint32_t tP = tmem + lane_off + kTP + 64 * x;
-        const uint32_t tO = tmem + lane_off + kTO + 64 * x;
-        int cnt = 0;     // S blocks of this slot consumed so far
-        bool ok = true;  // warp-uniform
-        for (int tl = 0; tl < my_units && ok; ++tl) {
-            int sh, q0;
-            bool two;
-            unit_of(tl, sh, q0, two);
-            if (x == 1 && !two) continue;
-            const int qs = q0 + QT * x;
-            const int pos = qs + r;
-            const bool wact = qs + 32 * qw < L;  // this warp has valid query rows
-            // this row's token and gate, loaded now so the load is long done by the epilogue
-            int64_t tok = 0;
-            float gate = 1.0f;
-            if (pos < L) {
-                const int64_t s = sh / H;
-                tok = mode == ops::SEQ_TIME ? ((s / NB) * Tn + pos) * NB + (s % NB) : s * NB + pos;
-                if (gates) gate = __ldg(gates + tok * H + sh % H);
-            }
-            float m = 0.f, l = 0.f;
-            for (int j = 0; j < nkv; ++j) {
-                ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_s[x], cnt & 1, err));
-                if (!ok) break;
-                tc_fence_after();
-                if (wact) {
-                    const int kend = min(TKB, L - j * TKB);  // valid keys of this block (warp-uniform)
-                    // S is read from TMEM one 64-column half at a time (S keeps its
-                    // columns: P has its own), so a thread holds 64 scores, not 128
-                    uint32_t sv[2][32];
-                    auto load_half = [&](int hf) {
-#pragma unroll
-                        for (int c = 0; c < 2; ++c)
-                            if ((2 * hf + c) * 32 < kend) tmem_ld32(tS + 32 * (2 * hf + c), sv[c]);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int c = 0; c < 2; ++c) reg_pin32(sv[c]);
-                    };
-                    // probabilities with offset mo -> P columns as 16-bit pairs
-                    // (masked keys 0); returns the block's row sum
-                    auto emit = [&](float mo) {
-                        float rsp[8];
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) rsp[u] = 0.f;
-#pragma unroll
-                        for (int hf = 0; hf < 2; ++hf) {
-                            if (hf * 64 < kend) load_half(hf);
-#pragma unroll
-                            for (int c2 = 0; c2 < 2; ++c2) {
-                                const int c = 2 * hf + c2;
-                                uint32_t pk[16];
-                                if (c * 32 >= kend) {
-#pragma unroll
-                                    for (int i = 0; i < 16; ++i) pk[i] = 0u;
-                                } else {
-                                    const int nv = kend - c * 32;
-#pragma unroll
-                                    for (int i = 0; i < 32; i += 2) {
-                                        float p2[2];
-#pragma unroll
-                                        for (int e = 0; e < 2; ++e) {
-                                            const int ii = i + e;
-                                            const float xx = fmaf(__uint_as_float(sv[c2][ii]), scale_log2, -mo);
-                                            float p = (ii & 3) == 3 ? exp2_fma(xx) : fast_exp2(xx);
-                                            if (nv < 32 && ii >= nv) p = 0.f;
-                                            rsp[ii & 7] += p;
-                                            p2[e] = p;
-                                        }
-                                        pk[i >> 1] = pack2(p2[0], p2[1], (T*)nullptr);
-                                    }
-                                }
-                                tmem_st16(tP + 16 * c, pk);
-                            }
-                        }
-                        return ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-                    };
-                    // row max of the valid scores of this block (log2 units)
-                    auto row_max = [&]() {
-                        float mxp[8];
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
-#pragma unroll
-                        for (int hf = 0; hf < 2; ++hf) {
-                            if (hf * 64 >= kend) continue;
-                            load_half(hf);
-#pragma unroll
-                            for (int c2 = 0; c2 < 2; ++c2) {
-                                const int c = 2 * hf + c2;
-                                if (c * 32 >= kend) continue;
-                                const int nv = kend - c * 32;
-#pragma unroll
-                                for (int i = 0; i < 32; ++i)
-                                    if (nv >= 32 || i < nv) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(sv[c2][i]));
-                            }
-                        }
-                        const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-                        return mx * scale_log2;  // the scale is positive
-                    };
-                    float rs;
-                    if (j == 0) {
-                        const float mb = row_max();
-                        m = mb == -INFINITY ? 0.f : mb;
-                        rs = emit(m);
-                    } else {
-                        rs = emit(m);
-                        const bool need = !(rs <= kRescaleSum);  // also catches inf / nan
-                        if (__any_sync(0xffffffffu, need)) {
-                            // O holds P.V of blocks < j: P.V(j-1) was issued before S(j),
-                            // whose completion was observed, so this wait returns at once
-                            ok = mbar_wait(&bar_o[x], (cnt - 1) & 1, err);
-                            ok = __all_sync(0xffffffffu, ok);
-                            if (ok) {
-                                tc_fence_after();
-                                // row_max reads S with warp-collective TMEM loads: every
-                                // lane calls it, each then keeps or raises its own offset
-                                const float mx = row_max();
-                                const float m_new = need ? fmaxf(m, mx) : m;
-                                const float alpha = fast_exp2(m - m_new);
-                                m = m_new;
-                                l *= alpha;
-                                tmem_st_wait();  // the first emit's P stores precede the rewrite
-#pragma unroll 1
-                                for (int c = 0; c < DH / 16; ++c) {
-                                    uint32_t ov[16];
-                                    tmem_ld16(tO + c * 16, ov);
-                                    tmem_ld_wait();
-#pragma unroll
-                                    for (int i = 0; i < 16; ++i)
-                                        ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                                    tmem_st16(tO + c * 16, ov);
-                                }
-                                rs = emit(m);
-                            }
-                        }
-                    }
-                    l += rs;
-                    tmem_st_wait();  // P (and O) stores complete
-                }
-                tc_fence_before();  // S reads, P / O stores ordered before the next MMAs
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_p[x]);
-                ++cnt;
-                if (!ok) break;
-            }
-            // the tile's last P.V: the latest on bar_o[x]; the one before it
-            // completed ahead of the last S, so the parity wait is exact
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_o[x], (cnt - 1) & 1, err));
-            if (ok && wact) {
-                tc_fence_after();
-                uint32_t ov[DH / 32][32];
-#pragma unroll
-                for (int c = 0; c < DH / 32; ++c) tmem_ld32(tO + c * 32, ov[c]);
-                tmem_ld_wait();
-                if (pos < L) {
-                    const int hd = sh % H;
-                    const float gs = gate / l;
-                    uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH);
-#pragma unroll
-                    for (int q = 0; q < DH / 8; ++q) {
-                        const uint32_t* o = &ov[q >> 2][(q & 3) * 8];
-                        dst[q] = make_uint4(
-                            pack2(__uint_as_float(o[0]) * gs, __uint_as_float(o[1]) * gs, (T*)nullptr),
-                            pack2(__uint_as_float(o[2]) * gs, __uint_as_float(o[3]) * gs, (T*)nullptr),
-                            pack2(__uint_as_float(o[4]) * gs, __uint_as_float(o[5]) * gs, (T*)nullptr),
-                            pack2(__uint_as_float(o[6]) * gs, __uint_as_float(o[7]) * gs, (T*)nullptr));
-                    }
-                }
-            }
-            tc_fence_before();  // O read before the slot's next P.V overwrites it
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 8) {
-        __syncwarp();
-        tc_fence_after();
-        tmem_dealloc(tmem, 512);
-    }
-}
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -992,31 +587,6 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
     MBR_CUDA(cudaGetLastError());
 }
 
-template <typename T>
-void launch_time(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, int nsh, int H, int L, int n_lo,
-                 float scale_log2, const float* gates, int mode, int NB, int Tn, void* merged, int* err,
-                 cudaStream_t st) {
-    auto kern = attn_time_kernel<T>;
-    static bool attr[64] = {};
-    static int sms[64] = {};
-    int dev = 0;
-    MBR_CUDA(cudaGetDevice(&dev));
-    MBR_CHECK(dev >= 0 && dev < 64, "device index out of range");
-    if (!attr[dev]) {
-        MBR_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TimeCfg::TOTAL));
-        MBR_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
-        attr[dev] = true;
-    }
-    // persistent: one CTA per SM walks the units (pairs of 128-query tiles)
-    const int64_t nunits = (int64_t)nsh * (((L + QT - 1) / QT + 1) / 2);
-    MBR_CHECK(nunits < (1ll << 30), "tc attention: too many tiles");
-    const int grid = (int)std::min<int64_t>(nunits, (int64_t)sms[dev]);
-    if (grid == 0) return;
-    kern<<<grid, 320, TimeCfg::TOTAL, st>>>(mq, mk, mv, nsh, H, L, n_lo, scale_log2, gates, mode, NB, Tn, (T*)merged,
-                                            err);
-    MBR_CUDA(cudaGetLastError());
-}
-
 }  // namespace
 
 bool attention_supported(int dim_head) { return dim_head == DH; }
@@ -1043,16 +613,16 @@ void attention(const void* q, const void* k, const void* v, const AttnLayout& la
     const bool pack = L <= 64;
     CUtensorMap mq, mk, mv;
     make_map(&mq, q, lay, H, L, pack ? 64 : QT, dtype);
-    make_map(&mk, k, lay, H, L, pack ? KB : TKB, dtype);
-    make_map(&mv, v, lay, H, L, pack ? KB : TKB, dtype);
+    make_map(&mk, k, lay, H, L, KB, dtype);
+    make_map(&mv, v, lay, H, L, KB, dtype);
     const float scale_log2 = scale * 1.4426950408889634f;
     const int n = (int)nsh;
     if (dtype == DT_BF16) {
         if (pack) launch<__nv_bfloat16, true>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
-        else launch_time<__nv_bfloat16>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        else launch<__nv_bfloat16, false>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
     } else {
         if (pack) launch<__half, true>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
-        else launch_time<__half>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
+        else launch<__half, false>(mq, mk, mv, n, H, L, lay.n_lo, scale_log2, gates, mode, NB, T, merged, d_err, st);
     }
 }
 

@@ -247,68 +247,103 @@ __global__ void __launch_bounds__(256) binary_vec_kernel(const T* __restrict__ a
     }
 }
 
-// out[r] = reduce(src[r][0..len)), contiguous rows: one warp per row.
+// out[r] = reduce(src[r][0..len)), contiguous rows of len % 8 == 0 (16-byte
+// aligned): one warp per group of 4 rows, each lane one 16-byte vector per row
+// and step, so a lane has 4 independent loads in flight even for the short
+// rows (192 to 512 elements) of the activations.
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) reduce_rows_kernel(const T* __restrict__ src, T* __restrict__ out,
-                                                          int64_t rows, int64_t len, bool vec) {
+                                                          int64_t rows, int64_t len) {
+    constexpr int R = 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const float init = OP == RED_MAX ? -INFINITY : 0.f;
+    for (int64_t r0 = warp0 * R; r0 < rows; r0 += nwarps * R) {
+        float acc[R];
+#pragma unroll
+        for (int q = 0; q < R; ++q) acc[q] = init;
+        for (int64_t k = 8 * lane; k < len; k += 256) {
+            float v[R][8];
+#pragma unroll
+            for (int q = 0; q < R; ++q)
+                if (r0 + q < rows) load8(src + (r0 + q) * len + k, v[q]);
+#pragma unroll
+            for (int q = 0; q < R; ++q)
+                if (r0 + q < rows)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[q] = OP == RED_MAX ? fmaxf(acc[q], v[q][e]) : acc[q] + v[q][e];
+        }
+#pragma unroll
+        for (int q = 0; q < R; ++q) {
+            const float a = OP == RED_MAX ? mbr::warp_max(acc[q]) : mbr::warp_sum(acc[q]);
+            if (lane == q && r0 + q < rows) out[r0 + q] = fromf<T>(OP == RED_MEAN ? a / (float)len : a);
+        }
+    }
+}
+
+// Rows of any length or alignment: one warp per row, scalar loads.
+template <typename T, int OP>
+__global__ void __launch_bounds__(256) reduce_rows_scalar_kernel(const T* __restrict__ src, T* __restrict__ out,
+                                                                 int64_t rows, int64_t len) {
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t r = warp0; r < rows; r += nwarps) {
-        const T* row = src + r * len;
-        float acc0 = OP == RED_MAX ? -INFINITY : 0.f, acc1 = acc0;
-        int64_t k = 0;
-        if (vec) {
-            // 16-byte vectors: 8 elements per lane, two vectors in flight
-            for (; k + 512 <= len; k += 512) {
-                float v[8], w[8];
-                load8(row + k + 8 * lane, v);
-                load8(row + k + 256 + 8 * lane, w);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    acc0 = OP == RED_MAX ? fmaxf(acc0, v[e]) : acc0 + v[e];
-                    acc1 = OP == RED_MAX ? fmaxf(acc1, w[e]) : acc1 + w[e];
-                }
-            }
-            for (; k + 256 <= len; k += 256) {
-                float v[8];
-                load8(row + k + 8 * lane, v);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc0 = OP == RED_MAX ? fmaxf(acc0, v[e]) : acc0 + v[e];
-            }
+        float acc = OP == RED_MAX ? -INFINITY : 0.f;
+        for (int64_t q = lane; q < len; q += 32) {
+            const float v = tof(src[r * len + q]);
+            acc = OP == RED_MAX ? fmaxf(acc, v) : acc + v;
         }
-        for (int64_t q = k + lane; q < len; q += 32) {
-            const float v = tof(row[q]);
-            acc1 = OP == RED_MAX ? fmaxf(acc1, v) : acc1 + v;
-        }
-        float acc = OP == RED_MAX ? fmaxf(acc0, acc1) : acc0 + acc1;
         acc = OP == RED_MAX ? mbr::warp_max(acc) : mbr::warp_sum(acc);
         if (lane == 0) out[r] = fromf<T>(OP == RED_MEAN ? acc / (float)len : acc);
     }
 }
 
-// Column partials: CTA (bx, by) reduces columns [32 bx, 32 bx + 32) over rows
-// by, by + gridDim.y, ... (each warp a strided subset, lanes = consecutive
-// columns) into part[by][col].
+// Column partials of a contiguous [len][n] (n % 8 == 0, 16-byte aligned):
+// CTA (bx, by) covers columns [256 bx, 256 bx + 256), each lane 8 consecutive
+// columns by one 16-byte load per row, over rows by, by + gridDim.y, ... split
+// among its 8 warps; the warps' partials are combined in shared memory into
+// part[by][col].
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) reduce_cols_partial_kernel(const T* __restrict__ src, float* __restrict__ part,
                                                                   int64_t len, int64_t n) {
-    __shared__ float sm[8][33];
+    __shared__ float sm[8][256];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t col = (int64_t)blockIdx.x * 32 + lane;
-    float acc = OP == RED_MAX ? -INFINITY : 0.f;
-    if (col < n)
-        for (int64_t r = (int64_t)blockIdx.y * 8 + w; r < len; r += (int64_t)gridDim.y * 8) {
-            const float v = tof(src[r * n + col]);
-            acc = OP == RED_MAX ? fmaxf(acc, v) : acc + v;
-        }
-    sm[w][lane] = acc;
-    __syncthreads();
-    if (w == 0) {
+    const int64_t c0 = (int64_t)blockIdx.x * 256 + 8 * lane;
+    const float init = OP == RED_MAX ? -INFINITY : 0.f;
+    float acc[8];
 #pragma unroll
-        for (int k = 1; k < 8; ++k) acc = OP == RED_MAX ? fmaxf(acc, sm[k][lane]) : acc + sm[k][lane];
-        if (col < n) part[(int64_t)blockIdx.y * n + col] = acc;
+    for (int e = 0; e < 8; ++e) acc[e] = init;
+    if (c0 < n) {
+        const int64_t step = (int64_t)gridDim.y * 8;
+        int64_t r = (int64_t)blockIdx.y * 8 + w;
+        // two rows' vectors in flight per lane
+        for (; r + step < len; r += 2 * step) {
+            float v[8], u[8];
+            load8(src + r * n + c0, v);
+            load8(src + (r + step) * n + c0, u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                acc[e] = OP == RED_MAX ? fmaxf(acc[e], v[e]) : acc[e] + v[e];
+                acc[e] = OP == RED_MAX ? fmaxf(acc[e], u[e]) : acc[e] + u[e];
+            }
+        }
+        if (r < len) {
+            float v[8];
+            load8(src + r * n + c0, v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = OP == RED_MAX ? fmaxf(acc[e], v[e]) : acc[e] + v[e];
+        }
     }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sm[w][8 * lane + e] = acc[e];
+    __syncthreads();
+    const int64_t col = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    float a = sm[0][threadIdx.x];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) a = OP == RED_MAX ? fmaxf(a, sm[k][threadIdx.x]) : a + sm[k][threadIdx.x];
+    if (col < n) part[(int64_t)blockIdx.y * n + col] = a;
 }
 template <typename T, int OP>
 __global__ void reduce_cols_final_kernel(const float* __restrict__ part, T* __restrict__ out, int splits, int64_t len,
@@ -317,6 +352,34 @@ __global__ void reduce_cols_final_kernel(const float* __restrict__ part, T* __re
         float acc = OP == RED_MAX ? -INFINITY : 0.f;
         for (int k = 0; k < splits; ++k) acc = OP == RED_MAX ? fmaxf(acc, part[(int64_t)k * n + c]) : acc + part[(int64_t)k * n + c];
         out[c] = fromf<T>(OP == RED_MEAN ? acc / (float)len : acc);
+    }
+}
+
+// dst[c][r] = src[r][c]: the contiguous copy of a transposed 2-D view
+// (source element (i, j) at src[j * ld_src + i]), through 32 x 32 shared-memory
+// tiles so both the reads and the writes are coalesced.
+template <typename E>
+__global__ void __launch_bounds__(256) transpose2d_kernel(const E* __restrict__ src, E* __restrict__ dst,
+                                                          int64_t rows, int64_t cols) {
+    // dst is [rows][cols] (rows = the view's dim 0); src holds it as [cols][rows]
+    __shared__ E tile[32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int64_t tb = blockIdx.x; tb < ((rows + 31) / 32) * ((cols + 31) / 32); tb += gridDim.x) {
+        const int64_t tr = tb / ((cols + 31) / 32), tc = tb % ((cols + 31) / 32);
+        const int64_t r0 = tr * 32, c0 = tc * 32;
+        // read: source rows are the view's columns; lanes along the view's rows (contiguous in src)
+#pragma unroll
+        for (int k = ty; k < 32; k += 8) {
+            const int64_t c = c0 + k, r = r0 + tx;
+            if (c < cols && r < rows) tile[k][tx] = src[c * rows + r];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = ty; k < 32; k += 8) {
+            const int64_t r = r0 + k, c = c0 + tx;
+            if (r < rows && c < cols) dst[r * cols + c] = tile[tx][k];
+        }
+        __syncthreads();
     }
 }
 
@@ -514,6 +577,28 @@ void copy(const void* src, int sdt, const int64_t* sstride, void* dst, int ddt, 
         MBR_CUDA(cudaGetLastError());
         return;
     }
+    // the contiguous copy of a transposed 2-D view: tiled through shared memory
+    {
+        int64_t sh2[2], ss2[2];
+        int k = 0;
+        for (int d = 0; d < nd && k <= 2; ++d)
+            if (shape[d] != 1) {
+                if (k < 2) sh2[k] = shape[d], ss2[k] = sstride[d];
+                ++k;
+            }
+        if (k == 2 && sdt == ddt && ss2[0] == 1 && ss2[1] == sh2[0] && is_contig(nd, shape, dstride)) {
+            const int64_t tiles = ((sh2[0] + 31) / 32) * ((sh2[1] + 31) / 32);
+            const unsigned gr = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sm_count() * 16));
+            if (sdt == F32)
+                transpose2d_kernel<float><<<gr, 256, 0, st>>>((const float*)src, (float*)dst, sh2[0], sh2[1]);
+            else if (sdt == I64)
+                transpose2d_kernel<int64_t><<<gr, 256, 0, st>>>((const int64_t*)src, (int64_t*)dst, sh2[0], sh2[1]);
+            else
+                transpose2d_kernel<uint16_t><<<gr, 256, 0, st>>>((const uint16_t*)src, (uint16_t*)dst, sh2[0], sh2[1]);
+            MBR_CUDA(cudaGetLastError());
+            return;
+        }
+    }
     const Geo g = make_geo(nd, shape, sstride, dstride, nullptr);
     if (fits32(n, nd, shape)) copy_kernel<uint32_t><<<grid(n), 256, 0, st>>>(g, src, sdt, dst, ddt, n);
     else copy_kernel<uint64_t><<<grid(n), 256, 0, st>>>(g, src, sdt, dst, ddt, n);
@@ -624,28 +709,25 @@ void reduce(int op, const void* src, int sdt, const int64_t* s_outer, int nd, co
             using T = std::remove_pointer_t<decltype(t)>;
             const bool vec = aligned16(src) && len % 8 == 0;
             const unsigned gr = (unsigned)std::max<int64_t>(
-                1, std::min<int64_t>((n_outer + 7) / 8, (int64_t)sm_count() * 16));
-            switch (op) {
-                case RED_SUM:
-                    reduce_rows_kernel<T, RED_SUM><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len, vec);
-                    break;
-                case RED_MEAN:
-                    reduce_rows_kernel<T, RED_MEAN><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len, vec);
-                    break;
-                default:
-                    reduce_rows_kernel<T, RED_MAX><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len, vec);
-                    break;
-            }
+                1, std::min<int64_t>((n_outer + 31) / 32, (int64_t)sm_count() * 16));
+            auto go = [&](auto opc) {
+                constexpr int OP = decltype(opc)::value;
+                if (vec) reduce_rows_kernel<T, OP><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len);
+                else reduce_rows_scalar_kernel<T, OP><<<gr, 256, 0, st>>>((const T*)src, (T*)out, n_outer, len);
+            };
+            if (op == RED_SUM) go(std::integral_constant<int, RED_SUM>());
+            else if (op == RED_MEAN) go(std::integral_constant<int, RED_MEAN>());
+            else go(std::integral_constant<int, RED_MAX>());
         })) {
         MBR_CUDA(cudaGetLastError());
         return;
     }
     // leading dim of a contiguous [len][n_outer]: column partials over CTAs
     if (nd == 1 && s_outer[0] == 1 && rstride == n_outer && sdt == odt && n_outer < (int64_t)sm_count() * 1024 &&
-        len >= 64 &&
+        len >= 64 && n_outer % 8 == 0 && aligned16(src) &&
         with_float_type(sdt, [&](auto* t) {
             using T = std::remove_pointer_t<decltype(t)>;
-            const int64_t bx = (n_outer + 31) / 32;
+            const int64_t bx = (n_outer + 255) / 256;
             const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((len + 63) / 64,
                                                                             (sm_count() * 8 + bx - 1) / bx));
             float* part = (float*)CudaMemoryPool::instance().allocate(sizeof(float) * (size_t)splits * n_outer, st);

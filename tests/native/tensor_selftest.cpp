@@ -212,6 +212,10 @@ int main() {
             expect(near(x.max(-1).to_f32().to_cpu_f32(), e_max, 0.f), "row max" + tag);
             expect(near(x.sum(0).to_f32().to_cpu_f32(), e_col, stol), "column sum" + tag);
             expect(near(x.max(0).to_f32().to_cpu_f32(), e_cmax, 0.f), "column max" + tag);
+            std::vector<float> e_t((size_t)n);
+            for (int i = 0; i < rows; ++i)
+                for (int k = 0; k < cols; ++k) e_t[(size_t)k * rows + i] = hx[(size_t)i * cols + k];
+            expect(near(x.transpose(0, 1).contiguous().to_f32().to_cpu_f32(), e_t, 0.f), "2-D transpose" + tag);
         }
     }
 
