@@ -148,10 +148,12 @@ __global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restric
     const float4* h4 = reinterpret_cast<const float4*>(gamma2);
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    // software pipeline: the next row pair's loads are in flight while this
-    // pair is reduced, normalised and stored
-    float4 nx[2][MAXC];
-    auto load_pair = [&](int64_t mp) {
+    // software pipeline: the loads of the next PF row pairs are in flight while
+    // this pair is reduced, normalised and stored (PF = 2 while the buffers fit
+    // the register budget, for D <= 384)
+    constexpr int PF = MAXC <= 3 ? 2 : 1;
+    float4 nx[PF][2][MAXC];
+    auto load_pair = [&](int64_t mp, float4 (&dst)[2][MAXC]) {
         const bool two_p = mp + 1 < M;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
@@ -159,11 +161,13 @@ __global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restric
 #pragma unroll
             for (int i = 0; i < MAXC; ++i) {
                 const int c = lane + 32 * i;
-                nx[r][i] = c < D4 ? __ldcs(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                dst[r][i] = c < D4 ? __ldcs(x4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
     };
-    if (2 * wid < M) load_pair(2 * wid);
+#pragma unroll
+    for (int k = 0; k < PF; ++k)
+        if (2 * wid + 2 * warps * k < M) load_pair(2 * wid + 2 * warps * k, nx[k]);
     for (int64_t m0 = 2 * wid; m0 < M; m0 += 2 * warps) {
         const bool two = m0 + 1 < M;
         float4 v[2][MAXC];
@@ -172,11 +176,17 @@ __global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restric
         for (int r = 0; r < 2; ++r)
 #pragma unroll
             for (int i = 0; i < MAXC; ++i) {
-                v[r][i] = nx[r][i];
+                v[r][i] = nx[0][r][i];
                 ss[r] += v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y + v[r][i].z * v[r][i].z +
                          v[r][i].w * v[r][i].w;
             }
-        if (m0 + 2 * warps < M) load_pair(m0 + 2 * warps);
+#pragma unroll
+        for (int k = 0; k + 1 < PF; ++k)
+#pragma unroll
+            for (int r = 0; r < 2; ++r)
+#pragma unroll
+                for (int i = 0; i < MAXC; ++i) nx[k][r][i] = nx[k + 1][r][i];
+        if (m0 + 2 * warps * PF < M) load_pair(m0 + 2 * warps * PF, nx[PF - 1]);
         ss[0] = warp_sum(ss[0]);
         ss[1] = warp_sum(ss[1]);
 #pragma unroll
