@@ -17,11 +17,8 @@
 // each token (apply_gates_and_merge_heads).  All waits are bounded (error word
 // instead of a hang).
 //
-// The time axis is bound by the 16-per-clock exponential unit (one exponential
-// per score against 2 x 64 MACs on the tensor core): every fourth exponential
-// of a full 32-column chunk runs on the FMA pipe (exp2_fma), and warps whose
-// 32 query rows all lie past the sequence end (the last tile's tail) compute
-// none.
+// Warps whose 32 query rows all lie past the sequence end (the last query
+// tile's tail) compute no exponentials.
 #include <cuda.h>
 
 #include <algorithm>
@@ -103,24 +100,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-// 2^x on the FMA pipe for x <= 64 (smaller x clamped to -126, whose result,
-// ~1e-38, is as good as 0 here): x = n + f with n = round(x) (the 1.5 * 2^23
-// shift leaves n in the low mantissa bits of t) and f in [-0.5, 0.5]; 2^f by a
-// degree-3 polynomial (relative-error fit on [-0.5, 0.5] by iteratively
-// reweighted least squares, max relative error 7.5e-5 in fp32, below a
-// 16-bit probability's rounding); 2^n added to the exponent field as n << 23.
-__device__ __forceinline__ float exp2_fma(float x) {
-    x = fminf(fmaxf(x, -126.0f), 64.0f);
-    const float t = x + 12582912.0f;
-    const float f = x - (t - 12582912.0f);
-    float p = fmaf(5.517166853e-02f, f, 2.426111400e-01f);
-    p = fmaf(p, f, 6.932609677e-01f);
-    p = fmaf(p, f, 9.999280572e-01f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
-// 10 warps: three share one SM sub-partition's 16 K registers, so at most 168
-// registers per thread.
 template <typename T, bool PACK>
 __global__ void __maxnreg__(168)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -413,9 +392,7 @@ __global__ void __maxnreg__(168)
                     if (c * 32 + 32 <= kend) {  // whole chunk valid: no per-element masking
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            const float xx = fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo);
-                            // time axis: every fourth exponential on the FMA pipe
-                            p[i] = (!PACK && (i & 3) == 3) ? exp2_fma(xx) : fast_exp2(xx);
+                            p[i] = fast_exp2(fmaf(__uint_as_float(sv[c][i]), scale_log2, -mo));
                             rsp[i & 7] += p[i];
                         }
                     } else {

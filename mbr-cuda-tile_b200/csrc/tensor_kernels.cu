@@ -121,11 +121,6 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, flo
 template <typename T>
 __device__ __forceinline__ void store8(T* p, const float (&v)[8]);
 template <>
-__device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
-    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
-}
-template <>
 __device__ __forceinline__ void store8<__half>(__half* p, const float (&v)[8]) {
     uint4 u;
     __half2* h = reinterpret_cast<__half2*>(&u);
@@ -182,14 +177,83 @@ __device__ __forceinline__ float un(float x, float p0, float p1) {
         if (i_ < (n8)) { const int64_t u = i_; __VA_ARGS__; }                          \
     } while (0)
 
-// y = convert(a), contiguous (S == D: a vector copy)
+// Unit u of the vector loops is the 8 elements one lane moves per step.  A
+// warp's 32 consecutive units form one 256-element block: for 16-bit types
+// lane l takes elements 8l .. 8l+7 (one 16-byte access); for fp32 it takes
+// 4l .. 4l+3 and 128+4l .. 128+4l+3, so each of its two 16-byte accesses is a
+// fully used 512-byte run across the warp (two 32-byte halves of every sector
+// coming from different instructions would leave sectors partly written).  The
+// fp32 units past the last whole block keep 8 contiguous elements.
+template <typename T>
+__device__ __forceinline__ int64_t unit_elem(int64_t u, int64_t full_units, int half) {
+    if constexpr (sizeof(T) == 4) {
+        if (u < full_units) return 256 * (u >> 5) + 4 * (u & 31) + 128 * half;
+    }
+    return 8 * u + 4 * half;
+}
+template <typename T>
+__device__ __forceinline__ void load_unit(const T* p, int64_t u, int64_t full_units, float (&v)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p + unit_elem<T>(u, full_units, 0)));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p + unit_elem<T>(u, full_units, 1)));
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+        load8(p + 8 * u, v);
+    }
+}
+template <typename T>
+__device__ __forceinline__ void store_unit(T* p, int64_t u, int64_t full_units, const float (&v)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        *reinterpret_cast<float4*>(p + unit_elem<T>(u, full_units, 0)) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(p + unit_elem<T>(u, full_units, 1)) = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        store8(p + 8 * u, v);
+    }
+}
+// the [D] broadcast operand's values for unit u (D % 8 == 0): element e uses b[e % D]
+template <typename T>
+__device__ __forceinline__ void load_unit_bcast(const T* b, int64_t u, int64_t full_units, int64_t D, bool m32,
+                                                float (&v)[8]) {
+    auto col = [&](int64_t e) { return m32 ? (int64_t)((uint32_t)e % (uint32_t)D) : e % D; };
+    if constexpr (sizeof(T) == 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(b + col(unit_elem<T>(u, full_units, 0))));
+        const float4 c = __ldg(reinterpret_cast<const float4*>(b + col(unit_elem<T>(u, full_units, 1))));
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
+    } else {
+        load8(b + col(8 * u), v);
+    }
+}
+
+// y = convert(a), contiguous (S == D: a vector copy).  The units of source and
+// destination must cover the same elements: fp32 on either side uses the fp32
+// layout for both.
 template <typename S, typename D>
 __global__ void __launch_bounds__(256) cvt_vec_kernel(const S* __restrict__ a, D* __restrict__ y, int64_t n) {
-    const int64_t n8 = n >> 3;
+    const int64_t n8 = n >> 3, full = 32 * (n >> 8);
+    using L = std::conditional_t<sizeof(S) == 4 || sizeof(D) == 4, float, S>;  // unit layout
     VEC_LOOP(n8, {
         float v[8];
-        load8(a + 8 * u, v);
-        store8(y + 8 * u, v);
+        if constexpr (sizeof(L) == 4 && sizeof(S) != 4) {  // 16-bit source, fp32 layout: 8-byte loads
+            const int64_t e0 = unit_elem<L>(u, full, 0), e1 = unit_elem<L>(u, full, 1);
+            const uint2 q0 = __ldg(reinterpret_cast<const uint2*>(a + e0));
+            const uint2 q1 = __ldg(reinterpret_cast<const uint2*>(a + e1));
+            const S* h0 = reinterpret_cast<const S*>(&q0);
+            const S* h1 = reinterpret_cast<const S*>(&q1);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) v[k] = tof(h0[k]), v[4 + k] = tof(h1[k]);
+        } else {
+            load_unit(a, u, full, v);
+        }
+        if constexpr (sizeof(L) == 4 && sizeof(D) != 4) {  // 16-bit destination, fp32 layout
+            const int64_t e0 = unit_elem<L>(u, full, 0), e1 = unit_elem<L>(u, full, 1);
+            D o0[4], o1[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) o0[k] = fromf<D>(v[k]), o1[k] = fromf<D>(v[4 + k]);
+            *reinterpret_cast<uint2*>(y + e0) = *reinterpret_cast<uint2*>(o0);
+            *reinterpret_cast<uint2*>(y + e1) = *reinterpret_cast<uint2*>(o1);
+        } else {
+            store_unit(y, u, full, v);
+        }
     });
     if (blockIdx.x == 0 && threadIdx.x < (n & 7)) {
         const int64_t i = 8 * n8 + threadIdx.x;
@@ -199,24 +263,24 @@ __global__ void __launch_bounds__(256) cvt_vec_kernel(const S* __restrict__ a, D
 
 template <typename T>
 __global__ void __launch_bounds__(256) fill_vec_kernel(T* __restrict__ y, int64_t n, float val) {
-    const int64_t n8 = n >> 3;
+    const int64_t n8 = n >> 3, full = 32 * (n >> 8);
     float v[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) v[k] = val;
-    VEC_LOOP(n8, store8(y + 8 * u, v));
+    VEC_LOOP(n8, store_unit(y, u, full, v));
     if (blockIdx.x == 0 && threadIdx.x < (n & 7)) y[8 * n8 + threadIdx.x] = fromf<T>(val);
 }
 
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) unary_vec_kernel(const T* __restrict__ a, T* __restrict__ y, int64_t n,
                                                         float p0, float p1) {
-    const int64_t n8 = n >> 3;
+    const int64_t n8 = n >> 3, full = 32 * (n >> 8);
     VEC_LOOP(n8, {
         float v[8];
-        load8(a + 8 * u, v);
+        load_unit(a, u, full, v);
 #pragma unroll
         for (int k = 0; k < 8; ++k) v[k] = un<OP>(v[k], p0, p1);
-        store8(y + 8 * u, v);
+        store_unit(y, u, full, v);
     });
     if (blockIdx.x == 0 && threadIdx.x < (n & 7)) {
         const int64_t i = 8 * n8 + threadIdx.x;
@@ -229,16 +293,17 @@ __global__ void __launch_bounds__(256) unary_vec_kernel(const T* __restrict__ a,
 template <typename T, int OP, int BM>
 __global__ void __launch_bounds__(256) binary_vec_kernel(const T* __restrict__ a, const T* __restrict__ b,
                                                          T* __restrict__ y, int64_t n, int64_t D) {
-    const int64_t n8 = n >> 3;
+    const int64_t n8 = n >> 3, full = 32 * (n >> 8);
+    const bool m32 = n < ((int64_t)1 << 32);  // 32-bit column arithmetic
     const float bs = BM == 2 ? tof(b[0]) : 0.f;
     VEC_LOOP(n8, {
         float v[8], w[8];
-        load8(a + 8 * u, v);
-        if constexpr (BM == 0) load8(b + 8 * u, w);
-        else if constexpr (BM == 1) load8(b + (8 * u) % D, w);
+        load_unit(a, u, full, v);
+        if constexpr (BM == 0) load_unit(b, u, full, w);
+        else if constexpr (BM == 1) load_unit_bcast(b, u, full, D, m32, w);
 #pragma unroll
         for (int k = 0; k < 8; ++k) v[k] = bin<OP>(v[k], BM == 2 ? bs : w[k]);
-        store8(y + 8 * u, v);
+        store_unit(y, u, full, v);
     });
     if (blockIdx.x == 0 && threadIdx.x < (n & 7)) {
         const int64_t i = 8 * n8 + threadIdx.x;
@@ -345,12 +410,25 @@ __global__ void __launch_bounds__(256) reduce_cols_partial_kernel(const T* __res
     for (int k = 1; k < 8; ++k) a = OP == RED_MAX ? fmaxf(a, sm[k][threadIdx.x]) : a + sm[k][threadIdx.x];
     if (col < n) part[(int64_t)blockIdx.y * n + col] = a;
 }
+// part [splits][n] -> out [n]: CTA of 256 threads per 32 columns, its 8 warps
+// summing interleaved subsets of the splits, combined in shared memory.
 template <typename T, int OP>
-__global__ void reduce_cols_final_kernel(const float* __restrict__ part, T* __restrict__ out, int splits, int64_t len,
-                                         int64_t n) {
-    GRID_STRIDE(c, n) {
-        float acc = OP == RED_MAX ? -INFINITY : 0.f;
-        for (int k = 0; k < splits; ++k) acc = OP == RED_MAX ? fmaxf(acc, part[(int64_t)k * n + c]) : acc + part[(int64_t)k * n + c];
+__global__ void __launch_bounds__(256) reduce_cols_final_kernel(const float* __restrict__ part, T* __restrict__ out,
+                                                                int splits, int64_t len, int64_t n) {
+    __shared__ float sm[8][33];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+    float acc = OP == RED_MAX ? -INFINITY : 0.f;
+    if (c < n)
+        for (int k = w; k < splits; k += 8) {
+            const float v = part[(int64_t)k * n + c];
+            acc = OP == RED_MAX ? fmaxf(acc, v) : acc + v;
+        }
+    sm[w][lane] = acc;
+    __syncthreads();
+    if (w == 0 && c < n) {
+#pragma unroll
+        for (int k = 1; k < 8; ++k) acc = OP == RED_MAX ? fmaxf(acc, sm[k][lane]) : acc + sm[k][lane];
         out[c] = fromf<T>(OP == RED_MEAN ? acc / (float)len : acc);
     }
 }
@@ -728,14 +806,16 @@ void reduce(int op, const void* src, int sdt, const int64_t* s_outer, int nd, co
         with_float_type(sdt, [&](auto* t) {
             using T = std::remove_pointer_t<decltype(t)>;
             const int64_t bx = (n_outer + 255) / 256;
-            const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((len + 63) / 64,
+            // enough CTAs to fill the GPU, at least 64 rows per warp
+            const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((len + 511) / 512,
                                                                             (sm_count() * 8 + bx - 1) / bx));
             float* part = (float*)CudaMemoryPool::instance().allocate(sizeof(float) * (size_t)splits * n_outer, st);
             const dim3 g1((unsigned)bx, (unsigned)splits);
             auto go = [&](auto opc) {
                 constexpr int OP = decltype(opc)::value;
                 reduce_cols_partial_kernel<T, OP><<<g1, 256, 0, st>>>((const T*)src, part, len, n_outer);
-                reduce_cols_final_kernel<T, OP><<<grid(n_outer), 256, 0, st>>>(part, (T*)out, splits, len, n_outer);
+                reduce_cols_final_kernel<T, OP><<<(unsigned)((n_outer + 31) / 32), 256, 0, st>>>(part, (T*)out, splits,
+                                                                                              len, n_outer);
             };
             if (op == RED_SUM) go(std::integral_constant<int, RED_SUM>());
             else if (op == RED_MEAN) go(std::integral_constant<int, RED_MEAN>());
