@@ -11,13 +11,16 @@
 //    template parameters, so the inner loop has no branches or conversions
 //    other than the element's own; a [D] operand broadcast over rows and a
 //    scalar operand have their own vector paths;
-//  * reductions over a contiguous last dim use one warp per row: 16-byte
-//    loads along the row, fp32 accumulation, a shuffle butterfly at the end;
+//  * reductions over a contiguous last dim give a warp 8 rows at a time:
+//    16-byte loads along the rows, fp32 accumulation, a reduce-scatter
+//    shuffle butterfly at the end;
 //    reductions over the leading dim of a contiguous [len][n] tensor with few
 //    outputs (column sums) split the rows over CTAs (coalesced rows, a shared
 //    memory combine, fp32 partials from the stream-ordered pool, then a
 //    second pass); other reductions keep one thread per output, whose strided
 //    walk is coalesced across neighbouring outputs;
+//  * the contiguous copy of a transposed 2-D view goes through shared-memory
+//    tiles (64 x 64 for 4-byte elements, 32-bit pairs for 16-bit ones);
 //  * everything else (views with arbitrary strides, mixed dtypes) takes the
 //    generic strided kernels, with 32-bit index arithmetic when the element
 //    count allows.
@@ -312,38 +315,100 @@ __global__ void __launch_bounds__(256) binary_vec_kernel(const T* __restrict__ a
     }
 }
 
-// out[r] = reduce(src[r][0..len)), contiguous rows of len % 8 == 0 (16-byte
-// aligned): one warp per group of 4 rows, each lane one 16-byte vector per row
-// and step, so a lane has 4 independent loads in flight even for the short
-// rows (192 to 512 elements) of the activations.
+// ---- 16-byte units of the reductions: 16 / sizeof(T) elements, kept raw
+// (4 registers) until they are folded into fp32 accumulators ----
+template <int OP>
+__device__ __forceinline__ float red(float a, float b) {
+    return OP == RED_MAX ? fmaxf(a, b) : a + b;
+}
 template <typename T, int OP>
-__global__ void __launch_bounds__(256) reduce_rows_kernel(const T* __restrict__ src, T* __restrict__ out,
-                                                          int64_t rows, int64_t len) {
-    constexpr int R = 4;
+__device__ __forceinline__ float fold16(const uint4& u) {
+    if constexpr (sizeof(T) == 4) {
+        const float* f = reinterpret_cast<const float*>(&u);
+        return red<OP>(red<OP>(f[0], f[1]), red<OP>(f[2], f[3]));
+    } else {
+        float2 p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (std::is_same<T, __half>::value) p[i] = __half22float2(reinterpret_cast<const __half2*>(&u)[i]);
+            else p[i] = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&u)[i]);
+        }
+        return red<OP>(red<OP>(red<OP>(p[0].x, p[0].y), red<OP>(p[1].x, p[1].y)),
+                       red<OP>(red<OP>(p[2].x, p[2].y), red<OP>(p[3].x, p[3].y)));
+    }
+}
+// per-element fold of one unit into VE column accumulators
+template <typename T, int OP>
+__device__ __forceinline__ void fold16_cols(const uint4& u, float (&acc)[16 / sizeof(T)]) {
+    if constexpr (sizeof(T) == 4) {
+        const float* f = reinterpret_cast<const float*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] = red<OP>(acc[e], f[e]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 p;
+            if constexpr (std::is_same<T, __half>::value) p = __half22float2(reinterpret_cast<const __half2*>(&u)[i]);
+            else p = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&u)[i]);
+            acc[2 * i] = red<OP>(acc[2 * i], p.x);
+            acc[2 * i + 1] = red<OP>(acc[2 * i + 1], p.y);
+        }
+    }
+}
+
+// out[r] = reduce(src[r][0..len)), contiguous rows whose length is a whole
+// number of 16-byte units (16-byte aligned).  A warp takes 8 consecutive rows
+// per step and each lane loads one 16-byte unit of each of them, so 8 loads
+// are in flight per lane even for the short rows (192 to 512 elements) of the
+// activations; the raw units stay in 4 registers each until folded, which
+// keeps enough warps resident.  The 8 row sums leave the warp through a
+// reduce-scatter butterfly (4 + 2 + 1 + 1 + 1 shuffles instead of 8 x 5):
+// after it, lanes 4q .. 4q+3 hold row q's total.
+template <typename T, int OP>
+__global__ void __launch_bounds__(256, 4) reduce_rows_kernel(const T* __restrict__ src, T* __restrict__ out,
+                                                             int64_t rows, int64_t len) {
+    constexpr int R = 8, VE = 16 / (int)sizeof(T);
     const int lane = threadIdx.x & 31;
     const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t units = len / VE;
+    const uint4* s = reinterpret_cast<const uint4*>(src);
     const float init = OP == RED_MAX ? -INFINITY : 0.f;
     for (int64_t r0 = warp0 * R; r0 < rows; r0 += nwarps * R) {
         float acc[R];
 #pragma unroll
         for (int q = 0; q < R; ++q) acc[q] = init;
-        for (int64_t k = 8 * lane; k < len; k += 256) {
-            float v[R][8];
+        for (int64_t k = lane; k < units; k += 32) {
+            uint4 raw[R];
 #pragma unroll
             for (int q = 0; q < R; ++q)
-                if (r0 + q < rows) load8(src + (r0 + q) * len + k, v[q]);
+                if (r0 + q < rows) raw[q] = __ldcs(s + (r0 + q) * units + k);
 #pragma unroll
             for (int q = 0; q < R; ++q)
-                if (r0 + q < rows)
+                if (r0 + q < rows) acc[q] = red<OP>(acc[q], fold16<T, OP>(raw[q]));
+        }
+        // reduce-scatter: each stage halves the rows a lane carries
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[q] = OP == RED_MAX ? fmaxf(acc[q], v[q][e]) : acc[q] + v[q][e];
+        for (int i = 0; i < 4; ++i) {
+            const bool hi = lane & 16;
+            const float send = hi ? acc[i] : acc[i + 4], keep = hi ? acc[i + 4] : acc[i];
+            acc[i] = red<OP>(keep, __shfl_xor_sync(0xffffffffu, send, 16));
         }
 #pragma unroll
-        for (int q = 0; q < R; ++q) {
-            const float a = OP == RED_MAX ? mbr::warp_max(acc[q]) : mbr::warp_sum(acc[q]);
-            if (lane == q && r0 + q < rows) out[r0 + q] = fromf<T>(OP == RED_MEAN ? a / (float)len : a);
+        for (int i = 0; i < 2; ++i) {
+            const bool hi = lane & 8;
+            const float send = hi ? acc[i] : acc[i + 2], keep = hi ? acc[i + 2] : acc[i];
+            acc[i] = red<OP>(keep, __shfl_xor_sync(0xffffffffu, send, 8));
         }
+        {
+            const bool hi = lane & 4;
+            const float send = hi ? acc[0] : acc[1], keep = hi ? acc[1] : acc[0];
+            acc[0] = red<OP>(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+        }
+        acc[0] = red<OP>(acc[0], __shfl_xor_sync(0xffffffffu, acc[0], 2));
+        acc[0] = red<OP>(acc[0], __shfl_xor_sync(0xffffffffu, acc[0], 1));
+        const int q = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+        if ((lane & 3) == 0 && r0 + q < rows) out[r0 + q] = fromf<T>(OP == RED_MEAN ? acc[0] / (float)len : acc[0]);
     }
 }
 
@@ -365,65 +430,71 @@ __global__ void __launch_bounds__(256) reduce_rows_scalar_kernel(const T* __rest
     }
 }
 
-// Column partials of a contiguous [len][n] (n % 8 == 0, 16-byte aligned):
-// CTA (bx, by) covers columns [256 bx, 256 bx + 256), each lane 8 consecutive
-// columns by one 16-byte load per row, over rows by, by + gridDim.y, ... split
-// among its 8 warps; the warps' partials are combined in shared memory into
-// part[by][col].
+// Column partials of a contiguous [len][n] (n a whole number of 16-byte
+// units, 16-byte aligned): CTA (bx, by) covers the W = 32 units' columns
+// [W bx, W bx + W) (256 columns for 16-bit types, 128 for fp32), each lane
+// one unit's columns, over rows by, by + gridDim.y, ... split among its 8
+// warps with 16 rows' units in flight per lane; the warps' partials are
+// combined in shared memory into part[by][col].
 template <typename T, int OP>
-__global__ void __launch_bounds__(256) reduce_cols_partial_kernel(const T* __restrict__ src, float* __restrict__ part,
-                                                                  int64_t len, int64_t n) {
-    __shared__ float sm[8][256];
+__global__ void __launch_bounds__(256, 2) reduce_cols_partial_kernel(const T* __restrict__ src,
+                                                                     float* __restrict__ part, int64_t len,
+                                                                     int64_t n) {
+    constexpr int VE = 16 / (int)sizeof(T), W = 32 * VE, U = 16;
+    __shared__ float sm[8][W];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t c0 = (int64_t)blockIdx.x * 256 + 8 * lane;
+    const int64_t c0 = (int64_t)blockIdx.x * W + VE * lane;
     const float init = OP == RED_MAX ? -INFINITY : 0.f;
-    float acc[8];
+    float acc[VE];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = init;
+    for (int e = 0; e < VE; ++e) acc[e] = init;
     if (c0 < n) {
-        const int64_t step = (int64_t)gridDim.y * 8;
+        const int64_t step = (int64_t)gridDim.y * 8, nu = n / VE;
+        const uint4* col = reinterpret_cast<const uint4*>(src + c0);
         int64_t r = (int64_t)blockIdx.y * 8 + w;
-        // two rows' vectors in flight per lane
-        for (; r + step < len; r += 2 * step) {
-            float v[8], u[8];
-            load8(src + r * n + c0, v);
-            load8(src + (r + step) * n + c0, u);
+        for (; r + (U - 1) * step < len; r += U * step) {
+            uint4 raw[U];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                acc[e] = OP == RED_MAX ? fmaxf(acc[e], v[e]) : acc[e] + v[e];
-                acc[e] = OP == RED_MAX ? fmaxf(acc[e], u[e]) : acc[e] + u[e];
-            }
-        }
-        if (r < len) {
-            float v[8];
-            load8(src + r * n + c0, v);
+            for (int u = 0; u < U; ++u) raw[u] = __ldcs(col + (r + u * step) * nu);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = OP == RED_MAX ? fmaxf(acc[e], v[e]) : acc[e] + v[e];
+            for (int u = 0; u < U; ++u) fold16_cols<T, OP>(raw[u], acc);
         }
+        for (; r < len; r += step) fold16_cols<T, OP>(__ldcs(col + r * nu), acc);
     }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sm[w][8 * lane + e] = acc[e];
+    for (int e = 0; e < VE; ++e) sm[w][VE * lane + e] = acc[e];
     __syncthreads();
-    const int64_t col = (int64_t)blockIdx.x * 256 + threadIdx.x;
-    float a = sm[0][threadIdx.x];
+    for (int c = threadIdx.x; c < W; c += 256) {
+        float a = sm[0][c];
 #pragma unroll
-    for (int k = 1; k < 8; ++k) a = OP == RED_MAX ? fmaxf(a, sm[k][threadIdx.x]) : a + sm[k][threadIdx.x];
-    if (col < n) part[(int64_t)blockIdx.y * n + col] = a;
+        for (int k = 1; k < 8; ++k) a = red<OP>(a, sm[k][c]);
+        const int64_t gc = (int64_t)blockIdx.x * W + c;
+        if (gc < n) part[(int64_t)blockIdx.y * n + gc] = a;
+    }
 }
 // part [splits][n] -> out [n]: CTA of 256 threads per 32 columns, its 8 warps
-// summing interleaved subsets of the splits, combined in shared memory.
+// summing interleaved subsets of the splits (four loads in flight per lane),
+// combined in shared memory.
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) reduce_cols_final_kernel(const float* __restrict__ part, T* __restrict__ out,
                                                                 int splits, int64_t len, int64_t n) {
     __shared__ float sm[8][33];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t c = (int64_t)blockIdx.x * 32 + lane;
-    float acc = OP == RED_MAX ? -INFINITY : 0.f;
-    if (c < n)
-        for (int k = w; k < splits; k += 8) {
-            const float v = part[(int64_t)k * n + c];
-            acc = OP == RED_MAX ? fmaxf(acc, v) : acc + v;
+    const float init = OP == RED_MAX ? -INFINITY : 0.f;
+    float a4[4] = {init, init, init, init};
+    if (c < n) {
+        int k = w;
+        for (; k + 24 < splits; k += 32) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = part[(int64_t)(k + 8 * u) * n + c];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) a4[u] = red<OP>(a4[u], v[u]);
         }
+        for (; k < splits; k += 8) a4[0] = red<OP>(a4[0], part[(int64_t)k * n + c]);
+    }
+    float acc = red<OP>(red<OP>(a4[0], a4[1]), red<OP>(a4[2], a4[3]));
     sm[w][lane] = acc;
     __syncthreads();
     if (w == 0 && c < n) {
@@ -456,6 +527,81 @@ __global__ void __launch_bounds__(256) transpose2d_kernel(const E* __restrict__ 
         for (int k = ty; k < 32; k += 8) {
             const int64_t r = r0 + k, c = c0 + tx;
             if (r < rows && c < cols) dst[r * cols + c] = tile[tx][k];
+        }
+        __syncthreads();
+    }
+}
+
+// The same copy for 4-byte elements through 64 x 64 tiles: each thread has
+// 16 loads in flight (a 32 x 32 tile gives 4, too few bytes in flight per SM
+// to cover HBM latency).
+__global__ void __launch_bounds__(256) transpose64_u32_kernel(const uint32_t* __restrict__ src,
+                                                              uint32_t* __restrict__ dst, int64_t rows, int64_t cols) {
+    __shared__ uint32_t tile[64][65];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int64_t tcn = (cols + 63) / 64, ntiles = ((rows + 63) / 64) * tcn;
+    for (int64_t tb = blockIdx.x; tb < ntiles; tb += gridDim.x) {
+        const int64_t r0 = (tb / tcn) * 64, c0 = (tb % tcn) * 64;
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int k = ty + 8 * (i >> 1), x = tx + 32 * (i & 1);
+            const int64_t c = c0 + k, r = r0 + x;
+            v[i] = (c < cols && r < rows) ? __ldcs(src + c * rows + r) : 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tile[ty + 8 * (i >> 1)][tx + 32 * (i & 1)] = v[i];
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int k = ty + 8 * (i >> 1), x = tx + 32 * (i & 1);
+            const int64_t r = r0 + k, c = c0 + x;
+            if (r < rows && c < cols) __stcs(dst + r * cols + c, tile[x][k]);
+        }
+        __syncthreads();
+    }
+}
+
+// 16-bit elements with even rows and cols, moved as 32-bit pairs.  Source
+// words A = src[2p][2q .. 2q+1] and B = src[2p+1][2q .. 2q+1] (two
+// neighbouring source rows) give the destination words dst[2q][2p .. 2p+1] =
+// (A.lo, B.lo) and dst[2q+1][2p .. 2p+1] = (A.hi, B.hi), so every global
+// access is a full 4-byte word and a warp moves 128 contiguous bytes.  A tile
+// is 32 p x 64 q (64 source rows x 128 source columns); each thread has 16
+// loads in flight.
+__global__ void __launch_bounds__(256) transpose_pairs16_kernel(const uint32_t* __restrict__ src,
+                                                                uint32_t* __restrict__ dst, int64_t rows,
+                                                                int64_t cols) {
+    __shared__ uint32_t lo[32][65], hi[32][65];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int64_t np = cols / 2, nq = rows / 2;  // words per dst row, words per src row
+    const int64_t tpn = (np + 31) / 32, ntiles = ((nq + 63) / 64) * tpn;
+    for (int64_t tb = blockIdx.x; tb < ntiles; tb += gridDim.x) {
+        const int64_t q0 = (tb / tpn) * 64, p0 = (tb % tpn) * 32;
+        uint32_t a[8], b[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int pl = ty + 8 * (i >> 1), ql = tx + 32 * (i & 1);
+            const int64_t p = p0 + pl, q = q0 + ql;
+            const bool ok = p < np && q < nq;
+            a[i] = ok ? __ldcs(src + (2 * p) * nq + q) : 0u;
+            b[i] = ok ? __ldcs(src + (2 * p + 1) * nq + q) : 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int pl = ty + 8 * (i >> 1), ql = tx + 32 * (i & 1);
+            lo[pl][ql] = __byte_perm(a[i], b[i], 0x5410);
+            hi[pl][ql] = __byte_perm(a[i], b[i], 0x7632);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int ql = ty + 8 * j;
+            const int64_t q = q0 + ql, p = p0 + tx;
+            if (q < nq && p < np) {
+                __stcs(dst + (2 * q) * np + p, lo[tx][ql]);
+                __stcs(dst + (2 * q + 1) * np + p, hi[tx][ql]);
+            }
         }
         __syncthreads();
     }
@@ -667,8 +813,16 @@ void copy(const void* src, int sdt, const int64_t* sstride, void* dst, int ddt, 
         if (k == 2 && sdt == ddt && ss2[0] == 1 && ss2[1] == sh2[0] && is_contig(nd, shape, dstride)) {
             const int64_t tiles = ((sh2[0] + 31) / 32) * ((sh2[1] + 31) / 32);
             const unsigned gr = (unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)sm_count() * 16));
+            const auto grid_for = [&](int64_t t) {
+                return (unsigned)std::max<int64_t>(1, std::min<int64_t>(t, (int64_t)sm_count() * 8));
+            };
+            const bool words = ((uintptr_t)src & 3) == 0 && ((uintptr_t)dst & 3) == 0;
             if (sdt == F32)
-                transpose2d_kernel<float><<<gr, 256, 0, st>>>((const float*)src, (float*)dst, sh2[0], sh2[1]);
+                transpose64_u32_kernel<<<grid_for(((sh2[0] + 63) / 64) * ((sh2[1] + 63) / 64)), 256, 0, st>>>(
+                    (const uint32_t*)src, (uint32_t*)dst, sh2[0], sh2[1]);
+            else if (sdt != I64 && words && sh2[0] % 2 == 0 && sh2[1] % 2 == 0)
+                transpose_pairs16_kernel<<<grid_for(((sh2[0] / 2 + 63) / 64) * ((sh2[1] / 2 + 31) / 32)), 256, 0,
+                                           st>>>((const uint32_t*)src, (uint32_t*)dst, sh2[0], sh2[1]);
             else if (sdt == I64)
                 transpose2d_kernel<int64_t><<<gr, 256, 0, st>>>((const int64_t*)src, (int64_t*)dst, sh2[0], sh2[1]);
             else
@@ -805,10 +959,12 @@ void reduce(int op, const void* src, int sdt, const int64_t* s_outer, int nd, co
         len >= 64 && n_outer % 8 == 0 && aligned16(src) &&
         with_float_type(sdt, [&](auto* t) {
             using T = std::remove_pointer_t<decltype(t)>;
-            const int64_t bx = (n_outer + 255) / 256;
-            // enough CTAs to fill the GPU, at least 64 rows per warp
-            const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((len + 511) / 512,
-                                                                            (sm_count() * 8 + bx - 1) / bx));
+            const int64_t bx = (n_outer + 32 * (16 / (int64_t)sizeof(T)) - 1) / (32 * (16 / (int64_t)sizeof(T)));
+            // two CTAs per SM (each warp then has 16 rows' loads in flight per
+            // step, enough to cover HBM latency) and at least 16 rows per warp,
+            // so the second pass sums few partials
+            const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((len + 127) / 128,
+                                                                            (sm_count() * 2 + bx - 1) / bx));
             float* part = (float*)CudaMemoryPool::instance().allocate(sizeof(float) * (size_t)splits * n_outer, st);
             const dim3 g1((unsigned)bx, (unsigned)splits);
             auto go = [&](auto opc) {

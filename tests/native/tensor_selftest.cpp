@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <functional>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "memory_pool.h"
@@ -165,8 +166,11 @@ int main() {
     for (DType dt : {DType::Float32, DType::Float16, DType::BFloat16}) {
         const std::string tn = dt == DType::Float32 ? "f32" : dt == DType::Float16 ? "f16" : "bf16";
         const float tol = dt == DType::Float32 ? 1e-5f : dt == DType::Float16 ? 2e-3f : 1.6e-2f;
-        for (int cols : {64, 70}) {  // 70: rows not a multiple of 8 elements (vector tails / scalar rows)
-            const int rows = 1000, n = rows * cols;
+        // 70: rows not a multiple of 8 elements (vector tails / scalar rows);
+        // 1003 x 72: a partial group of 8 rows and odd 16-bit transposes;
+        // 999 x 33: odd sizes everywhere
+        for (auto rc : {std::pair<int, int>{1000, 64}, {1000, 70}, {1003, 72}, {999, 33}}) {
+            const int rows = rc.first, cols = rc.second, n = rows * cols;
             std::vector<float> hx(n), hy(n), hr(cols);
             for (int i = 0; i < n; ++i) {
                 hx[i] = (float)((i * 37) % 101) / 16.0f - 3.0f;  // exact in every dtype
@@ -177,7 +181,7 @@ int main() {
             Tensor y = Tensor::from_cpu_f32(hy.data(), {rows, cols}).to_dtype(dt);
             Tensor r = Tensor::from_cpu_f32(hr.data(), {cols}).to_dtype(dt);
             Tensor s1 = Tensor::full({1}, 0.75f, dt);
-            const std::string tag = " " + tn + " [1000 x " + std::to_string(cols) + "]";
+            const std::string tag = " " + tn + " [" + std::to_string(rows) + " x " + std::to_string(cols) + "]";
             std::vector<float> e_add(n), e_div(n), e_row(n), e_sc(n), e_cl(n);
             for (int i = 0; i < n; ++i) {
                 e_add[i] = hx[i] + hy[i];
