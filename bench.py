@@ -364,6 +364,7 @@ def main():
     m.profile(False)
     T = cfg["chunk_size"] // cfg["stft_hop_length"] + 1
     flops_fwd = model_flops(cfg, T, wl["chunk_batch"], band_dims(cfg))
+    flops_fwd["ffn"] = flops_fwd["gemm_ffn1"] + flops_fwd["gemm_ffn2"]  # the fused FFN block: both contractions
     kind = max(prof, key=lambda k: prof[k][0])
     kms, kn = prof[kind]
     roof = None

@@ -270,6 +270,18 @@ MBR_API int mbr_op_rope(const void* d_x, const float* d_cos, const float* d_sin,
 MBR_API int mbr_op_linear(const void* d_x, const void* d_w, const float* d_bias, void* d_y, int64_t rows, int in,
                           int out, int act, int dtype, void* stream);
 
+/* Feed-forward block with its residual add, as one tcgen05 kernel:
+ * resid [rows][dim] (fp32) += GELU(x . w1^T + b1) . w2^T + b2, with x
+ * [rows][dim], w1 [hidden][dim], w2 [dim][hidden] in dtype (fp16 / bf16), b1
+ * [hidden] and b2 [dim] fp32, GELU the exact erf form, the hidden activations
+ * rounded to dtype (they never reach device memory).  Replaces
+ * try_feedforward_fused_residual (src/mbr_cuda_tile.cu:6840) over the fused
+ * FFN kernels of src/mbr_ffn12_cutile.cu.  Needs dim 256 or 384, hidden a
+ * multiple of 64 and 16-byte aligned pointers (else MBR_ERR_UNSUPPORTED);
+ * the call returns after the stream drains. */
+MBR_API int mbr_op_ffn(const void* d_x, const void* d_w1, const float* d_b1, const void* d_w2, const float* d_b2,
+                       float* d_resid, int64_t rows, int dim, int hidden, int dtype, void* stream);
+
 /* Multi-head attention with the head merge: q, k, v [B][heads][N][dim_head]
  * (dtype), out [B][N][heads*dim_head] = softmax(q k^T * scale) v, multiplied
  * by gates [B][N][heads] (fp32, already sigmoid'ed) when d_gates is non-null.

@@ -564,6 +564,14 @@ MBR_API int mbr_op_linear(const void* d_x, const void* d_w, const float* d_bias,
     });
 }
 
+MBR_API int mbr_op_ffn(const void* d_x, const void* d_w1, const float* d_b1, const void* d_w2, const float* d_b2,
+                       float* d_resid, int64_t rows, int dim, int hidden, int dtype, void* stream) {
+    return guard([&] {
+        need(d_x && d_w1 && d_b1 && d_w2 && d_b2 && d_resid && rows >= 0 && dim > 0 && hidden > 0, "bad argument");
+        mbr::opsapi::ffn(d_x, d_w1, d_b1, d_w2, d_b2, d_resid, rows, dim, hidden, dtype, (cudaStream_t)stream);
+    });
+}
+
 MBR_API int mbr_op_attention(const void* d_q, const void* d_k, const void* d_v, int64_t B, int heads, int N,
                              int dim_head, float scale, const float* d_gates, void* d_out, int dtype, void* stream) {
     return guard([&] {

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.h"
@@ -350,6 +351,8 @@ MelBandRoformer::MelBandRoformer(const ModelWeights& w, int device, int dtype) :
         }
     gemm_backend_ = dtype_ == DT_F32 ? BACKEND_SIMT : BACKEND_TC;
     attn_backend_ = dtype_ == DT_F32 ? BACKEND_SIMT : BACKEND_TC;
+    const char* ff = std::getenv("MBR_FFN_FUSED");
+    ffn_fused_ = ff && ff[0] == '1';
 }
 
 MelBandRoformer::~MelBandRoformer() {
@@ -515,9 +518,25 @@ MelBandRoformer::Workspace& MelBandRoformer::workspace(int B, int64_t L) {
                 firsts.push_back(first);
             }
         }
+        // the fused FFN blocks (FFN1 + GELU + FFN2 + residual) of every layer
+        std::vector<size_t> ffn_firsts;
+        if (ffn_fused_ && tc::ffn_supported(D_, hid_, dtype_)) {
+            for (size_t i = 0; i + 3 < ws->layer_plans.size(); i += 4) {
+                Plan& p1 = ws->layer_plans[i + 2];
+                const Plan& p2 = ws->layer_plans[i + 3];
+                tc::FfnLaunch F;
+                size_t first = 0;
+                tc::ffn_prepare(p1.a_base, p1.b_base, ws->h_groups[p1.first].bias, p2.b_base,
+                                ws->h_groups[p2.first].bias, ws->R, ws->M, D_, hid_, dtype_, tiles, F, first);
+                p1.ffn = (int)ws->ffn_launches.size();
+                ws->ffn_launches.push_back(F);
+                ffn_firsts.push_back(first);
+            }
+        }
         MBR_CUDA(cudaMalloc(&ws->d_tiles, sizeof(int4) * std::max<size_t>(1, tiles.size())));
         MBR_CUDA(cudaMemcpy(ws->d_tiles, tiles.data(), sizeof(int4) * tiles.size(), cudaMemcpyHostToDevice));
         for (size_t i = 0; i < ws->launches.size(); ++i) ws->launches[i].tiles = ws->d_tiles + firsts[i];
+        for (size_t i = 0; i < ws->ffn_launches.size(); ++i) ws->ffn_launches[i].items = ws->d_tiles + ffn_firsts[i];
     }
     Workspace& ref = *ws;
     ws_[key] = std::move(ws);
@@ -782,8 +801,12 @@ void MelBandRoformer::run_transformer(Workspace& ws, const TransW& tw, int mode,
         run_gemm(ws, p[1], PK_GEMM_OUT, st);
         MBR_LAUNCH(PK_NORM, ops::rms_norm(ws.R, M, D_, lw.ff_gamma, scale, ws.xn, dtype_, 0, NB_, nullptr, nullptr,
                                           nullptr, 0, nullptr, st));
-        run_gemm(ws, p[2], PK_GEMM_FFN1, st);
-        run_gemm(ws, p[3], PK_GEMM_FFN2, st);
+        if (p[2].ffn >= 0) {
+            MBR_LAUNCH(PK_FFN, tc::ffn_launch(ws.ffn_launches[p[2].ffn], dtype_, d_err_, st));
+        } else {
+            run_gemm(ws, p[2], PK_GEMM_FFN1, st);
+            run_gemm(ws, p[3], PK_GEMM_FFN2, st);
+        }
     }
     // final RMSNorm of the transformer; the model's last one also writes the
     // band-major 16-bit copy the mask estimators read

@@ -17,6 +17,7 @@
 
 #include "common.h"
 #include "ops_api.h"
+#include "ffn_tc.h"
 #include "gemm_tc.h"
 #include "ops.h"
 #include "weights.h"
@@ -79,6 +80,7 @@ enum ProfKind {
     PK_GEMM_MASK_OUT,
     PK_MASK_SCATTER,
     PK_ISTFT,
+    PK_FFN,  // fused FFN1 + GELU + FFN2 (+ residual)
     PK_COUNT
 };
 
@@ -151,6 +153,7 @@ private:
         // head-major for the CUDA-core attention
         int launch_scatter = -1;
         int qkv_mode = -1;  // QKV projection of a time (0) / band (1) transformer
+        int ffn = -1;       // FFN1 plan: index into Workspace::ffn_launches of the fused FFN block
         // operand tensor shapes for the tensor-core path (rows x cols, elements)
         const void* a_base = nullptr;
         int64_t a_rows = 0, a_cols = 0;
@@ -204,6 +207,7 @@ private:
         ops::GemmGroup* d_groups;
         std::vector<ops::GemmGroup> h_groups;
         std::vector<tc::GemmLaunch> launches;
+        std::vector<tc::FfnLaunch> ffn_launches;
         int4* d_tiles = nullptr;
         Plan band_split;
         std::vector<Plan> layer_plans;  // [depth][2][layers][4]: qkv, out, ffn1, ffn2
@@ -232,6 +236,9 @@ private:
         hid_ = 1536;
     int64_t J_ = 0, KP_ = 0;
     int gemm_backend_ = BACKEND_SIMT, attn_backend_ = BACKEND_SIMT;
+    // FFN1 + GELU + FFN2 as one kernel where it applies (MBR_FFN_FUSED=1; the
+    // default keeps the two GEMMs, measured faster on B200)
+    bool ffn_fused_ = false;
     int64_t launches_ = 0;
     bool graphs_on_ = true;
     void drop_graphs();

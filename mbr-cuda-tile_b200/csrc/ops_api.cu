@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "ops_api.h"
 #include "attention_tc.h"
+#include "ffn_tc.h"
 #include "gemm_tc.h"
 #include "ops.h"
 
@@ -716,6 +717,32 @@ void linear(const void* x, const void* w, const float* bias, void* y, int64_t ro
         ops::gemm_simt(S.d_group, 1, g.M, out, dtype, epi, st);
     }
     check_op_error(st);  // the scratch (and the pageable sources above) are reused next call
+}
+
+void ffn(const void* x, const void* w1, const float* b1, const void* w2, const float* b2, float* resid, int64_t rows,
+         int dim, int hidden, int dtype, cudaStream_t st) {
+    if (!tc::ffn_supported(dim, hidden, dtype))
+        throw Error(ERR_UNSUPPORTED, "ffn: needs fp16/bf16, dim 256 or 384 and hidden a multiple of 64");
+    if (rows == 0) return;
+    int dev = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    MBR_CHECK(dev >= 0 && dev < kMaxDevices, "device index out of range");
+    LinearScratch& S = linear_scratch(dev);
+    std::lock_guard<std::mutex> lock(S.mu);
+    std::vector<int4> items;
+    tc::FfnLaunch L;
+    size_t first = 0;
+    tc::ffn_prepare(x, w1, b1, w2, b2, resid, rows, dim, hidden, dtype, items, L, first);
+    if (items.size() > S.tile_cap) {
+        if (S.d_tiles) MBR_CUDA(cudaFree(S.d_tiles));
+        S.d_tiles = nullptr;
+        MBR_CUDA(cudaMalloc(&S.d_tiles, items.size() * sizeof(int4)));
+        S.tile_cap = items.size();
+    }
+    MBR_CUDA(cudaMemcpyAsync(S.d_tiles, items.data(), items.size() * sizeof(int4), cudaMemcpyHostToDevice, st));
+    L.items = S.d_tiles + first;
+    tc::ffn_launch(L, dtype, op_error_word(), st);
+    check_op_error(st);  // the scratch (and the pageable source above) are reused next call
 }
 
 void add(const void* a, const void* b, void* y, int64_t n, int dtype, cudaStream_t st) {

@@ -63,6 +63,10 @@ void attention(const void* q, const void* k, const void* v, int64_t B, int H, in
 // stream drains (the launch descriptors live in per-device scratch).
 void linear(const void* x, const void* w, const float* bias, void* y, int64_t rows, int in, int out, int act,
             int dtype, cudaStream_t st);
+// resid += GELU(x w1^T + b1) w2^T + b2 through the fused tcgen05 FFN kernel
+// (dim 256 / 384, hidden % 64 == 0, fp16 / bf16); returns after the stream drains.
+void ffn(const void* x, const void* w1, const float* b1, const void* w2, const float* b2, float* resid, int64_t rows,
+         int dim, int hidden, int dtype, cudaStream_t st);
 // STFT frames of an L-sample signal (center, reflect pad n_fft/2)
 int64_t stft_frames(int64_t L, int hop);
 // sig [n][L] -> out [n][1025][T] complex (n_fft 2048, periodic Hann, onesided)

@@ -29,7 +29,7 @@ EXPORTS = [
     "mbr_forward_chunk", "mbr_forward_tap", "mbr_separate_device", "mbr_separate", "mbr_shard_info",
     "mbr_shard_run", "mbr_shard_window", "mbr_plan_shard_window", "mbr_shard_run_window", "mbr_shard_add_boundary", "mbr_shard_finalize", "mbr_set_graphs", "mbr_set_backend", "mbr_last_launches",
     "mbr_sync_check", "mbr_profile_enable", "mbr_profile_read",
-    "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_op_attention", "mbr_op_linear",
+    "mbr_op_rms_norm", "mbr_op_add", "mbr_op_gelu", "mbr_op_sigmoid_gate", "mbr_op_rope", "mbr_op_attention", "mbr_op_linear", "mbr_op_ffn",
     "mbr_rope_tables",
     "mbr_op_band_gather", "mbr_op_mask_scatter", "mbr_op_stft", "mbr_op_istft", "mbr_op_istft_noalloc",
     "mbr_plan_shard", "mbr_wav_info", "mbr_wav_read", "mbr_wav_write",
@@ -38,7 +38,8 @@ EXPORTS = [
 
 # Kernel classes of mbr_profile_read.
 PROFILE_KINDS = ["stft", "band_gather", "gemm_bandsplit", "norm", "gemm_qkv", "rope", "attn_time", "attn_freq",
-                 "gemm_out", "gemm_ffn1", "gemm_ffn2", "gemm_mask_hidden", "gemm_mask_out", "mask_scatter", "istft"]
+                 "gemm_out", "gemm_ffn1", "gemm_ffn2", "gemm_mask_hidden", "gemm_mask_out", "mask_scatter", "istft",
+                 "ffn"]
 
 _lib = None
 
@@ -90,6 +91,7 @@ def lib():
         L.mbr_op_rope.argtypes = [fp, fp, fp, fp, i64, c_int, c_int, c_int, vp]
         L.mbr_op_linear.argtypes = [fp, fp, fp, fp, i64, c_int, c_int, c_int, c_int, vp]
         L.mbr_op_attention.argtypes = [fp, fp, fp, i64, c_int, c_int, c_int, c_float, fp, fp, c_int, vp]
+        L.mbr_op_ffn.argtypes = [fp, fp, fp, fp, fp, fp, i64, c_int, c_int, c_int, vp]
         L.mbr_rope_tables.argtypes = [c_int, c_int, fp, fp]
         L.mbr_op_band_gather.argtypes = [vp, fp, c_int, c_int, fp, c_int, vp]
         L.mbr_op_mask_scatter.argtypes = [vp, fp, fp, c_int, c_int, c_int, fp, c_int, vp]
@@ -202,6 +204,17 @@ def op_linear(x, w, bias=None, act=ACT_NONE, out=None, stream=None):
     b = _ptr(bias) if bias is not None else None
     _check(lib().mbr_op_linear(_ptr(x), _ptr(w), b, _ptr(out), rows, fin, fout, int(act), _dt(x), _stream(stream)))
     return out
+
+
+def op_ffn(x, w1, b1, w2, b2, resid, stream=None):
+    """resid [rows, dim] fp32 += GELU(x . w1^T + b1) . w2^T + b2 (x, w1 [hidden, dim], w2 [dim, hidden]
+    fp16 / bf16; b1, b2 fp32), in place; returns resid."""
+    rows, dim = x.shape
+    hidden = w1.shape[0]
+    assert w1.shape == (hidden, dim) and w2.shape == (dim, hidden) and resid.shape == (rows, dim)
+    _check(lib().mbr_op_ffn(_ptr(x), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(resid), rows, dim, hidden, _dt(x),
+                            _stream(stream)))
+    return resid
 
 
 def op_attention(q, k, v, scale=0.0, gates=None, out=None, stream=None):
