@@ -711,6 +711,9 @@ def run_op_sweep(args):
         for _ in range(reps):
             flush.zero_()
             torch.sum(flush_rd, 0, out=flush_sum)
+            # the GPU spins (~50 us) while the host issues the start event and the op, so the
+            # event pair brackets the launch itself and not the Python and ctypes call overhead
+            torch.cuda._sleep(100000)
             e0.record()
             fn()
             e1.record()
