@@ -744,12 +744,16 @@ def run_op_sweep(args):
             dt, e = tdt[dtype], torch.tensor([], dtype=tdt[dtype]).element_size()
             for B in [int(b) for b in args.batches.split(",") if b]:
                 rows = B * T * NB
-                for D in ((192, 384, 512) if any(want(o) for o in ("rms_norm", "add", "gelu", "sigmoid_gate", "rope"))
-                          else ()):
+                row_ops = ("copy", "rms_norm", "add", "gelu", "sigmoid_gate", "rope")
+                for D in ((192, 384, 512) if any(want(o) for o in row_ops) else ()):
                     N = rows * D
                     x = torch.randn(rows, D, generator=gen, device="cuda").to(dt)
                     y = torch.empty_like(x)
                     gamma = torch.ones(D, device="cuda")
+                    if want("copy"):
+                        # reference line, not one of this library's ops: torch's own device copy of the
+                        # same bytes under the same timing, i.e. what HBM gives a transfer of this size
+                        report("copy", dtype, D, B, 2 * N * e, timed(lambda: y.copy_(x)))
                     if want("rms_norm"):
                         report("rms_norm", dtype, D, B, 2 * N * e + D * 4,
                                timed(lambda: cudasep.op_rms_norm(x, gamma, D ** 0.5, y=y)))
@@ -786,7 +790,8 @@ def run_op_sweep(args):
         model.close()
     by_op = {}
     for r in results:
-        by_op.setdefault(r["op"], []).append(r["frac_of_hbm_peak"])
+        if r["op"] != "copy":  # the reference line is not one of the ops
+            by_op.setdefault(r["op"], []).append(r["frac_of_hbm_peak"])
     print(json.dumps({"metric": "tensor-op HBM GB/s vs peak", "peak_gbs": peak,
                       "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy bandwidth)",
                       "median_frac_by_op": {k: sorted(v)[len(v) // 2] for k, v in by_op.items()},

@@ -72,6 +72,13 @@ __device__ __forceinline__ void cp_async(void* smem, const void* gmem) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(s), "l"(gmem), "n"(N) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// closes this thread's current group of asynchronous copies
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// waits until at most N of this thread's committed copy groups are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -102,23 +109,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// The reference's GELU 0.5 x (1 + erf(x)) (see gelu_erf) for the stand-alone
-// op: erf by Abramowitz & Stegun 7.1.26, erf(z) = 1 - (a1 t + ... + a5 t^5)
-// e^{-z^2}, t = 1 / (1 + p z), |error| <= 1.5e-7.  With q = 0.5 x (1 - erf(|x|))
-// (the tail, kept as a product so it does not cancel) gelu(x) = x - q for
-// x >= 0, q otherwise.
-__device__ __forceinline__ float gelu_as(float x) {
-    const float z = fabsf(x);
-    const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
-    float p = fmaf(1.061405429f, t, -1.453152027f);
-    p = fmaf(p, t, 1.421413741f);
-    p = fmaf(p, t, -0.284496736f);
-    p = fmaf(p, t, 0.254829592f);
-    const float e = ex2_approx(x * x * -1.4426950408889634f);  // e^{-x^2} = 2^{-x^2 log2(e)}
-    const float q = 0.5f * x * (p * t) * e;
-    return x >= 0.0f ? x - q : q;
 }
 
 // The reference's GELU 0.5 x (1 + erf(x)) (see gelu_erf) of N values (N even)

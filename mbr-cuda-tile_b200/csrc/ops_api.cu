@@ -5,6 +5,7 @@
 // vectorised, coalesced, one pass over HBM, reductions in registers.
 #include <algorithm>
 #include <cmath>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -132,8 +133,7 @@ __global__ void __launch_bounds__(256) gelu_kernel(const T* __restrict__ a, T* _
             if (i0 + u * stride < n8) {
                 Vec8<T> x;
                 x.set(ra[u]);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) x.v[k] = gelu_as(x.v[k]);  // exact-erf GELU, A&S 7.1.26
+                gelu_tail(x.v);  // the reference's 0.5 x (1 + erf(x)), one exponential per element
                 x.store(y + 8 * (i0 + u * stride));
             }
     }
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kBandWarps * 32) gather_tiled_kernel(
 
 // Mask scatter-average (apply_mask_and_scatter, gather form):
 // out[b][s][c][f][t] = sum_{j: fi_j = f*C+c} spec[b][c][f][t] * mask[s][b*T+t][j] / nbpf[f*C+c]
-// (each term divided, as the reference does before its atomic add).
+// (each term scaled by 1 / nbpf before the sum; the reference divides each term before its atomic add).
 // One CTA per (frequency-range tile, 32 frames, b, s).  Everything the CTA
 // reads is copied into shared memory with asynchronous copies issued up front
 // (the tile's spectrum rows, bin weights and entry tables, then the masks of
@@ -459,20 +459,14 @@ __global__ void __launch_bounds__(kBandWarps * 32) scatter_tiled_kernel(
         const float den = fmaxf(nbs[row], 1e-8f);
         float2 acc = make_float2(0.f, 0.f);
         const int q0 = bos[row], q1 = bos[row + 1];
-        if ((__float_as_uint(den) & 0x7fffffu) == 0u) {
-            // power-of-two weight: the product with its exact reciprocal is the correctly rounded quotient
-            const float inv = 1.f / den;
-            for (int q = q0; q < q1; ++q) {
-                const float2 mm = pair_to_f32<T>(mkl[bks[q]]);
-                acc.x += (xv.x * mm.x - xv.y * mm.y) * inv;
-                acc.y += (xv.x * mm.y + xv.y * mm.x) * inv;
-            }
-        } else {
-            for (int q = q0; q < q1; ++q) {
-                const float2 mm = pair_to_f32<T>(mkl[bks[q]]);
-                acc.x += (xv.x * mm.x - xv.y * mm.y) / den;
-                acc.y += (xv.x * mm.y + xv.y * mm.x) / den;
-            }
+        // each term times the row's correctly rounded reciprocal: exact for
+        // power-of-two weights, within about one ulp of the quotient otherwise,
+        // and one division per row instead of two per term
+        const float inv = 1.f / den;
+        for (int q = q0; q < q1; ++q) {
+            const float2 mm = pair_to_f32<T>(mkl[bks[q]]);
+            acc.x += (xv.x * mm.x - xv.y * mm.y) * inv;
+            acc.y += (xv.x * mm.y + xv.y * mm.x) * inv;
         }
         op[(c * (F - nf) + row) * Tn] = acc;
     }
@@ -575,6 +569,31 @@ __global__ void istft_ola_ref_kernel(const float* __restrict__ frames, int64_t n
 
 unsigned grid_for(int64_t work, int threads) {
     return (unsigned)std::max<int64_t>(1, std::min<int64_t>(nblk(work, threads), (int64_t)sm_count() * 16));
+}
+
+// CTAs of `kern` that fit on one SM at once (per device, cached).
+int resident_ctas(const void* kern, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> cache;
+    int dev = 0;
+    MBR_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(kern, dev);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    MBR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem));
+    n = std::max(1, n);
+    cache[key] = n;
+    return n;
+}
+
+// Grid of a grid-stride streaming kernel: at most one wave of resident CTAs,
+// so every CTA starts at once and the loads of the whole grid are in flight
+// together (a second wave would add its own ramp-up and tail).
+unsigned grid_one_wave(const void* kern, int64_t work, int threads, size_t smem = 0) {
+    const int64_t wave = (int64_t)sm_count() * resident_ctas(kern, threads, smem);
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(nblk(work, threads), wave));
 }
 
 // Frame scratch of the allocation-free iSTFT entry point: a fixed 16 MiB array
@@ -763,7 +782,7 @@ void sigmoid_gate(const void* x, const void* g, void* y, int64_t rows, int H, in
     MBR_CHECK(dh % 8 == 0, "gate: head dim must be a multiple of 8");
     MBR_CHECK(rows * H * dh / 8 < (1ll << 32), "gate: tensor too large");
     MBR_DISPATCH_DTYPE(dtype, T, {
-        gate_kernel<T><<<grid_for(rows * H * dh / 8, 256), 256, 0, st>>>((const T*)x, (const T*)g, (T*)y, rows, H,
+        gate_kernel<T><<<grid_one_wave((const void*)gate_kernel<T>, rows * H * dh / 8, 256), 256, 0, st>>>((const T*)x, (const T*)g, (T*)y, rows, H,
                                                                          dh);
     });
     MBR_CUDA(cudaGetLastError());
@@ -772,11 +791,13 @@ void sigmoid_gate(const void* x, const void* g, void* y, int64_t rows, int H, in
 template <typename T>
 bool launch_rms_group(int R, int NC, unsigned g, const void* x, const float* gamma, void* y, int64_t rows, int D,
                       float scale, cudaStream_t st) {
-#define MBR_RMS_GROUP(r_, nc_)                                                                      \
-    if (R == r_ && NC == nc_) {                                                                     \
-        rms_group_kernel<T, r_, nc_><<<g, 256, 0, st>>>((const T*)x, gamma, (T*)y, rows, D, scale); \
-        MBR_CUDA(cudaGetLastError());                                                               \
-        return true;                                                                                \
+#define MBR_RMS_GROUP(r_, nc_)                                                              \
+    if (R == r_ && NC == nc_) {                                                             \
+        auto k = rms_group_kernel<T, r_, nc_>;                                              \
+        const unsigned gg = std::min(g, grid_one_wave((const void*)k, (int64_t)g * 256, 256)); \
+        k<<<gg, 256, 0, st>>>((const T*)x, gamma, (T*)y, rows, D, scale);                    \
+        MBR_CUDA(cudaGetLastError());                                                       \
+        return true;                                                                        \
     }
     MBR_RMS_GROUP(1, 3) MBR_RMS_GROUP(1, 4) MBR_RMS_GROUP(2, 3) MBR_RMS_GROUP(2, 4) MBR_RMS_GROUP(3, 3)
     MBR_RMS_GROUP(4, 3) MBR_RMS_GROUP(4, 4) MBR_RMS_GROUP(6, 3) MBR_RMS_GROUP(8, 3) MBR_RMS_GROUP(8, 4)
@@ -794,7 +815,8 @@ void rms_norm(const void* x, const float* gamma, void* y, int64_t rows, int D, f
     for (int r = 1; r <= 8 && !R; ++r)
         if ((r * D8) % 32 == 0 && (r * D8) / 32 >= 3 && (r * D8) / 32 <= 4) R = r, NC = r * D8 / 32;
     if (R) {
-        const unsigned g = (unsigned)std::min<int64_t>(ceil_div(ceil_div(rows, R), 8), (int64_t)sm_count() * 8);
+        // one warp per row group: as many CTAs as there are groups of 8, capped at one wave
+        const unsigned g = (unsigned)ceil_div(ceil_div(rows, R), 8);
         bool done = false;
         MBR_DISPATCH_DTYPE(dtype, T, { done = launch_rms_group<T>(R, NC, g, x, gamma, y, rows, D, scale, st); });
         if (done) return;
@@ -813,7 +835,7 @@ void rope(const void* x, const float* cs, const float* sn, void* y, int64_t seqs
     MBR_CHECK(seqs * L * H * 8 < (1ll << 32), "rope: tensor too large");
     MBR_CHECK(((uintptr_t)cs & 15) == 0 && ((uintptr_t)sn & 15) == 0, "rope: tables must be 16-byte aligned");
     MBR_DISPATCH_DTYPE(dtype, T, {
-        rope_kernel<T><<<grid_for(seqs * L * H * 8, 256), 256, 0, st>>>((const T*)x, cs, sn, (T*)y, seqs, L, H);
+        rope_kernel<T><<<grid_one_wave((const void*)rope_kernel<T>, seqs * L * H * 8, 256), 256, 0, st>>>((const T*)x, cs, sn, (T*)y, seqs, L, H);
     });
     MBR_CUDA(cudaGetLastError());
 }
@@ -855,7 +877,8 @@ void band_gather(const float2* spec, int B, int C, int F, int T, const int* fi, 
     (void)fi;  // the tile tables carry the band map
     MBR_CHECK(C >= 1 && C <= 2 && bt.count == ceil_div(F, kBandTileBins) && bt.stride % 32 == 0,
               "band gather: one or two channels and a tile map of the spectrum");
-    MBR_CHECK(((uintptr_t)spec & 7) == 0 && ((uintptr_t)x & 3) == 0, "band gather: misaligned buffers");
+    MBR_CHECK(((uintptr_t)spec & 7) == 0 && ((uintptr_t)x & (dtype == DT_F32 ? 7 : 3)) == 0,
+              "band gather: misaligned buffers");
     MBR_CHECK((int64_t)C * F * T < (1ll << 31), "band gather: one batch entry of the spectrum exceeds 32-bit offsets");
     dim3 grid((unsigned)bt.count, (unsigned)ceil_div(T, kTT), (unsigned)B);
     MBR_DISPATCH_DTYPE(dtype, E, {

@@ -123,6 +123,23 @@ __device__ __forceinline__ void store4(T* p, float4 y) {
     }
 }
 
+// Packed f32x2 helpers of the row kernels: q + (v.x, v.y)^2 + (v.z, v.w)^2
+// as two pair sums, v * s * g (the product rounded in that order), and
+// q + (v.x w.x, v.y w.y) + (v.z w.z, v.w w.w).
+__device__ __forceinline__ float2 sq_acc2(float4 v, float2 q) {
+    q = __ffma2_rn(make_float2(v.x, v.y), make_float2(v.x, v.y), q);
+    return __ffma2_rn(make_float2(v.z, v.w), make_float2(v.z, v.w), q);
+}
+__device__ __forceinline__ float4 scale_mul2(float4 v, float s, float4 g) {
+    const float2 a = __fmul2_rn(__fmul2_rn(make_float2(v.x, v.y), make_float2(s, s)), make_float2(g.x, g.y));
+    const float2 b = __fmul2_rn(__fmul2_rn(make_float2(v.z, v.w), make_float2(s, s)), make_float2(g.z, g.w));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float2 dot_acc2(float4 v, float4 w, float2 q) {
+    q = __ffma2_rn(make_float2(v.x, v.y), make_float2(w.x, w.y), q);
+    return __ffma2_rn(make_float2(v.z, v.w), make_float2(w.z, w.w), q);
+}
+
 // One warp per row, rows strided over a persistent grid (the gate weights are
 // staged in shared memory once per CTA).  Each lane holds up to MAXC float4
 // chunks of the row in registers.  D % 4 == 0, D <= 128 * MAXC, H <= 32.
@@ -171,15 +188,17 @@ __global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restric
     for (int64_t m0 = 2 * wid; m0 < M; m0 += 2 * warps) {
         const bool two = m0 + 1 < M;
         float4 v[2][MAXC];
-        float ss[2] = {0.f, 0.f};
+        float ss[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int r = 0; r < 2; ++r) {
+            float2 q = make_float2(0.f, 0.f);  // packed partial sums of squares
 #pragma unroll
             for (int i = 0; i < MAXC; ++i) {
                 v[r][i] = nx[0][r][i];
-                ss[r] += v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y + v[r][i].z * v[r][i].z +
-                         v[r][i].w * v[r][i].w;
+                q = sq_acc2(v[r][i], q);
             }
+            ss[r] = q.x + q.y;
+        }
 #pragma unroll
         for (int k = 0; k + 1 < PF; ++k)
 #pragma unroll
@@ -197,21 +216,21 @@ __global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restric
             for (int i = 0; i < MAXC; ++i) {
                 const int c = lane + 32 * i;
                 const float4 g = c < D4 ? __ldg(g4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                v[r][i] = make_float4(v[r][i].x * inv * g.x, v[r][i].y * inv * g.y, v[r][i].z * inv * g.z,
-                                      v[r][i].w * inv * g.w);
+                v[r][i] = scale_mul2(v[r][i], inv, g);
                 if (c < D4 && r_out && (r == 0 || two)) reinterpret_cast<float4*>(r_out + m * D)[c] = v[r][i];
             }
         }
         if (gamma2) {
             // a second RMSNorm of the (stored) first result: the next block's
             // pre-norm, so the residual stream is read once for both
-            float s2[2] = {0.f, 0.f};
+            float s2[2];
 #pragma unroll
-            for (int r = 0; r < 2; ++r)
+            for (int r = 0; r < 2; ++r) {
+                float2 q = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int i = 0; i < MAXC; ++i)
-                    s2[r] += v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y + v[r][i].z * v[r][i].z +
-                             v[r][i].w * v[r][i].w;
+                for (int i = 0; i < MAXC; ++i) q = sq_acc2(v[r][i], q);
+                s2[r] = q.x + q.y;
+            }
             s2[0] = warp_sum(s2[0]);
             s2[1] = warp_sum(s2[1]);
 #pragma unroll
@@ -221,8 +240,7 @@ __global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restric
                 for (int i = 0; i < MAXC; ++i) {
                     const int c = lane + 32 * i;
                     const float4 g2 = c < D4 ? __ldg(h4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    v[r][i] = make_float4(v[r][i].x * inv2 * g2.x, v[r][i].y * inv2 * g2.y,
-                                          v[r][i].z * inv2 * g2.z, v[r][i].w * inv2 * g2.w);
+                    v[r][i] = scale_mul2(v[r][i], inv2, g2);
                 }
             }
         }
@@ -246,18 +264,18 @@ __global__ void __launch_bounds__(256, 2) rms_norm_kernel(const float* __restric
             float a[2][8];
 #pragma unroll
             for (int h = 0; h < 8; ++h) {
-                a[0][h] = 0.f;
-                a[1][h] = 0.f;
+                float2 q[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // packed partial dots
 #pragma unroll
                 for (int i = 0; i < MAXC; ++i) {
                     const int c = lane + 32 * i;
                     if (c < D4) {
                         const float4 w = swg4[h * D4 + c];
 #pragma unroll
-                        for (int r = 0; r < 2; ++r)
-                            a[r][h] += v[r][i].x * w.x + v[r][i].y * w.y + v[r][i].z * w.z + v[r][i].w * w.w;
+                        for (int r = 0; r < 2; ++r) q[r] = dot_acc2(v[r][i], w, q[r]);
                     }
                 }
+                a[0][h] = q[0].x + q[0].y;
+                a[1][h] = q[1].x + q[1].y;
             }
             const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
 #pragma unroll
