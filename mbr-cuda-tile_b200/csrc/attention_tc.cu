@@ -5,7 +5,8 @@
 //
 // One CTA (two per SM) = one 128-query tile of one (sequence, head) [or two
 // packed band sequences]: warps 0-3 run the softmax (thread r = query row r =
-// TMEM lane r), warp 4 issues the TMA loads and the MMAs.  Per 64-key block j:
+// TMEM lane r), warp 4 issues the TMA loads and warp 5 the MMAs.  Per 64-key
+// block j:
 //   S(j) = Q K(j)^T       -> TMEM buffer j%2 (128 x 64 fp32)
 //   P(j) = exp2(S*c - m)  -> TMEM buffer j%2 (16-bit pairs)
 //   O   += P(j) V(j)      -> TMEM (128 x 64 fp32), A operand read from TMEM
@@ -116,8 +117,10 @@ __global__ void __maxnreg__(168)
     uint64_t* bar_v = bar_k + NS;        // [NS] V stage landed
     uint64_t* bar_s = bar_v + NS;        // [2] S buffer computed
     uint64_t* bar_p = bar_s + 2;         // [2] softmax done with S buffer, P buffer written (4 warps)
-    uint64_t* bar_o = bar_p + 2;         // [2] P.V from P buffer complete
-    uint32_t* tmem_slot = (uint32_t*)(bar_o + 2);
+    uint64_t* bar_o = bar_p + 2;         // [2] P.V from P buffer complete (last two blocks)
+    uint64_t* kv_free = bar_o + 2;       // [NS] block g's P arrived: its K stage and V(g-2)'s are free
+    uint32_t* tmem_slot = (uint32_t*)(kv_free + NS);
+    static_assert((NQ + 3 * NS + 6) * 8 + 4 <= 256, "barrier region");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Persistent CTAs: this CTA takes tiles blockIdx.x, + gridDim.x, ...  Time
@@ -148,6 +151,7 @@ __global__ void __maxnreg__(168)
         for (int i = 0; i < NS; ++i) {
             mbar_init(&bar_k[i], 1);
             mbar_init(&bar_v[i], 1);
+            mbar_init(&kv_free[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bar_s[i], 1);
@@ -166,8 +170,9 @@ __global__ void __maxnreg__(168)
     const uint32_t tmem = *tmem_slot;
     const uint32_t tO = tmem + kTmemO;
 
-    if (warp == 4) {
-        // ---- producer + MMA warp: one elected lane issues, all lanes wait ----
+    if (warp >= 4) {
+        // ---- warp 4: TMA producer; warp 5: MMA issuer.  One elected lane
+        // issues, all lanes wait. ----
         auto wait_all = [&](uint64_t* b, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(b, parity, err));
         };
@@ -255,72 +260,89 @@ __global__ void __maxnreg__(168)
 #pragma unroll
             for (int k = 0; k < KB / 16; ++k)  // A: keys 16k.. = 8 packed columns; B: V keys 16k.. (MN-major, 2 KB)
                 mma_f16_ts(tO, a0 + 8 * k, b0 + 128 * k, idO, c.j != 0 || k > 0);
-            mma_commit(&bar_o[c.g & 1]);
-        };
-        // S(g) needs its tile's Q: wait for it at the tile's first block
-        auto s_ready = [&](const Cursor& c) -> bool {
-            if (c.j == 0 && !wait_all(&bar_q[c.tl % NQ], (c.tl / NQ) & 1)) return false;
-            return wait_all(&bar_k[c.g % NS], (c.g / NS) & 1);
+            // P.V(g) completes ahead of S(g+2), issued right behind it, whose
+            // commit the softmax waits for instead; only the last two blocks,
+            // which no S follows, commit their own barrier (one commit each)
+            if (c.g + 2 >= total) mma_commit(&bar_o[c.g & 1]);
         };
 
-        Cursor cs = cursor_at(0);             // next S to issue
-        Cursor cp = cs;                        // next P.V
-        Cursor ck = cursor_at(min(NS, total)); // next K load
-        Cursor cv = ck;                        // next V load
-        if (lane == 0) {
-            prefetch_tensormap(&tmQ);
-            prefetch_tensormap(&tmK);
-            prefetch_tensormap(&tmV);
-            for (int tl = 0; tl < NQ && tl < my_tiles; ++tl) load_q(tl);
-            Cursor c = cs;
-            for (int g = 0; g < NS && g < total; ++g, advance(c)) {
-                load_k(c);
-                load_v(c);
+        if (warp == 4) {
+            // Loads.  Stages are handed back by the MMA warp's plain arrive on
+            // kv_free[g % NS] once it has seen P(g): S(g) has completed, so K
+            // stage g is free, and so has P.V(g-2), issued before S(g), so V
+            // stage g-2 is free.  The MMA warp runs at most NS - 2 blocks ahead
+            // of these loads (S(g+2) needs K(g+2)), so the ring's parity waits
+            // are exact.
+            Cursor ck = cursor_at(min(NS, total));  // next K load
+            Cursor cv = ck;                          // next V load
+            if (lane == 0) {
+                prefetch_tensormap(&tmQ);
+                prefetch_tensormap(&tmK);
+                prefetch_tensormap(&tmV);
+                for (int tl = 0; tl < NQ && tl < my_tiles; ++tl) load_q(tl);
+                Cursor c = cursor_at(0);
+                for (int g = 0; g < NS && g < total; ++g, advance(c)) {
+                    load_k(c);
+                    load_v(c);
+                }
             }
-        }
-        __syncwarp();
-        // S(0), S(1) go ahead; afterwards S(g+2) is issued once the softmax has
-        // consumed S(g) (its buffer), right behind P(g).V(g).
-        bool ok = true;
-        for (int g = 0; g < 2 && g < total && ok; ++g, advance(cs)) {
-            ok = s_ready(cs);
-            if (ok) {
-                tc_fence_after();
-                if (elect_one()) issue_s(cs);
-                __syncwarp();
-            }
-        }
-        for (; cp.g < total && ok; advance(cp)) {
-            const int g = cp.g;
-            ok = wait_all(&bar_p[g & 1], (g >> 1) & 1);
-            if (!ok) break;
-            tc_fence_after();
-            // Freed by the softmax having consumed S(g): K stage g -> K(g+NS);
-            // V(g-2), whose P.V completed before S(g) did -> V(g-2+NS); after
-            // the last block of a tile, that tile's Q buffer -> Q(tile + NQ).
-            if (ck.g < total) {
-                if (lane == 0) load_k(ck);
-                advance(ck);
-            }
-            if (g >= 2 && cv.g < total) {
-                if (lane == 0) load_v(cv);
-                advance(cv);
-            }
-            if (lane == 0 && cp.j == nkv - 1 && cp.tl + NQ < my_tiles) load_q(cp.tl + NQ);
-            ok = wait_all(&bar_v[g % NS], (g / NS) & 1);
-            if (!ok) break;
-            tc_fence_after();
-            if (elect_one()) issue_pv(cp);
             __syncwarp();
-            // S(g+2) into the buffer S(g) held, behind P.V(g): its completion
-            // (bar_s) also tells the softmax that P buffer g%2 is free again
-            if (cs.g < total) {
-                ok = s_ready(cs);
+            bool ok = true;
+            for (Cursor cf = cursor_at(0); cf.g < total && ok; advance(cf)) {
+                const int g = cf.g;
+                ok = wait_all(&kv_free[g % NS], (g / NS) & 1);
                 if (!ok) break;
-                tc_fence_after();
-                if (elect_one()) issue_s(cs);
+                if (ck.g < total) {
+                    if (lane == 0) load_k(ck);
+                    advance(ck);
+                }
+                if (g >= 2 && cv.g < total) {
+                    if (lane == 0) load_v(cv);
+                    advance(cv);
+                }
+                // after a tile's last block (its last S has completed) its Q buffer -> Q(tile + NQ)
+                if (lane == 0 && cf.j == nkv - 1 && cf.tl + NQ < my_tiles) load_q(cf.tl + NQ);
                 __syncwarp();
-                advance(cs);
+            }
+        } else {
+            // S(g) needs its tile's Q (at the tile's first block), K(g) and, for
+            // the P.V(g) issued later, V(g)
+            auto s_ready = [&](const Cursor& c) -> bool {
+                if (c.j == 0 && !wait_all(&bar_q[c.tl % NQ], (c.tl / NQ) & 1)) return false;
+                return wait_all(&bar_k[c.g % NS], (c.g / NS) & 1) && wait_all(&bar_v[c.g % NS], (c.g / NS) & 1);
+            };
+            Cursor cs = cursor_at(0);  // next S to issue
+            Cursor cp = cs;            // next P.V
+            // S(0), S(1) go ahead; afterwards S(g+2) is issued once the softmax
+            // has consumed S(g) (its buffer), right behind P(g).V(g).
+            bool ok = true;
+            for (int g = 0; g < 2 && g < total && ok; ++g, advance(cs)) {
+                ok = s_ready(cs);
+                if (ok) {
+                    tc_fence_after();
+                    if (elect_one()) issue_s(cs);
+                    __syncwarp();
+                }
+            }
+            for (; cp.g < total && ok; advance(cp)) {
+                const int g = cp.g;
+                ok = wait_all(&bar_p[g & 1], (g >> 1) & 1);
+                if (!ok) break;
+                if (lane == 0) mbar_arrive(&kv_free[g % NS]);  // the producer may refill
+                tc_fence_after();
+                if (elect_one()) issue_pv(cp);  // V(g) landed: s_ready(g) waited for it
+                __syncwarp();
+                // S(g+2) into the buffer S(g) held, behind P.V(g): its completion
+                // (bar_s) also tells the softmax that P buffer g%2 is free again
+                // and that P.V(g) is complete
+                if (cs.g < total) {
+                    ok = s_ready(cs);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (elect_one()) issue_s(cs);
+                    __syncwarp();
+                    advance(cs);
+                }
             }
         }
     } else {
@@ -331,6 +353,13 @@ __global__ void __maxnreg__(168)
         // kRescaleSum, so P < 2^14 and O / l is the same softmax.
         const int r = threadIdx.x;
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        // P.V(x) is complete: through S(x+2), issued right behind it, or the
+        // block's own commit when no S follows (the last two blocks)
+        auto wait_pv = [&](int x) -> bool {
+            const bool ok1 = x + 2 < total ? mbar_wait(&bar_s[x & 1], ((x + 2) >> 1) & 1, err)
+                                           : mbar_wait(&bar_o[x & 1], 0, err);
+            return __all_sync(0xffffffffu, ok1);
+        };
         bool ok = true;  // warp-uniform: TMEM loads and stores are warp-collective
         for (int tl = 0; tl < my_tiles && ok; ++tl) {
         int sh0, sh1, q0;
@@ -440,7 +469,7 @@ __global__ void __maxnreg__(168)
                 const bool need = !(rs <= kRescaleSum);  // also catches inf / nan
                 if (__any_sync(0xffffffffu, need)) {
                     // O must hold exactly P.V of blocks < j: wait for P.V(g-1)
-                    ok = __all_sync(0xffffffffu, mbar_wait(&bar_o[(g - 1) & 1], ((g - 1) >> 1) & 1, err));
+                    ok = wait_pv(g - 1);
                     if (!ok) break;
                     tc_fence_after();
                     const float m_new = need ? fmaxf(m, row_max()) : m;
@@ -466,10 +495,9 @@ __global__ void __maxnreg__(168)
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_p[b]);
         }
-        // the tile's last P.V: it is the latest on its barrier, and the one
-        // before it completed ahead of S(g_last), so the parity wait is exact
+        // the tile's last P.V
         const int g_last = tl * nkv + nkv - 1;
-        ok = __all_sync(0xffffffffu, ok && mbar_wait(&bar_o[g_last & 1], (g_last >> 1) & 1, err));
+        ok = ok && wait_pv(g_last);
         if (ok) {
             tc_fence_after();
             uint32_t ov[DH / 32][32];
@@ -559,7 +587,7 @@ void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
     MBR_CHECK(ntiles < (1ll << 30), "tc attention: too many tiles");
     const int grid = (int)std::min<int64_t>(ntiles, 2 * (int64_t)sms[dev]);
     if (grid == 0) return;
-    kern<<<grid, 160, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, n_lo, scale_log2, gates, mode, NB, Tn,
+    kern<<<grid, 192, AttnSmem::TOTAL, st>>>(mq, mk, mv, nsh, H, L, n_lo, scale_log2, gates, mode, NB, Tn,
                                               (T*)merged, err);
     MBR_CUDA(cudaGetLastError());
 }
