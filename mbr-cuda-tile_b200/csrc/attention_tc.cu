@@ -62,8 +62,14 @@ struct AttnCfg {
     static constexpr int TOTAL = BAR + 256;
     static_assert(2 * (TOTAL + 1024) <= 233472, "two CTAs per SM");
 };
-// TMEM columns (256 allocated): S double buffer (fp32) at 0 and 64, O at 128,
-// P double buffer (16-bit pairs, the A operand of P.V) at 192 and 224.
+// TMEM columns (256 allocated): S double buffer (fp32) at 0 and 64, O at 128.
+// Time axis: P double buffer (16-bit pairs, the A operand of P.V) at 192 and
+// 224.  Band axis (two key blocks per tile, so the per-tile epilogue weighs
+// more): each block's P is written over the first 32 columns of its own S once
+// the softmax has read S, and O is double buffered by tile parity at 128 and
+// 192, so a tile's output is read while the next tile's blocks already
+// accumulate (measured: band 23 % faster per step; the time axis, 13 blocks
+// per tile, measured 7 % slower this way and keeps separate P buffers).
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kTmemO = 128, kTmemP = 192;
 
@@ -119,8 +125,9 @@ __global__ void __maxnreg__(168)
     uint64_t* bar_p = bar_s + 2;         // [2] softmax done with S buffer, P buffer written (4 warps)
     uint64_t* bar_o = bar_p + 2;         // [2] P.V from P buffer complete (last two blocks)
     uint64_t* kv_free = bar_o + 2;       // [NS] block g's P arrived: its K stage and V(g-2)'s are free
-    uint32_t* tmem_slot = (uint32_t*)(kv_free + NS);
-    static_assert((NQ + 3 * NS + 6) * 8 + 4 <= 256, "barrier region");
+    uint64_t* o_free = kv_free + NS;     // [2] O buffer read by the softmax's epilogue (4 warps)
+    uint32_t* tmem_slot = (uint32_t*)(o_free + 2);
+    static_assert((NQ + 3 * NS + 8) * 8 + 4 <= 256, "barrier region");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Persistent CTAs: this CTA takes tiles blockIdx.x, + gridDim.x, ...  Time
@@ -157,6 +164,7 @@ __global__ void __maxnreg__(168)
             mbar_init(&bar_s[i], 1);
             mbar_init(&bar_p[i], 4);
             mbar_init(&bar_o[i], 1);
+            mbar_init(&o_free[i], 4);
         }
         fence_barrier_init();
     }
@@ -254,12 +262,13 @@ __global__ void __maxnreg__(168)
             for (int k = 0; k < DH / 16; ++k) mma_f16(d, q + 2 * k, k0 + 2 * k, idS, k > 0);
             mma_commit(&bar_s[c.g & 1]);
         };
-        auto issue_pv = [&](const Cursor& c) {  // O (+)= P(g & 1) V(g), P read from TMEM; O restarts per tile
-            const uint32_t a0 = tmem + kTmemP + 32 * (c.g & 1);
+        auto issue_pv = [&](const Cursor& c) {  // O(tile % 2) (+)= P(g) V(g), P read from TMEM; O restarts per tile
+            const uint32_t a0 = PACK ? tmem + 64 * (c.g & 1) : tmem + kTmemP + 32 * (c.g & 1);
+            const uint32_t d = PACK ? tO + 64 * (c.tl & 1) : tO;
             const uint64_t b0 = dV + (uint64_t)(512 * (c.g % NS));
 #pragma unroll
             for (int k = 0; k < KB / 16; ++k)  // A: keys 16k.. = 8 packed columns; B: V keys 16k.. (MN-major, 2 KB)
-                mma_f16_ts(tO, a0 + 8 * k, b0 + 128 * k, idO, c.j != 0 || k > 0);
+                mma_f16_ts(d, a0 + 8 * k, b0 + 128 * k, idO, c.j != 0 || k > 0);
             // P.V(g) completes ahead of S(g+2), issued right behind it, whose
             // commit the softmax waits for instead; only the last two blocks,
             // which no S follows, commit their own barrier (one commit each)
@@ -329,6 +338,10 @@ __global__ void __maxnreg__(168)
                 ok = wait_all(&bar_p[g & 1], (g >> 1) & 1);
                 if (!ok) break;
                 if (lane == 0) mbar_arrive(&kv_free[g % NS]);  // the producer may refill
+                // a tile's first P.V overwrites the O buffer of the tile two
+                // before, once the softmax's epilogue has read it
+                if (PACK && cp.j == 0 && cp.tl >= 2) ok = wait_all(&o_free[cp.tl & 1], ((cp.tl >> 1) - 1) & 1);
+                if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) issue_pv(cp);  // V(g) landed: s_ready(g) waited for it
                 __syncwarp();
@@ -360,8 +373,41 @@ __global__ void __maxnreg__(168)
                                            : mbar_wait(&bar_o[x & 1], 0, err);
             return __all_sync(0xffffffffu, ok1);
         };
+        // A tile's output (band axis: after the next tile's first block, when
+        // its last P.V has long completed): O of tile parity pd_par is read,
+        // normalised, gated and stored, and the buffer handed back.
+        bool pd_have = false, pd_valid = false;
+        int64_t pd_tok = 0;
+        float pd_gs = 0.f;
+        int pd_hd = 0, pd_glast = 0, pd_par = 0;
+        auto flush = [&]() -> bool {
+            if (!wait_pv(pd_glast)) return false;
+            tc_fence_after();
+            const uint32_t tOp = tO + 64 * pd_par + lane_off;  // pd_par is 0 on the time axis
+            uint32_t ov[DH / 32][32];
+#pragma unroll
+            for (int c = 0; c < DH / 32; ++c) tmem_ld32(tOp + c * 32, ov[c]);
+            tmem_ld_wait();
+            if (pd_valid) {
+                uint4* dst = reinterpret_cast<uint4*>(merged + pd_tok * (int64_t)H * DH + pd_hd * DH);
+#pragma unroll
+                for (int q = 0; q < DH / 8; ++q) {
+                    const uint32_t* o = &ov[q >> 2][(q & 3) * 8];
+                    dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * pd_gs, __uint_as_float(o[1]) * pd_gs, (T*)nullptr),
+                                        pack2(__uint_as_float(o[2]) * pd_gs, __uint_as_float(o[3]) * pd_gs, (T*)nullptr),
+                                        pack2(__uint_as_float(o[4]) * pd_gs, __uint_as_float(o[5]) * pd_gs, (T*)nullptr),
+                                        pack2(__uint_as_float(o[6]) * pd_gs, __uint_as_float(o[7]) * pd_gs, (T*)nullptr));
+                }
+            }
+            tc_fence_before();  // O read before the tile two ahead overwrites the buffer
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free[pd_par]);
+            pd_have = false;
+            return true;
+        };
         bool ok = true;  // warp-uniform: TMEM loads and stores are warp-collective
         for (int tl = 0; tl < my_tiles && ok; ++tl) {
+        const uint32_t tOc = PACK ? tO + 64 * (tl & 1) : tO;  // this tile's O buffer
         int sh0, sh1, q0;
         tile_of(tl, sh0, sh1, q0);
         int seg = 0, pos, sh = sh0;
@@ -400,9 +446,10 @@ __global__ void __maxnreg__(168)
             for (int c = 0; c < 2; ++c)
                 if (c * 32 < kend) tmem_ld32(tmem + lane_off + 64 * b + 32 * c, sv[c]);
             tmem_ld_wait();
-            // P buffer b (TMEM) is free: P.V(g-2) was issued before S(g), whose
-            // completion was just observed
-            const uint32_t tP = tmem + lane_off + kTmemP + 32 * b;
+            // P buffer b (or, band axis, the S(g) just read) is free: P.V(g-2),
+            // its last reader, was issued before S(g), whose completion was
+            // just observed
+            const uint32_t tP = PACK ? tmem + lane_off + 64 * b : tmem + lane_off + kTmemP + 32 * b;
             // exponentials with offset mo -> P buffer b in TMEM as 16-bit pairs
             // (masked keys get zeros); returns the row sum of this block
             auto emit = [&](float mo) {
@@ -479,11 +526,11 @@ __global__ void __maxnreg__(168)
 #pragma unroll 1
                     for (int c = 0; c < DH / 16; ++c) {  // 16 columns at a time: S is still live
                         uint32_t ov[16];
-                        tmem_ld16(tO + lane_off + c * 16, ov);
+                        tmem_ld16(tOc + lane_off + c * 16, ov);
                         tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st16(tO + lane_off + c * 16, ov);
+                        tmem_st16(tOc + lane_off + c * 16, ov);
                     }
                     tmem_st_wait();
                     rs = emit(m);
@@ -494,32 +541,22 @@ __global__ void __maxnreg__(168)
             tc_fence_before();  // S reads / P and O stores ordered before the next MMAs
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_p[b]);
-        }
-        // the tile's last P.V
-        const int g_last = tl * nkv + nkv - 1;
-        ok = ok && wait_pv(g_last);
-        if (ok) {
-            tc_fence_after();
-            uint32_t ov[DH / 32][32];
-#pragma unroll
-            for (int c = 0; c < DH / 32; ++c) tmem_ld32(tO + lane_off + c * 32, ov[c]);
-            tmem_ld_wait();
-            if (valid) {
-                const int hd = sh % H;
-                const float gs = gate / l;
-                uint4* dst = reinterpret_cast<uint4*>(merged + tok * (int64_t)H * DH + hd * DH);
-#pragma unroll
-                for (int q = 0; q < DH / 8; ++q) {
-                    const uint32_t* o = &ov[q >> 2][(q & 3) * 8];
-                    dst[q] = make_uint4(pack2(__uint_as_float(o[0]) * gs, __uint_as_float(o[1]) * gs, (T*)nullptr),
-                                        pack2(__uint_as_float(o[2]) * gs, __uint_as_float(o[3]) * gs, (T*)nullptr),
-                                        pack2(__uint_as_float(o[4]) * gs, __uint_as_float(o[5]) * gs, (T*)nullptr),
-                                        pack2(__uint_as_float(o[6]) * gs, __uint_as_float(o[7]) * gs, (T*)nullptr));
-                }
+            if (PACK && j == 0 && pd_have) {  // the previous tile's output
+                ok = flush();
+                if (!ok) break;
             }
-            tc_fence_before();  // O read before the next tile's first P.V overwrites it
         }
+        // this tile's output: on the band axis after the next tile's first block
+        pd_have = ok;
+        pd_valid = valid;
+        pd_tok = tok;
+        pd_gs = gate / l;
+        pd_hd = sh % H;
+        pd_glast = tl * nkv + nkv - 1;
+        pd_par = PACK ? tl & 1 : 0;
+        if (!PACK && ok) ok = flush();
         }  // tiles
+        if (ok && pd_have) flush();
     }
     tc_fence_before();
     __syncthreads();
