@@ -47,18 +47,22 @@ constexpr int KB = 64;   // keys per block (one 128-byte swizzle atom of P per r
 constexpr float kRescaleSum = 16384.0f;
 
 // Shared-memory plan: NQ Q tiles in flight (persistent CTAs prefetch the next
-// tiles; band tiles have only two key blocks, so they prefetch further) and an
-// NS-stage K / V ring.  Two CTAs share an SM, so the layout carries no
-// alignment slack: the kernel checks that the dynamic window is 1024-byte
-// aligned instead.
+// tiles; band tiles have only two key blocks, so they prefetch further), an
+// NSK-stage K ring and an NSV-stage V ring.  A K stage is refilled two blocks
+// after the S that read it was issued, a V stage four blocks after (its P.V
+// completes behind the S two blocks later), so the V ring is the deeper one:
+// both give their loads the same lead.  Two CTAs share an SM, so the layout
+// carries no alignment slack: the kernel checks that the dynamic window is
+// 1024-byte aligned instead.
 template <bool PACK>
 struct AttnCfg {
-    static constexpr int NS = PACK ? 4 : 5;  // K / V stages of 64 x 64 (8 KB each)
-    static constexpr int NQ = PACK ? 3 : 2;  // Q tiles of 128 x 64 (16 KB)
+    static constexpr int NSK = PACK ? 3 : 4;  // K stages of 64 x 64 (8 KB each)
+    static constexpr int NSV = PACK ? 5 : 6;  // V stages
+    static constexpr int NQ = PACK ? 3 : 2;   // Q tiles of 128 x 64 (16 KB)
     static constexpr int Q = 0;
     static constexpr int K = NQ * 16384;
-    static constexpr int V = K + NS * 8192;
-    static constexpr int BAR = V + NS * 8192;
+    static constexpr int V = K + NSK * 8192;
+    static constexpr int BAR = V + NSV * 8192;
     static constexpr int TOTAL = BAR + 256;
     static_assert(2 * (TOTAL + 1024) <= 233472, "two CTAs per SM");
 };
@@ -113,21 +117,21 @@ __global__ void __maxnreg__(168)
                    const __grid_constant__ CUtensorMap tmV, int nsh, int H, int L, int n_lo, float scale_log2,
                    const float* __restrict__ gates, int mode, int NB, int Tn, T* __restrict__ merged, int* err) {
     using AttnSmem = AttnCfg<PACK>;
-    constexpr int NS = AttnSmem::NS, NQ = AttnSmem::NQ;
+    constexpr int NSK = AttnSmem::NSK, NSV = AttnSmem::NSV, NQ = AttnSmem::NQ;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     if (!smem_aligned_or_flag(smem_raw, err)) return;  // uniform over the CTA
     uint8_t* sm = smem_raw;
     uint64_t* bar = (uint64_t*)(sm + AttnSmem::BAR);
     uint64_t* bar_q = bar;               // [NQ] Q tile landed
-    uint64_t* bar_k = bar + NQ;          // [NS] K stage landed
-    uint64_t* bar_v = bar_k + NS;        // [NS] V stage landed
-    uint64_t* bar_s = bar_v + NS;        // [2] S buffer computed
+    uint64_t* bar_k = bar + NQ;          // [NSK] K stage landed
+    uint64_t* bar_v = bar_k + NSK;       // [NSV] V stage landed
+    uint64_t* bar_s = bar_v + NSV;       // [2] S buffer computed
     uint64_t* bar_p = bar_s + 2;         // [2] softmax done with S buffer, P buffer written (4 warps)
     uint64_t* bar_o = bar_p + 2;         // [2] P.V from P buffer complete (last two blocks)
-    uint64_t* kv_free = bar_o + 2;       // [NS] block g's P arrived: its K stage and V(g-2)'s are free
-    uint64_t* o_free = kv_free + NS;     // [2] O buffer read by the softmax's epilogue (4 warps)
+    uint64_t* kv_free = bar_o + 2;       // [NSK] block g's P arrived: its K stage and V(g-2)'s are free
+    uint64_t* o_free = kv_free + NSK;    // [2] O buffer read by the softmax's epilogue (4 warps)
     uint32_t* tmem_slot = (uint32_t*)(o_free + 2);
-    static_assert((NQ + 3 * NS + 8) * 8 + 4 <= 256, "barrier region");
+    static_assert((NQ + 2 * NSK + NSV + 8) * 8 + 4 <= 256, "barrier region");
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Persistent CTAs: this CTA takes tiles blockIdx.x, + gridDim.x, ...  Time
@@ -155,11 +159,11 @@ __global__ void __maxnreg__(168)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NQ; ++i) mbar_init(&bar_q[i], 1);
-        for (int i = 0; i < NS; ++i) {
+        for (int i = 0; i < NSK; ++i) {
             mbar_init(&bar_k[i], 1);
-            mbar_init(&bar_v[i], 1);
             mbar_init(&kv_free[i], 1);
         }
+        for (int i = 0; i < NSV; ++i) mbar_init(&bar_v[i], 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(&bar_s[i], 1);
             mbar_init(&bar_p[i], 4);
@@ -238,12 +242,12 @@ __global__ void __maxnreg__(168)
             }
         };
         auto load_k = [&](const Cursor& c) {
-            const int st = c.g % NS;
+            const int st = c.g % NSK;
             mbar_arrive_expect_tx(&bar_k[st], 8192);
             tma_load_5d(sm + AttnSmem::K + st * 8192, &tmK, 0, c.h, c.p, c.slo, c.shi, &bar_k[st]);
         };
         auto load_v = [&](const Cursor& c) {
-            const int st = c.g % NS;
+            const int st = c.g % NSV;
             mbar_arrive_expect_tx(&bar_v[st], 8192);
             tma_load_5d(sm + AttnSmem::V + st * 8192, &tmV, 0, c.h, c.p, c.slo, c.shi, &bar_v[st]);
         };
@@ -256,7 +260,7 @@ __global__ void __maxnreg__(168)
         const uint64_t dV = sdesc_sw128_mn(smem_u32(sm + AttnSmem::V));
         auto issue_s = [&](const Cursor& c) {  // S buffer (g & 1) = Q(tile) K(g)^T
             const uint64_t q = dQ + (uint64_t)(1024 * (c.tl % NQ));
-            const uint64_t k0 = dK + (uint64_t)(512 * (c.g % NS));
+            const uint64_t k0 = dK + (uint64_t)(512 * (c.g % NSK));
             const uint32_t d = tmem + (uint32_t)(64 * (c.g & 1));
 #pragma unroll
             for (int k = 0; k < DH / 16; ++k) mma_f16(d, q + 2 * k, k0 + 2 * k, idS, k > 0);
@@ -265,7 +269,7 @@ __global__ void __maxnreg__(168)
         auto issue_pv = [&](const Cursor& c) {  // O(tile % 2) (+)= P(g) V(g), P read from TMEM; O restarts per tile
             const uint32_t a0 = PACK ? tmem + 64 * (c.g & 1) : tmem + kTmemP + 32 * (c.g & 1);
             const uint32_t d = PACK ? tO + 64 * (c.tl & 1) : tO;
-            const uint64_t b0 = dV + (uint64_t)(512 * (c.g % NS));
+            const uint64_t b0 = dV + (uint64_t)(512 * (c.g % NSV));
 #pragma unroll
             for (int k = 0; k < KB / 16; ++k)  // A: keys 16k.. = 8 packed columns; B: V keys 16k.. (MN-major, 2 KB)
                 mma_f16_ts(d, a0 + 8 * k, b0 + 128 * k, idO, c.j != 0 || k > 0);
@@ -277,21 +281,21 @@ __global__ void __maxnreg__(168)
 
         if (warp == 4) {
             // Loads.  Stages are handed back by the MMA warp's plain arrive on
-            // kv_free[g % NS] once it has seen P(g): S(g) has completed, so K
+            // kv_free[g % NSK] once it has seen P(g): S(g) has completed, so K
             // stage g is free, and so has P.V(g-2), issued before S(g), so V
-            // stage g-2 is free.  The MMA warp runs at most NS - 2 blocks ahead
-            // of these loads (S(g+2) needs K(g+2)), so the ring's parity waits
-            // are exact.
-            Cursor ck = cursor_at(min(NS, total));  // next K load
-            Cursor cv = ck;                          // next V load
+            // stage g-2 is free.  The MMA warp runs at most NSK - 2 blocks
+            // ahead of these loads (S(g+2) needs K(g+2)), so the ring's parity
+            // waits are exact.
+            Cursor ck = cursor_at(min(NSK, total));  // next K load
+            Cursor cv = cursor_at(min(NSV, total));  // next V load
             if (lane == 0) {
                 prefetch_tensormap(&tmQ);
                 prefetch_tensormap(&tmK);
                 prefetch_tensormap(&tmV);
                 for (int tl = 0; tl < NQ && tl < my_tiles; ++tl) load_q(tl);
                 Cursor c = cursor_at(0);
-                for (int g = 0; g < NS && g < total; ++g, advance(c)) {
-                    load_k(c);
+                for (int g = 0; g < NSV && g < total; ++g, advance(c)) {
+                    if (g < NSK) load_k(c);
                     load_v(c);
                 }
             }
@@ -299,7 +303,7 @@ __global__ void __maxnreg__(168)
             bool ok = true;
             for (Cursor cf = cursor_at(0); cf.g < total && ok; advance(cf)) {
                 const int g = cf.g;
-                ok = wait_all(&kv_free[g % NS], (g / NS) & 1);
+                ok = wait_all(&kv_free[g % NSK], (g / NSK) & 1);
                 if (!ok) break;
                 if (ck.g < total) {
                     if (lane == 0) load_k(ck);
@@ -318,7 +322,7 @@ __global__ void __maxnreg__(168)
             // the P.V(g) issued later, V(g)
             auto s_ready = [&](const Cursor& c) -> bool {
                 if (c.j == 0 && !wait_all(&bar_q[c.tl % NQ], (c.tl / NQ) & 1)) return false;
-                return wait_all(&bar_k[c.g % NS], (c.g / NS) & 1) && wait_all(&bar_v[c.g % NS], (c.g / NS) & 1);
+                return wait_all(&bar_k[c.g % NSK], (c.g / NSK) & 1) && wait_all(&bar_v[c.g % NSV], (c.g / NSV) & 1);
             };
             Cursor cs = cursor_at(0);  // next S to issue
             Cursor cp = cs;            // next P.V
@@ -337,7 +341,7 @@ __global__ void __maxnreg__(168)
                 const int g = cp.g;
                 ok = wait_all(&bar_p[g & 1], (g >> 1) & 1);
                 if (!ok) break;
-                if (lane == 0) mbar_arrive(&kv_free[g % NS]);  // the producer may refill
+                if (lane == 0) mbar_arrive(&kv_free[g % NSK]);  // the producer may refill
                 // a tile's first P.V overwrites the O buffer of the tile two
                 // before, once the softmax's epilogue has read it
                 if (PACK && cp.j == 0 && cp.tl >= 2) ok = wait_all(&o_free[cp.tl & 1], ((cp.tl >> 1) - 1) & 1);
