@@ -11,7 +11,7 @@
 //   P(j) = exp2(S*c - m)  -> TMEM buffer j%2 (16-bit pairs)
 //   O   += P(j) V(j)      -> TMEM (128 x 64 fp32), A operand read from TMEM
 // S(j+2) is computed while the softmax works on S(j+1), so the softmax warps
-// do not wait for the tensor cores; K and V stream through a 4-stage ring.
+// do not wait for the tensor cores; K and V stream through their own rings.
 // V keeps the [seq][H][L][64] layout of q and k: its 64-key tile is the
 // MN-major B operand of the P.V product.  The epilogue multiplies by the
 // sigmoid gate (loaded at the tile's start) and writes the merged-head row of
