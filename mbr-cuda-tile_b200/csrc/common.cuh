@@ -72,13 +72,6 @@ __device__ __forceinline__ void cp_async(void* smem, const void* gmem) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(s), "l"(gmem), "n"(N) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-// closes this thread's current group of asynchronous copies
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// waits until at most N of this thread's committed copy groups are still in flight
-template <int N>
-__device__ __forceinline__ void cp_async_wait_group() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
