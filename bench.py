@@ -676,7 +676,7 @@ def run_tensor_sweep(args):
 
 
 def run_op_sweep(args):
-    """Tensor-op sweep: activations [B*801*60, D] seeded
+    """Tensor-op sweep (the benchmark's op-sweep configuration): activations [B*801*60, D] seeded
     N(0, 1), D in {192, 384, 512}, B in {1, 4, 8}, fp32 / fp16 / bf16.  Each op
     is timed with CUDA events around one launch after an L2 flush (a 256 MiB
     write followed by a 256 MiB read, so the launch meets a cold L2 and none of

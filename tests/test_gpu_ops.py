@@ -1,5 +1,5 @@
 """GPU parity of the stand-alone op entry points (the reference op library's
-ops, BASELINE op-sweep shapes) against CPU references.
+ops, at the op-sweep benchmark shapes) against CPU references.
 
 Inputs are seeded N(0, 1) activations of shape [B*801*60, D].  The CPU
 reference evaluates in fp64 from the same (already rounded) inputs; tolerances:
@@ -176,7 +176,7 @@ def test_band_gather_and_mask_scatter(torch_cuda, make_csm, B, dtype):
 
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
 def test_full_size_sweep_properties(torch_cuda, dtype):
-    """BASELINE's largest sweep shape (B = 8, D = 512): add then subtract returns
+    """The op sweep's largest shape (B = 8, D = 512): add then subtract returns
     the input (to one rounding), RMSNorm rows have RMS == gamma-weighted scale."""
     torch = torch_cuda
     import cudasep
